@@ -1,0 +1,1131 @@
+// warp_div.cu -- B200 (sm_100a) kernels of the `warp_div` rANS coder and the
+// C ABI declared in include/fcai_warp_div.h.
+//
+// Format (fixed by the reference, coders/cuda/warp_ans_kernel*.cu): the B x N
+// symbols of a batch are cut into K = ceil(C / P) chunks per image of
+// chunk_len = P * (N / C) consecutive symbols.  Inside a chunk, lane L of 32
+// owns symbols start + L, start + L + 32, ...  Each lane is an independent
+// 64-bit rANS stream (L = 2^31, 32-bit renormalisation, 16-bit CDFs, 4-bit
+// bypass escapes); its words are stored interleaved (word r of lane L at
+// r*32 + L) and every chunk is padded to the longest lane (max_rounds).
+//
+// Design (B200-first, not a translation of the reference):
+//  * encode is one persistent kernel: each warp codes one chunk at a time,
+//    with every CDF row of the batch staged once per CTA in shared memory as
+//    packed {start, freq-1} u32 entries.  Renormalisation words go to a
+//    transposed staging area [chunk][emission j][lane] so that both the
+//    lanes' writes and the later pack are 128-byte row accesses.  The last
+//    CTA to finish computes the chunk offsets (exclusive scan of
+//    max_rounds * 32) and a status block, so the host needs one small
+//    device-to-host read to size the payload.
+//  * pack writes each chunk's rounds as full 128-byte rows (coalesced), plus
+//    the header, in one kernel.
+//  * decode is a validation/scan kernel (header words, round table, length)
+//    followed by one persistent kernel whose CDF search starts from a
+//    128-bucket slot->symbol table per CDF row in shared memory, so a lookup
+//    is one table read plus (on average < 1) linear steps instead of a
+//    binary search over global memory.
+//  * all loops over payload words are bounded by the chunk's rounds and by
+//    the escape limit (<= 8 nibbles), so corrupt payloads raise an error
+//    instead of reading out of bounds.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/fcai_warp_div.h"
+#include "fcai_common.h"
+
+namespace fcai {
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int sm_count() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 148;
+    if (dev < 64 && cache[dev]) return cache[dev];
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (dev < 64) cache[dev] = n;
+    return n;
+}
+
+}  // namespace fcai
+
+namespace wd {
+
+constexpr int kLanes = 32;
+constexpr int kWarps = 8;                 // warps per CTA
+constexpr int kThreads = kLanes * kWarps;
+constexpr uint64_t kRansL = 1ull << 31;
+constexpr uint32_t kBypassBits = 4;
+constexpr uint32_t kBypassMax = 15;
+constexpr int kLutShift = 9;              // decode LUT bucket = slot >> 9
+constexpr int kLutBuckets = 65536 >> kLutShift;
+constexpr int kMaxSymbolWords = 10;       // <= 8 nibbles + count + symbol puts
+constexpr int64_t kCtrlBytes = 256;
+constexpr int kMaxSmemBytes = 200 * 1024;
+
+// Error flags (bit mask accumulated in the control block).
+enum : uint32_t {
+    kFlagIndexRange = 1u << 0,
+    kFlagNonChannel = 1u << 1,  // informational: indexes differ from the channel layout
+    kFlagTable = 1u << 2,
+    kFlagOverflow = 1u << 3,
+    kFlagHeader = 1u << 4,
+    kFlagRounds = 1u << 5,
+    kFlagCorrupt = 1u << 6,
+};
+
+struct Control {
+    unsigned int done;      // CTAs finished (reset by the last one)
+    unsigned int flags;     // OR of flags (reset by the last one)
+    unsigned int max_used;  // longest lane in words (reset by the last one)
+    unsigned int pad0;
+    long long status[8];    // written by the last CTA, read by the host
+    unsigned int pad1[44];
+};
+static_assert(sizeof(Control) <= kCtrlBytes, "control block too large");
+// status[] slots
+constexpr int kStTotalWords = 0, kStFlags = 1, kStMaxUsed = 2, kStRowsCap = 3;
+
+__host__ __device__ inline int64_t align256(int64_t v) { return (v + 255) & ~int64_t(255); }
+
+struct EncLayout {
+    int64_t rounds, used, offsets, stage, fixed_bytes;
+};
+
+__host__ __device__ inline EncLayout enc_layout(int64_t chunks) {
+    EncLayout l;
+    l.rounds = kCtrlBytes;
+    l.used = l.rounds + align256(chunks * 4);
+    l.offsets = l.used + align256(chunks * kLanes * 4);
+    l.stage = l.offsets + align256(chunks * 8);
+    l.fixed_bytes = l.stage;
+    return l;
+}
+
+struct DecLayout {
+    int64_t offsets, fixed_bytes;
+};
+
+__host__ __device__ inline DecLayout dec_layout(int64_t chunks) {
+    DecLayout l;
+    l.offsets = kCtrlBytes;
+    l.fixed_bytes = l.offsets + align256(chunks * 8);
+    return l;
+}
+
+// floor((2^64 - 1) / f) for f in [2, 65536]; entries 0 and 1 unused.
+__device__ uint64_t g_magic[65537];
+
+__global__ void init_magic_kernel() {
+    int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f <= 65536) g_magic[f] = f >= 2 ? (~0ull) / (uint64_t)f : 0ull;
+}
+
+// ---------------------------------------------------------------------------
+// CDF tables
+// ---------------------------------------------------------------------------
+
+// Packed entry of symbol v of a row: start | (freq - 1) << 16.  Valid rows
+// have 0 <= start <= 65535 and 1 <= freq <= 65536.
+__device__ __forceinline__ uint32_t pack_entry(int32_t a, int32_t b, uint32_t &flags) {
+    if (a < 0 || b <= a || b > 65536) {
+        flags |= kFlagTable;
+        return 0u;  // start 0, freq 1: keeps the coder in bounds
+    }
+    return (uint32_t)a | ((uint32_t)(b - a - 1) << 16);
+}
+
+struct TableArgs {
+    const int32_t *__restrict__ cdfs;
+    const int32_t *__restrict__ sizes;
+    const int32_t *__restrict__ offs;
+    int C, L;
+};
+
+// Stages every row into shared memory: entries [C][L-1] and {offset, maxv}.
+// With lut != nullptr also builds the decode bucket table [C][kLutBuckets].
+__device__ void stage_tables(const TableArgs &t, uint32_t *s_tab, int2 *s_ch, uint16_t *s_lut,
+                             uint32_t &flags) {
+    const int Ls = t.L - 1;
+    for (int c = threadIdx.x; c < t.C; c += blockDim.x) {
+        int32_t size = __ldg(t.sizes + c);
+        if (size < 2 || size > t.L) {
+            flags |= kFlagTable;
+            size = size < 2 ? 2 : t.L;
+        }
+        s_ch[c] = make_int2(__ldg(t.offs + c), size - 2);
+    }
+    __syncthreads();
+    const int total = t.C * Ls;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        int c = e / Ls, v = e - c * Ls;
+        int maxv = s_ch[c].y;
+        uint32_t ent = 0u;
+        if (v <= maxv) {
+            const int32_t *row = t.cdfs + (int64_t)c * t.L;
+            int32_t a = __ldg(row + v), b = __ldg(row + v + 1);
+            ent = pack_entry(a, b, flags);
+            if (s_lut) {
+                // buckets whose first slot lies in this symbol's range; the
+                // first symbol also owns slots below cdf[0] and the last one
+                // the slots above cdf[size-1] (binary-search semantics)
+                int lo = v == 0 ? 0 : (int)(ent & 0xFFFFu);
+                int hi = v == maxv ? 65536 : (int)(ent & 0xFFFFu) + (int)(ent >> 16) + 1;
+                int u0 = (lo + (1 << kLutShift) - 1) >> kLutShift;
+                int u1 = (hi + (1 << kLutShift) - 1) >> kLutShift;
+                if (u1 > kLutBuckets) u1 = kLutBuckets;
+                for (int u = u0; u < u1; ++u) s_lut[c * kLutBuckets + u] = (uint16_t)v;
+            }
+        }
+        s_tab[e] = ent;
+    }
+    __syncthreads();
+}
+
+// Validation of all rows when they are read from global memory.
+__device__ void validate_tables_global(const TableArgs &t, uint32_t &flags) {
+    for (int c = threadIdx.x; c < t.C; c += blockDim.x) {
+        int32_t size = __ldg(t.sizes + c);
+        if (size < 2 || size > t.L) {
+            flags |= kFlagTable;
+            continue;
+        }
+        const int32_t *row = t.cdfs + (int64_t)c * t.L;
+        for (int v = 0; v + 1 < size; ++v) pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
+    }
+}
+
+template <bool kSmem>
+struct Tables {
+    const uint32_t *s_tab;
+    const int2 *s_ch;
+    const uint16_t *s_lut;
+    TableArgs g;
+
+    __device__ __forceinline__ int2 chan(int c) const {
+        if (kSmem) return s_ch[c];
+        int32_t size = __ldg(g.sizes + c);
+        size = size < 2 ? 2 : (size > g.L ? g.L : size);
+        return make_int2(__ldg(g.offs + c), size - 2);
+    }
+    __device__ __forceinline__ uint32_t entry(int c, int v, uint32_t &flags) const {
+        if (kSmem) return s_tab[c * (g.L - 1) + v];
+        const int32_t *row = g.cdfs + (int64_t)c * g.L;
+        return pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
+    }
+    // First s in [0, maxv] with cdf[s+1] > slot (maxv if none); returns the
+    // symbol and its entry.
+    __device__ __forceinline__ int search(int c, int maxv, uint32_t slot, uint32_t &ent, uint32_t &flags) const {
+        if (kSmem) {
+            int s = s_lut[c * kLutBuckets + (slot >> kLutShift)];
+            if (s > maxv) s = maxv;
+            const uint32_t *row = s_tab + c * (g.L - 1);
+            uint32_t e = row[s];
+            while (s < maxv && (e & 0xFFFFu) + (e >> 16) + 1u <= slot) e = row[++s];
+            ent = e;
+            return s;
+        }
+        const int32_t *row = g.cdfs + (int64_t)c * g.L;
+        int lo = 0, hi = maxv;
+        while (lo < hi) {
+            int mid = (lo + hi) >> 1;
+            if ((uint32_t)__ldg(row + mid + 1) > slot) hi = mid;
+            else lo = mid + 1;
+        }
+        ent = pack_entry(__ldg(row + lo), __ldg(row + lo + 1), flags);
+        return lo;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// rANS primitives (rans64_gpu.cuh:21-55, rans64_gpu_v2.cuh:90-120 semantics)
+// ---------------------------------------------------------------------------
+
+struct LaneWriter {
+    uint32_t *rows;  // stage of this chunk, row j of this lane at j * 32
+    int cap;         // rows available
+    int j;           // words emitted so far
+    __device__ __forceinline__ void emit(uint32_t w) {
+        if (j < cap) rows[j * kLanes] = w;
+        ++j;
+    }
+};
+
+__device__ __forceinline__ void put_symbol(uint64_t &x, uint32_t start, uint32_t freq, LaneWriter &w) {
+    if (x >= ((uint64_t)freq << 47)) {  // ((L >> 16) << 32) * freq
+        w.emit((uint32_t)x);
+        x >>= 32;
+    }
+    uint64_t q;
+    uint32_t r;
+    if (freq <= 1u) {
+        q = freq ? x : 0ull;
+        r = freq ? 0u : (uint32_t)x;
+    } else {
+        q = __umul64hi(x, g_magic[freq]);  // floor(x / freq) or one less
+        uint64_t rr = x - q * (uint64_t)freq;
+        if (rr >= freq) {
+            ++q;
+            rr -= freq;
+        }
+        r = (uint32_t)rr;
+    }
+    x = (q << 16) + (uint64_t)(r + start);
+}
+
+__device__ __forceinline__ void put_nibble(uint64_t &x, uint32_t val, LaneWriter &w) {
+    if (x >= (4096ull << 47)) {  // freq = 1 << (16 - 4)
+        w.emit((uint32_t)x);
+        x >>= 32;
+    }
+    x = (x << kBypassBits) | (uint64_t)val;
+}
+
+// Escape code of an out-of-range value (warp_ans_kernel_v2.cu:148-164).
+__device__ __noinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter &w) {
+    int n_bypass = raw ? (31 - __clz(raw)) / (int)kBypassBits + 1 : 0;
+    for (int j = n_bypass - 1; j >= 0; --j) put_nibble(x, (raw >> (j * kBypassBits)) & kBypassMax, w);
+    int rem = n_bypass, n_full = 0;
+    while (rem >= (int)kBypassMax) {
+        rem -= (int)kBypassMax;
+        ++n_full;
+    }
+    put_nibble(x, (uint32_t)rem, w);
+    for (int k = 0; k < n_full; ++k) put_nibble(x, kBypassMax, w);
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide exclusive scan (used by the single "last" CTA)
+// ---------------------------------------------------------------------------
+
+__device__ uint64_t block_exclusive_scan(uint64_t v, uint64_t *s_warp, uint64_t &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    uint64_t inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        uint64_t w = lane < nwarps ? s_warp[lane] : 0ull;
+        uint64_t wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint64_t n = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += n;
+        }
+        if (lane < nwarps) s_warp[lane] = wi - w;
+        if (lane == 31) s_warp[32] = wi;
+    }
+    __syncthreads();
+    uint64_t r = s_warp[warp] + inc - v;
+    total = s_warp[32];
+    __syncthreads();
+    return r;
+}
+
+// offsets[c] = sum_{c' < c} rounds[c'] * 32; returns the total (all threads).
+__device__ uint64_t scan_rounds(const int32_t *rounds, int64_t n, unsigned long long *offsets, uint64_t *s_warp) {
+    const int64_t per = (n + blockDim.x - 1) / blockDim.x;
+    const int64_t lo = (int64_t)threadIdx.x * per;
+    const int64_t hi = lo + per < n ? lo + per : n;
+    uint64_t sum = 0;
+    for (int64_t c = lo; c < hi; ++c) sum += (uint64_t)(uint32_t)__ldcg(rounds + c) * kLanes;
+    uint64_t total;
+    uint64_t run = block_exclusive_scan(sum, s_warp, total);
+    for (int64_t c = lo; c < hi; ++c) {
+        offsets[c] = run;
+        run += (uint64_t)(uint32_t)__ldcg(rounds + c) * kLanes;
+    }
+    return total;
+}
+
+// ---------------------------------------------------------------------------
+// Encode
+// ---------------------------------------------------------------------------
+
+// Where encode reads its symbols / decode writes its result.
+enum Mode : int {
+    kModeIdx = 0,      // int32 symbols with explicit indexes[B,N]
+    kModeChannel = 1,  // int32 symbols, channel layout index = i / HW
+    kModeLatent = 2,   // fp32 latent y with per-channel medians, channel layout:
+                       // symbol = (int)rint(y - median)  (factorized.py:46-49),
+                       // y_hat = (float)symbol + median  (factorized.py:99-101)
+};
+
+struct EncParams {
+    const int32_t *__restrict__ sym;
+    const int32_t *__restrict__ idx;     // kModeIdx only
+    const float *__restrict__ y;         // kModeLatent only
+    const float *__restrict__ medians;   // kModeLatent only
+    TableArgs t;
+    int B, N, P, K, chunk_len, HW;
+    int rows_cap;
+    int64_t chunks;
+    Control *ctrl;
+    int32_t *rounds;
+    int32_t *used;
+    unsigned long long *offsets;
+    uint32_t *stage;
+    uint32_t *max_rounds_out;
+};
+
+template <int kMode, bool kSmem>
+__global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
+    constexpr bool kIdx = kMode == kModeIdx;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ uint64_t s_warp[33];
+    __shared__ unsigned int s_flags, s_max_used;
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        s_flags = 0;
+        s_max_used = 0;
+    }
+    uint32_t flags = 0;
+    const int C = p.t.C;
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    int2 *s_ch = reinterpret_cast<int2 *>(smem + (((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll));
+    if (kSmem) {
+        stage_tables(p.t, s_tab, s_ch, nullptr, flags);
+    } else {
+        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
+        __syncthreads();
+    }
+    Tables<kSmem> tab{s_tab, s_ch, nullptr, p.t};
+
+    const int lane = threadIdx.x & 31;
+    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+    unsigned int my_max_used = 0;
+    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
+        const int b = (int)(chunk / p.K);
+        const int k = (int)(chunk - (int64_t)b * p.K);
+        const int start = k * p.chunk_len;
+        const int end = min(start + p.chunk_len, p.N);
+        const int first = start + lane;
+        LaneWriter w{p.stage + chunk * (int64_t)p.rows_cap * kLanes + lane, p.rows_cap, 0};
+        if (first < end) {
+            const int n = (end - 1 - first) / kLanes + 1;
+            int i = first + (n - 1) * kLanes;
+            int ct = i / p.HW, rem = i - ct * p.HW;  // channel-layout position tracker
+            const int32_t *srow = kMode == kModeLatent ? nullptr : p.sym + (int64_t)b * p.N;
+            const float *yrow = kMode == kModeLatent ? p.y + (int64_t)b * p.N : nullptr;
+            const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
+            uint64_t x = kRansL;
+#pragma unroll 2
+            for (int t = 0; t < n; ++t) {
+                int32_t s;
+                if (kMode == kModeLatent) {
+                    // torch.round (half to even) then .int(), both in fp32
+                    s = __float2int_rz(rintf(__ldg(yrow + i) - __ldg(p.medians + ct)));
+                } else {
+                    s = __ldg(srow + i);
+                }
+                int c = ct;
+                if (kIdx) {
+                    const int32_t ci = __ldg(irow + i);
+                    if (ci != ct) flags |= kFlagNonChannel;
+                    if ((unsigned)ci >= (unsigned)C) {
+                        flags |= kFlagIndexRange;
+                        c = 0;
+                    } else {
+                        c = ci;
+                    }
+                }
+                const int2 ch = tab.chan(c);
+                int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
+                const int32_t maxv = ch.y;
+                if (value < 0 || value >= maxv) {
+                    // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
+                    uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
+                                             : ((uint32_t)value - (uint32_t)maxv) * 2u;
+                    put_escape(x, raw, w);
+                    value = maxv;
+                }
+                const uint32_t e = tab.entry(c, value, flags);
+                put_symbol(x, e & 0xFFFFu, (e >> 16) + 1u, w);
+                i -= kLanes;
+                rem -= kLanes;
+                while (rem < 0) {
+                    rem += p.HW;
+                    --ct;
+                }
+            }
+            w.emit((uint32_t)(x >> 32));  // flush: decode order is low, high, ...
+            w.emit((uint32_t)x);
+        }
+        const int used = w.j;
+        int rounds = used;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, o));
+        p.used[chunk * kLanes + lane] = used;
+        if (lane == 0) {
+            p.rounds[chunk] = rounds;
+            p.max_rounds_out[chunk] = (uint32_t)rounds;
+        }
+        if ((unsigned)rounds > my_max_used) my_max_used = (unsigned)rounds;
+    }
+    if (my_max_used > (unsigned)p.rows_cap) flags |= kFlagOverflow;
+
+    // CTA summary, then the last CTA computes offsets and the status block.
+    if (flags) atomicOr(&s_flags, flags);
+    if (my_max_used) atomicMax(&s_max_used, my_max_used);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (s_flags) atomicOr(&p.ctrl->flags, s_flags);
+        atomicMax(&p.ctrl->max_used, s_max_used);
+        __threadfence();
+        s_last = atomicAdd(&p.ctrl->done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    uint64_t total = scan_rounds(p.rounds, p.chunks, p.offsets, s_warp);
+    if (threadIdx.x == 0) {
+        volatile Control *ctl = p.ctrl;
+        ctl->status[kStTotalWords] = (long long)total;
+        ctl->status[kStFlags] = (long long)ctl->flags;
+        ctl->status[kStMaxUsed] = (long long)ctl->max_used;
+        ctl->status[kStRowsCap] = p.rows_cap;
+        ctl->flags = 0;
+        ctl->max_used = 0;
+        ctl->done = 0;
+    }
+}
+
+struct PackParams {
+    const Control *ctrl;
+    const int32_t *rounds;
+    const int32_t *used;
+    const unsigned long long *offsets;
+    const uint32_t *stage;
+    int64_t chunks;
+    int B, N, K, chunk_len;
+    int64_t header_bytes;
+    int64_t packed_bytes;
+    uint8_t *packed;
+};
+
+__global__ void __launch_bounds__(kThreads) pack_kernel(PackParams p) {
+    const long long total_words = p.ctrl->status[kStTotalWords];
+    const int rows_cap = (int)p.ctrl->status[kStRowsCap];
+    if (p.header_bytes + 4 * (int64_t)total_words != p.packed_bytes) return;  // not the last encode's size
+    uint32_t *hdr = reinterpret_cast<uint32_t *>(p.packed);
+    if (blockIdx.x == 0 && threadIdx.x < 8) {
+        uint32_t h = 0;
+        switch (threadIdx.x) {
+            case 0: h = (uint32_t)p.N; break;
+            case 1: h = (uint32_t)p.chunk_len; break;
+            case 2: h = ((uint32_t)p.K & 0xFFFFu) | (((uint32_t)p.B & 0xFFFFu) << 16); break;
+            case 3: h = 2u | (32u << 16); break;
+            default: h = 0u;
+        }
+        hdr[threadIdx.x] = h;
+    }
+    // zero the pad between the round table and header_bytes (<= 12 bytes)
+    const int64_t table_end = 32 + 4 * p.chunks;
+    if (blockIdx.x == 0 && threadIdx.x >= 8 && threadIdx.x < 8 + (p.header_bytes - table_end) / 4)
+        hdr[table_end / 4 + (threadIdx.x - 8)] = 0u;
+    const int lane = threadIdx.x & 31;
+    uint32_t *body = reinterpret_cast<uint32_t *>(p.packed + p.header_bytes);
+    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
+        const int rounds = p.rounds[chunk];
+        int used = p.used[chunk * kLanes + lane];
+        if (used > rows_cap) used = 0;  // overflowed staging: never packed by the host
+        if (lane == 0) hdr[8 + chunk] = (uint32_t)rounds;
+        const uint32_t *st = p.stage + chunk * (int64_t)rows_cap * kLanes + lane;
+        uint32_t *out = body + p.offsets[chunk] + lane;
+        for (int r = 0; r < rounds; ++r) out[r * kLanes] = r < used ? st[(used - 1 - r) * kLanes] : 0u;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Decode
+// ---------------------------------------------------------------------------
+
+struct DecPrepParams {
+    const uint8_t *packed;
+    const uint32_t *max_rounds;
+    int64_t chunks;
+    int B, N, K, chunk_len;
+    int64_t header_bytes, packed_bytes;
+    Control *ctrl;
+    unsigned long long *offsets;
+};
+
+// Header check (coders/warp_div.py:161-176), rounds >= 2 and total length
+// (coders/warp_div.py:62-67), and chunk offsets.
+__global__ void __launch_bounds__(1024) decode_prep_kernel(DecPrepParams p) {
+    __shared__ uint64_t s_warp[33];
+    __shared__ unsigned int s_flags;
+    if (threadIdx.x == 0) s_flags = 0;
+    __syncthreads();
+    uint32_t flags = 0;
+    const uint32_t *hdr = reinterpret_cast<const uint32_t *>(p.packed);
+    if (threadIdx.x == 0) {
+        if (hdr[0] != (uint32_t)p.N || hdr[1] != (uint32_t)p.chunk_len ||
+            hdr[2] != (((uint32_t)p.B << 16) | (uint32_t)p.K) || hdr[3] != ((32u << 16) | 2u) || hdr[4] != 0u ||
+            hdr[5] != 0u)
+            flags |= kFlagHeader;
+    }
+    // round table: max_rounds as int32 at word 8 (fits: header_bytes >= 32 + 4*B*K)
+    const int32_t *mr = reinterpret_cast<const int32_t *>(p.max_rounds);
+    for (int64_t c = threadIdx.x; c < p.chunks; c += blockDim.x) {
+        if ((int32_t)hdr[8 + c] != mr[c]) flags |= kFlagRounds;
+        if (p.max_rounds[c] < 2u || p.max_rounds[c] > 0x7fffffffu) flags |= kFlagCorrupt;
+    }
+    uint64_t total = scan_rounds(mr, p.chunks, p.offsets, s_warp);
+    if (threadIdx.x == 0 && p.header_bytes + 4 * (int64_t)total != p.packed_bytes) flags |= kFlagCorrupt;
+    if (flags) atomicOr(&s_flags, flags);
+    __syncthreads();
+    if (threadIdx.x == 0 && s_flags) atomicOr(&p.ctrl->flags, s_flags);
+}
+
+struct DecParams {
+    const uint8_t *__restrict__ packed;
+    int64_t header_bytes;
+    const uint32_t *__restrict__ max_rounds;
+    const int32_t *__restrict__ idx;       // kModeIdx only
+    const float *__restrict__ medians;     // kModeLatent only
+    float *__restrict__ y_out;             // kModeLatent only
+    TableArgs t;
+    int B, N, K, chunk_len, HW;
+    int64_t chunks;
+    Control *ctrl;
+    const unsigned long long *offsets;
+    int32_t *__restrict__ out;
+};
+
+struct LaneReader {
+    const uint32_t *__restrict__ base;  // chunk body + lane
+    int word, rounds;
+    bool bad;
+    __device__ __forceinline__ uint32_t next() {
+        if (word < rounds) return __ldg(base + (int64_t)(word++) * kLanes);
+        bad = true;
+        return 0u;
+    }
+};
+
+__device__ __forceinline__ uint32_t get_nibble(uint64_t &x, LaneReader &rd) {
+    uint32_t v = (uint32_t)x & kBypassMax;
+    x >>= kBypassBits;
+    if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
+    return v;
+}
+
+// Escape decode (warp_ans_kernel.cu:308-325).  Returns false on a corrupt
+// count (the format never needs more than 8 nibbles).
+__device__ __noinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
+    uint32_t v = get_nibble(x, rd);
+    uint32_t n_bypass = v;
+    while (v == kBypassMax && !rd.bad) {
+        v = get_nibble(x, rd);
+        n_bypass += v;
+    }
+    if (n_bypass > 8u || rd.bad) return false;
+    uint32_t raw = 0;
+    for (uint32_t j = 0; j < n_bypass; ++j) raw |= get_nibble(x, rd) << (j * kBypassBits);
+    int32_t val = (int32_t)raw >> 1;  // int32 arithmetic shift, as in the reference
+    if (raw & 1u) val = -val - 1;
+    else val = (int32_t)((uint32_t)val + (uint32_t)maxv);
+    value = val;
+    return true;
+}
+
+template <int kMode, bool kSmem>
+__global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
+    constexpr bool kIdx = kMode == kModeIdx;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ unsigned int s_flags;
+    __shared__ int s_last;
+    if (threadIdx.x == 0) s_flags = 0;
+    uint32_t flags = 0;
+    // prep (or an earlier CTA) found a bad payload or table
+    const bool skip = (*((volatile unsigned int *)&p.ctrl->flags) & ~kFlagNonChannel) != 0;
+    const int C = p.t.C;
+    const int64_t tab_bytes = ((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll;
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    int2 *s_ch = reinterpret_cast<int2 *>(smem + tab_bytes);
+    uint16_t *s_lut = reinterpret_cast<uint16_t *>(smem + tab_bytes + (int64_t)C * 8);
+    if (kSmem) {
+        stage_tables(p.t, s_tab, s_ch, s_lut, flags);
+    } else {
+        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
+        __syncthreads();
+    }
+    Tables<kSmem> tab{s_tab, s_ch, s_lut, p.t};
+    const int lane = threadIdx.x & 31;
+    const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
+    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); !skip && chunk < p.chunks;
+         chunk += warp_stride) {
+        const int b = (int)(chunk / p.K);
+        const int k = (int)(chunk - (int64_t)b * p.K);
+        const int64_t start64 = (int64_t)k * p.chunk_len;
+        if (start64 >= p.N) continue;
+        const int start = (int)start64;
+        const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
+        const int first = start + lane;
+        if (first >= end) continue;
+        LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false};
+        uint64_t x = (uint64_t)rd.next();
+        x |= (uint64_t)rd.next() << 32;
+        const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
+        int32_t *orow = kMode == kModeLatent ? nullptr : p.out + (int64_t)b * p.N;
+        float *yrow = kMode == kModeLatent ? p.y_out + (int64_t)b * p.N : nullptr;
+        int ct = first / p.HW, rem = first - ct * p.HW;
+        for (int i = first; i < end; i += kLanes) {
+            int c = ct;
+            if (kIdx) {
+                const int32_t ci = __ldg(irow + i);
+                if (ci != ct) flags |= kFlagNonChannel;
+                if ((unsigned)ci >= (unsigned)C) {
+                    flags |= kFlagIndexRange;
+                    c = 0;
+                } else {
+                    c = ci;
+                }
+            }
+            const int2 ch = tab.chan(c);
+            const uint32_t slot = (uint32_t)x & 0xFFFFu;
+            uint32_t e;
+            int32_t value = tab.search(c, ch.y, slot, e, flags);
+            x = (uint64_t)((e >> 16) + 1u) * (x >> 16) + (uint64_t)slot - (uint64_t)(e & 0xFFFFu);
+            if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
+            if (value == ch.y && !get_escape(x, rd, ch.y, value)) {
+                rd.bad = true;
+                break;
+            }
+            const int32_t sym = (int32_t)((uint32_t)value + (uint32_t)ch.x);
+            if (kMode == kModeLatent) yrow[i] = __int2float_rn(sym) + __ldg(p.medians + c);
+            else orow[i] = sym;
+            rem += kLanes;
+            while (rem >= p.HW) {
+                rem -= p.HW;
+                ++ct;
+            }
+        }
+        if (rd.bad) flags |= kFlagCorrupt;
+    }
+    if (flags) atomicOr(&s_flags, flags);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (s_flags) atomicOr(&p.ctrl->flags, s_flags);
+        __threadfence();
+        s_last = atomicAdd(&p.ctrl->done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last && threadIdx.x == 0) {
+        __threadfence();
+        volatile Control *ctl = p.ctrl;
+        ctl->status[kStFlags] = (long long)ctl->flags;
+        ctl->flags = 0;
+        ctl->done = 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+static std::mutex g_init_mutex;
+static bool g_magic_ready[64];
+
+static int ensure_magic(cudaStream_t stream) {
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fcai::fail(FCAI_ERR_CUDA, "device ordinal %d unsupported", dev);
+    std::lock_guard<std::mutex> lock(g_init_mutex);
+    if (g_magic_ready[dev]) return FCAI_OK;
+    init_magic_kernel<<<(65537 + 255) / 256, 256, 0, stream>>>();
+    FCAI_CUDA_TRY(cudaGetLastError());
+    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    g_magic_ready[dev] = true;
+    return FCAI_OK;
+}
+
+struct Dims {
+    int B, N, C, P, K, chunk_len, HW;
+    int64_t chunks, header_bytes;
+};
+
+static int make_dims(int32_t B, int32_t N, int32_t C, int32_t P, Dims &d) {
+    // warp_ans_kernel_v2.cu:198-203
+    if (B <= 0 || N <= 0 || C <= 0) return fcai::fail(FCAI_ERR_INVALID, "empty/invalid coder input dimensions");
+    if (N % C != 0)
+        return fcai::fail(FCAI_ERR_INVALID, "WarpANS currently requires symbols per batch divisible by CDF count");
+    if (P <= 0 || P > C) return fcai::fail(FCAI_ERR_INVALID, "P_ch must be in [1, C]");
+    if (B > 65535 || C > 65535) return fcai::fail(FCAI_ERR_INVALID, "B/C exceed WarpANS header field capacity");
+    if ((int64_t)N * C >= INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "coder dimensions exceed kernel index range");
+    d.B = B;
+    d.N = N;
+    d.C = C;
+    d.P = P;
+    d.HW = N / C;
+    d.K = (C + P - 1) / P;
+    d.chunk_len = P * d.HW;
+    d.chunks = (int64_t)B * d.K;
+    if (d.chunks > INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "B * K exceeds the header's int32 range");
+    d.header_bytes = (32 + 4 * d.chunks + 15) & ~int64_t(15);
+    return FCAI_OK;
+}
+
+static inline int64_t rows_worst(const Dims &d) {
+    return (int64_t)kMaxSymbolWords * ((d.chunk_len + kLanes - 1) / kLanes) + 2;
+}
+
+static int64_t encode_smem_bytes(int C, int L) { return (((int64_t)C * (L - 1) * 4 + 15) & ~15ll) + (int64_t)C * 8; }
+static int64_t decode_smem_bytes(int C, int L) {
+    return encode_smem_bytes(C, L) + (int64_t)C * kLutBuckets * 2;
+}
+
+// Per (kernel, device) launch shape: the dynamic shared memory opt-in is
+// raised to the largest size seen and the occupancy is queried once per
+// distinct size, so repeated calls do no driver queries.
+struct LaunchCache {
+    const void *fn;
+    int dev;
+    int64_t smem_optin;
+    int64_t smem_last;
+    int occ_last;
+};
+static std::mutex g_launch_mutex;
+static LaunchCache g_launch[64];
+static int g_launch_n = 0;
+
+template <typename K>
+static int grid_for(K kernel, int64_t smem, int64_t chunks, int &grid) {
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    int occ = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_launch_mutex);
+        LaunchCache *e = nullptr;
+        for (int i = 0; i < g_launch_n; ++i)
+            if (g_launch[i].fn == (const void *)kernel && g_launch[i].dev == dev) e = &g_launch[i];
+        if (!e && g_launch_n < 64) {
+            e = &g_launch[g_launch_n++];
+            *e = LaunchCache{(const void *)kernel, dev, 48 * 1024, -1, 0};
+        }
+        if (e && e->smem_last == smem) {
+            occ = e->occ_last;
+        } else {
+            if (smem > (e ? e->smem_optin : 48 * 1024)) {
+                FCAI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                if (e) e->smem_optin = smem;
+            }
+            FCAI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, (size_t)smem));
+            if (e) {
+                e->smem_last = smem;
+                e->occ_last = occ;
+            }
+        }
+    }
+    if (occ < 1) occ = 1;
+    int64_t want = (chunks + kWarps - 1) / kWarps;
+    int64_t cap = (int64_t)fcai::sm_count() * occ;
+    grid = (int)(want < cap ? want : cap);
+    if (grid < 1) grid = 1;
+    return FCAI_OK;
+}
+
+template <int kMode, bool kSmem>
+static int launch_encode(const EncParams &p, int64_t smem, cudaStream_t stream) {
+    int grid = 1, rc;
+    if ((rc = grid_for(encode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, grid))) return rc;
+    encode_kernel<kMode, kSmem><<<grid, kThreads, kSmem ? smem : 0, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+template <int kMode, bool kSmem>
+static int launch_decode(const DecParams &p, int64_t smem, cudaStream_t stream) {
+    int grid = 1, rc;
+    if ((rc = grid_for(decode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, grid))) return rc;
+    decode_kernel<kMode, kSmem><<<grid, kThreads, kSmem ? smem : 0, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+static int check_tables_args(const int32_t *cdfs, int32_t C, int32_t L, const int32_t *sizes, const int32_t *offs) {
+    if (!cdfs || !sizes || !offs) return fcai::fail(FCAI_ERR_INVALID, "null CDF table pointer");
+    if (L < 2) return fcai::fail(FCAI_ERR_INVALID, "CDF table cannot be empty");
+    if ((int64_t)C * L >= INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "CDF table too large");
+    return FCAI_OK;
+}
+
+static int flags_to_status(long long flags, bool encode) {
+    if (flags & kFlagIndexRange) return fcai::fail(FCAI_ERR_INDEX_RANGE, "indexes contain a value outside the CDF table range");
+    if (flags & kFlagTable)
+        return fcai::fail(FCAI_ERR_TABLE,
+                          "CDF table invalid: cdf_sizes must lie in [2, L] and each row must be strictly "
+                          "increasing within [0, 65536]");
+    if (!encode) {
+        if (flags & kFlagHeader)
+            return fcai::fail(FCAI_ERR_HEADER, "warp_div packed header is inconsistent with payload metadata");
+        if (flags & kFlagRounds)
+            return fcai::fail(FCAI_ERR_ROUNDS, "warp_div packed header round counts do not match payload metadata");
+        if (flags & kFlagCorrupt)
+            return fcai::fail(FCAI_ERR_CORRUPT, "warp_div payload body is inconsistent with its chunk rounds");
+    }
+    return FCAI_OK;
+}
+
+// Shared body of the encode entry points.
+static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes, const float *y,
+                       const float *medians, int32_t B, int32_t N, const int32_t *cdfs, int32_t C, int32_t L,
+                       const int32_t *cdf_sizes, const int32_t *offsets, int32_t P, void *workspace,
+                       int64_t workspace_bytes, uint32_t *max_rounds, fcai_warp_div_encode_info *info,
+                       cudaStream_t stream) {
+    Dims d;
+    int rc = make_dims(B, N, C, P, d);
+    if (rc) return rc;
+    if ((rc = check_tables_args(cdfs, C, L, cdf_sizes, offsets))) return rc;
+    if (!workspace || !max_rounds || !info) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    if (mode == kModeLatent ? (!y || !medians) : !symbols) return fcai::fail(FCAI_ERR_INVALID, "null input");
+    EncLayout el = enc_layout(d.chunks);
+    int64_t avail = workspace_bytes - el.fixed_bytes;
+    int64_t rows_cap = avail > 0 ? avail / (d.chunks * kLanes * 4) : 0;
+    if (rows_cap > rows_worst(d)) rows_cap = rows_worst(d);
+    if (rows_cap < 2) {
+        info->required_workspace_bytes = el.fixed_bytes + d.chunks * rows_worst(d) * kLanes * 4;
+        return fcai::fail(FCAI_ERR_WORKSPACE, "encode workspace of %lld bytes is too small",
+                          (long long)workspace_bytes);
+    }
+    if ((rc = ensure_magic(stream))) return rc;
+
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    EncParams p;
+    p.sym = symbols;
+    p.idx = indexes;
+    p.y = y;
+    p.medians = medians;
+    p.t = TableArgs{cdfs, cdf_sizes, offsets, C, L};
+    p.B = d.B;
+    p.N = d.N;
+    p.P = d.P;
+    p.K = d.K;
+    p.chunk_len = d.chunk_len;
+    p.HW = d.HW;
+    p.rows_cap = (int)rows_cap;
+    p.chunks = d.chunks;
+    p.ctrl = reinterpret_cast<Control *>(ws);
+    p.rounds = reinterpret_cast<int32_t *>(ws + el.rounds);
+    p.used = reinterpret_cast<int32_t *>(ws + el.used);
+    p.offsets = reinterpret_cast<unsigned long long *>(ws + el.offsets);
+    p.stage = reinterpret_cast<uint32_t *>(ws + el.stage);
+    p.max_rounds_out = max_rounds;
+
+    const int64_t smem = encode_smem_bytes(C, L);
+    const bool sm = smem <= kMaxSmemBytes;
+    if (mode == kModeIdx) rc = sm ? launch_encode<kModeIdx, true>(p, smem, stream) : launch_encode<kModeIdx, false>(p, smem, stream);
+    else if (mode == kModeChannel) rc = sm ? launch_encode<kModeChannel, true>(p, smem, stream) : launch_encode<kModeChannel, false>(p, smem, stream);
+    else rc = sm ? launch_encode<kModeLatent, true>(p, smem, stream) : launch_encode<kModeLatent, false>(p, smem, stream);
+    if (rc) return rc;
+    long long status[8];
+    FCAI_CUDA_TRY(cudaMemcpyAsync(status, p.ctrl->status, sizeof(status), cudaMemcpyDeviceToHost, stream));
+    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+
+    const long long flags = status[kStFlags];
+    info->header_bytes = d.header_bytes;
+    info->chunk_len = d.chunk_len;
+    info->p_ch = d.P;
+    info->index_layout_is_channel = (flags & kFlagNonChannel) ? 0 : 1;
+    info->packed_bytes = d.header_bytes + 4 * (int64_t)status[kStTotalWords];
+    info->required_workspace_bytes = el.fixed_bytes + d.chunks * (int64_t)status[kStMaxUsed] * kLanes * 4;
+    if ((rc = flags_to_status(flags, true))) return rc;
+    if (flags & kFlagOverflow)
+        return fcai::fail(FCAI_ERR_WORKSPACE, "encode staging needs %lld workspace bytes, %lld given",
+                          (long long)info->required_workspace_bytes, (long long)workspace_bytes);
+    return FCAI_OK;
+}
+
+// Shared body of the decode entry points.
+static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
+                       int64_t header_bytes, int32_t chunk_len, const int32_t *indexes, int32_t B, int32_t N,
+                       const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets,
+                       const float *medians, int32_t *symbols_out, float *y_out, void *workspace,
+                       int64_t workspace_bytes, int32_t check, int32_t *index_layout_is_channel,
+                       cudaStream_t stream) {
+    // warp_ans_kernel.cu:489-503
+    if (B <= 0 || N <= 0 || C <= 0 || N % C != 0)
+        return fcai::fail(FCAI_ERR_INVALID, "invalid decode dimensions/channel layout");
+    if (K <= 0 || header_bytes < 32 || chunk_len <= 0) return fcai::fail(FCAI_ERR_INVALID, "invalid payload metadata");
+    if (header_bytes >= packed_bytes) return fcai::fail(FCAI_ERR_INVALID, "header exceeds packed payload size");
+    int rc = check_tables_args(cdfs, C, L, cdf_sizes, offsets);
+    if (rc) return rc;
+    if (!packed || !max_rounds || !workspace) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    if (mode == kModeLatent ? (!medians || !y_out) : !symbols_out) return fcai::fail(FCAI_ERR_INVALID, "null output");
+    const int64_t chunks = (int64_t)B * K;
+    if (chunks > INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "B * K exceeds the header's int32 range");
+    // coders/warp_div.py:56-61 (structure of the payload sizes)
+    if (header_bytes % 16 || header_bytes < 32 + 4 * chunks)
+        return fcai::fail(FCAI_ERR_INVALID, "warp_div header size does not match chunk metadata");
+    if (packed_bytes % 4) return fcai::fail(FCAI_ERR_INVALID, "warp_div packed payload must be uint32 aligned");
+    DecLayout dl = dec_layout(chunks);
+    if (workspace_bytes < dl.fixed_bytes)
+        return fcai::fail(FCAI_ERR_WORKSPACE, "decode workspace needs %lld bytes", (long long)dl.fixed_bytes);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    Control *ctrl = reinterpret_cast<Control *>(ws);
+    unsigned long long *offs = reinterpret_cast<unsigned long long *>(ws + dl.offsets);
+
+    DecPrepParams pp{packed, max_rounds, chunks, B, N, K, chunk_len, header_bytes, packed_bytes, ctrl, offs};
+    decode_prep_kernel<<<1, 1024, 0, stream>>>(pp);
+    FCAI_CUDA_TRY(cudaGetLastError());
+
+    DecParams p;
+    p.packed = packed;
+    p.header_bytes = header_bytes;
+    p.max_rounds = max_rounds;
+    p.idx = indexes;
+    p.medians = medians;
+    p.y_out = y_out;
+    p.t = TableArgs{cdfs, cdf_sizes, offsets, C, L};
+    p.B = B;
+    p.N = N;
+    p.K = K;
+    p.chunk_len = chunk_len;
+    p.HW = N / C;
+    p.chunks = chunks;
+    p.ctrl = ctrl;
+    p.offsets = offs;
+    p.out = symbols_out;
+    const int64_t smem = decode_smem_bytes(C, L);
+    const bool sm = smem <= kMaxSmemBytes;
+    if (mode == kModeIdx) rc = sm ? launch_decode<kModeIdx, true>(p, smem, stream) : launch_decode<kModeIdx, false>(p, smem, stream);
+    else if (mode == kModeChannel) rc = sm ? launch_decode<kModeChannel, true>(p, smem, stream) : launch_decode<kModeChannel, false>(p, smem, stream);
+    else rc = sm ? launch_decode<kModeLatent, true>(p, smem, stream) : launch_decode<kModeLatent, false>(p, smem, stream);
+    if (rc) return rc;
+    if (!check) return FCAI_OK;
+    long long flags = 0;
+    FCAI_CUDA_TRY(cudaMemcpyAsync(&flags, &ctrl->status[kStFlags], sizeof(flags), cudaMemcpyDeviceToHost, stream));
+    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (index_layout_is_channel) *index_layout_is_channel = (flags & kFlagNonChannel) ? 0 : 1;
+    return flags_to_status(flags, false);
+}
+
+}  // namespace wd
+
+using namespace wd;
+
+extern "C" {
+
+const char *fcai_last_error(void) { return fcai::g_last_error.c_str(); }
+
+const char *fcai_version(void) { return "fcai-b200 0.1.0 (sm_100a)"; }
+
+int fcai_warp_div_plan_create(int32_t B, int32_t N, int32_t C, int32_t P, fcai_warp_div_plan *plan) {
+    fcai::clear_error();
+    if (!plan) return fcai::fail(FCAI_ERR_INVALID, "plan is null");
+    Dims d;
+    int rc = make_dims(B, N, C, P, d);
+    if (rc) return rc;
+    EncLayout el = enc_layout(d.chunks);
+    DecLayout dl = dec_layout(d.chunks);
+    plan->chunks = d.K;
+    plan->chunk_len = d.chunk_len;
+    plan->header_bytes = d.header_bytes;
+    plan->encode_workspace_bytes = el.fixed_bytes + d.chunks * rows_worst(d) * kLanes * 4;
+    plan->decode_workspace_bytes = dl.fixed_bytes;
+    plan->max_packed_bytes = d.header_bytes + d.chunks * rows_worst(d) * kLanes * 4;
+    return FCAI_OK;
+}
+
+int fcai_warp_div_encode(const int32_t *symbols, const int32_t *indexes, int32_t B, int32_t N, const int32_t *cdfs,
+                         int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets, int32_t P,
+                         void *workspace, int64_t workspace_bytes, uint32_t *max_rounds,
+                         fcai_warp_div_encode_info *info, fcai_stream_t stream) {
+    fcai::clear_error();
+    return encode_impl(indexes ? kModeIdx : kModeChannel, symbols, indexes, nullptr, nullptr, B, N, cdfs, C, L,
+                       cdf_sizes, offsets, P, workspace, workspace_bytes, max_rounds, info,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B, int32_t N, const int32_t *cdfs,
+                                int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets, int32_t P,
+                                void *workspace, int64_t workspace_bytes, uint32_t *max_rounds,
+                                fcai_warp_div_encode_info *info, fcai_stream_t stream) {
+    fcai::clear_error();
+    return encode_impl(kModeLatent, nullptr, nullptr, y, medians, B, N, cdfs, C, L, cdf_sizes, offsets, P, workspace,
+                       workspace_bytes, max_rounds, info, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fcai_warp_div_encode_pack(const void *workspace, int64_t workspace_bytes, int32_t B, int32_t N, int32_t C,
+                              int32_t P, uint8_t *packed, int64_t packed_bytes, fcai_stream_t stream_) {
+    fcai::clear_error();
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    Dims d;
+    int rc = make_dims(B, N, C, P, d);
+    if (rc) return rc;
+    if (!workspace || !packed) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    EncLayout el = enc_layout(d.chunks);
+    if (workspace_bytes < el.fixed_bytes) return fcai::fail(FCAI_ERR_WORKSPACE, "encode workspace too small");
+    if (packed_bytes < d.header_bytes || (packed_bytes - d.header_bytes) % (kLanes * 4))
+        return fcai::fail(FCAI_ERR_INVALID, "packed size %lld is not a warp_div payload size", (long long)packed_bytes);
+    const uint8_t *ws = static_cast<const uint8_t *>(workspace);
+    PackParams p;
+    p.ctrl = reinterpret_cast<const Control *>(ws);
+    p.rounds = reinterpret_cast<const int32_t *>(ws + el.rounds);
+    p.used = reinterpret_cast<const int32_t *>(ws + el.used);
+    p.offsets = reinterpret_cast<const unsigned long long *>(ws + el.offsets);
+    p.stage = reinterpret_cast<const uint32_t *>(ws + el.stage);
+    p.chunks = d.chunks;
+    p.B = d.B;
+    p.N = d.N;
+    p.K = d.K;
+    p.chunk_len = d.chunk_len;
+    p.header_bytes = d.header_bytes;
+    p.packed_bytes = packed_bytes;
+    p.packed = packed;
+    int64_t want = (d.chunks + kWarps - 1) / kWarps;
+    int64_t cap = (int64_t)fcai::sm_count() * 8;
+    int grid = (int)(want < cap ? want : cap);
+    pack_kernel<<<grid, kThreads, 0, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+int fcai_warp_div_decode(const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
+                         int64_t header_bytes, int32_t chunk_len, const int32_t *indexes, int32_t B, int32_t N,
+                         const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                         const int32_t *offsets, int32_t *symbols_out, void *workspace, int64_t workspace_bytes,
+                         int32_t check, int32_t *index_layout_is_channel, fcai_stream_t stream) {
+    fcai::clear_error();
+    return decode_impl(indexes ? kModeIdx : kModeChannel, packed, packed_bytes, max_rounds, K, header_bytes, chunk_len,
+                       indexes, B, N, cdfs, C, L, cdf_sizes, offsets, nullptr, symbols_out, nullptr, workspace,
+                       workspace_bytes, check, index_layout_is_channel, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fcai_warp_div_decode_latent(const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
+                                int64_t header_bytes, int32_t chunk_len, int32_t B, int32_t N, const int32_t *cdfs,
+                                int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets,
+                                const float *medians, float *y_hat_out, void *workspace, int64_t workspace_bytes,
+                                int32_t check, fcai_stream_t stream) {
+    fcai::clear_error();
+    return decode_impl(kModeLatent, packed, packed_bytes, max_rounds, K, header_bytes, chunk_len, nullptr, B, N, cdfs,
+                       C, L, cdf_sizes, offsets, medians, nullptr, y_hat_out, workspace, workspace_bytes, check,
+                       nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

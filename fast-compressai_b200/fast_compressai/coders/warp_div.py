@@ -1,0 +1,351 @@
+"""WarpANS ``warp_div`` GPU backend (B200 build).
+
+Public surface identical to the reference's coders/warp_div.py:20-215:
+``WarpDivPayload`` (frozen dataclass, same fields, same validation and format
+id) and ``WarpDivBackend.encode/decode``.  Payloads are device-local.
+
+Host overhead differs from the reference, not the results:
+  * the index range check, the header check and the round-table check run
+    on the GPU inside the coder (the reference copies the index min/max and
+    the header to the host before every call);
+  * the SHA-256 coding fingerprint has the reference's value
+    (sha256 over ``str(shape)`` + little-endian bytes of indexes, cdfs,
+    cdf_sizes, offsets), but when the coder reports that ``indexes`` is the
+    channel layout ``index = i // (N // C)`` the index part of the digest
+    comes from a per-(B, N, C) cache instead of a device-to-host copy;
+  * ``WarpDivPayload`` reuses the round statistics the encoder already
+    knows instead of re-reading ``max_rounds`` from the device.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import importlib
+import threading
+import weakref
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+import torch
+
+from .. import _native
+from .capabilities import warp_div_capability
+from .errors import CoderDependencyError, CoderInputError
+
+FORMAT_ID = "warpans-v2-warp-div-v1-decode"
+FORMAT_VERSION = 1
+
+# ---------------------------------------------------------------------------
+# max_rounds statistics registry: tensor identity -> (min >= 2, sum)
+# ---------------------------------------------------------------------------
+_STATS_LOCK = threading.Lock()
+_ROUND_STATS: dict[int, tuple] = {}
+
+
+def _remember_rounds(max_rounds: torch.Tensor, total_rounds: int) -> None:
+    with _STATS_LOCK:
+        _ROUND_STATS[id(max_rounds)] = (weakref.ref(max_rounds), max_rounds._version, max_rounds.data_ptr(),
+                                        True, int(total_rounds))
+        if len(_ROUND_STATS) > 4096:
+            for key in [k for k, v in _ROUND_STATS.items() if v[0]() is None]:
+                del _ROUND_STATS[key]
+
+
+def _round_stats(max_rounds: torch.Tensor) -> tuple[bool, int]:
+    """(all rounds >= 2, sum of rounds)."""
+    with _STATS_LOCK:
+        hit = _ROUND_STATS.get(id(max_rounds))
+    if hit is not None and hit[0]() is max_rounds and hit[1] == max_rounds._version and hit[2] == max_rounds.data_ptr():
+        return hit[3], hit[4]
+    rounds = max_rounds.to(torch.int64)
+    if rounds.numel() == 0:
+        return True, 0
+    both = torch.stack((rounds.min(), rounds.sum())).cpu()
+    return bool(int(both[0]) >= 2), int(both[1])
+
+
+@dataclass(frozen=True)
+class WarpDivPayload:
+    packed: torch.Tensor
+    max_rounds: torch.Tensor
+    header_bytes: int
+    chunk_len: int
+    p_ch: int
+    batch: int
+    symbols_per_batch: int
+    cdf_count: int
+    coding_fingerprint: str | None = None
+    format_id: str = FORMAT_ID
+    format_version: int = FORMAT_VERSION
+
+    def __post_init__(self) -> None:
+        # coders/warp_div.py:34-67 of the reference, same order and messages
+        if self.format_id != FORMAT_ID or self.format_version != FORMAT_VERSION:
+            raise CoderInputError("unsupported warp_div payload format")
+        if (not isinstance(self.packed, torch.Tensor) or self.packed.device.type != "cuda"
+                or self.packed.dtype != torch.uint8 or not self.packed.is_contiguous()):
+            raise CoderInputError("packed payload must be contiguous CUDA uint8")
+        if (not isinstance(self.max_rounds, torch.Tensor) or self.max_rounds.device != self.packed.device
+                or self.max_rounds.dtype != torch.uint32 or not self.max_rounds.is_contiguous()):
+            raise CoderInputError("max_rounds must be contiguous CUDA uint32 on the packed payload device")
+        if self.coding_fingerprint is not None and (
+            not isinstance(self.coding_fingerprint, str) or len(self.coding_fingerprint) != 64
+            or any(char not in "0123456789abcdef" for char in self.coding_fingerprint)
+        ):
+            raise CoderInputError("coding_fingerprint must be a SHA-256 hex digest")
+        if min(self.header_bytes, self.chunk_len, self.p_ch, self.batch, self.symbols_per_batch, self.cdf_count) <= 0:
+            raise CoderInputError("warp_div metadata values must be positive")
+        if self.p_ch > self.cdf_count or self.symbols_per_batch % self.cdf_count:
+            raise CoderInputError("warp_div payload P_ch/channel metadata is inconsistent")
+        expected_chunks = (self.cdf_count + self.p_ch - 1) // self.p_ch
+        if tuple(self.max_rounds.shape) != (self.batch, expected_chunks):
+            raise CoderInputError("warp_div max_rounds shape does not match payload metadata")
+        if self.chunk_len != self.p_ch * (self.symbols_per_batch // self.cdf_count):
+            raise CoderInputError("warp_div chunk_len does not match P_ch and symbol dimensions")
+        if self.header_bytes > self.packed.numel():
+            raise CoderInputError("warp_div header exceeds packed payload size")
+        if self.header_bytes % 16 or self.header_bytes < 32 + self.max_rounds.numel() * 4:
+            raise CoderInputError("warp_div header size does not match chunk metadata")
+        if self.packed.numel() % 4:
+            raise CoderInputError("warp_div packed payload must be uint32 aligned")
+        all_ok, total = _round_stats(self.max_rounds)
+        if not all_ok:
+            raise CoderInputError("warp_div chunk rounds must include two initial state words")
+        if self.header_bytes + total * 32 * 4 != self.packed.numel():
+            raise CoderInputError("warp_div packed payload length does not match chunk rounds")
+
+
+# ---------------------------------------------------------------------------
+# Coding fingerprint (reference coders/warp_div.py:152-158)
+# ---------------------------------------------------------------------------
+_FP_LOCK = threading.Lock()
+_CHANNEL_STATES: dict[tuple[int, int, int], "hashlib._Hash"] = {}
+_TABLE_BYTES: dict[int, tuple] = {}
+
+
+def _shape_bytes(shape) -> bytes:
+    return bytes(str(tuple(int(s) for s in shape)), "ascii")
+
+
+def _channel_layout_state(B: int, N: int, C: int):
+    """sha256 state after hashing the channel-layout index tensor [B, N]."""
+    key = (B, N, C)
+    with _FP_LOCK:
+        state = _CHANNEL_STATES.get(key)
+    if state is None:
+        state = hashlib.sha256()
+        state.update(_shape_bytes((B, N)))
+        row = (np.arange(N, dtype=np.int64) // (N // C)).astype("<i4").tobytes()
+        for _ in range(B):
+            state.update(row)
+        with _FP_LOCK:
+            if len(_CHANNEL_STATES) > 64:
+                _CHANNEL_STATES.clear()
+            _CHANNEL_STATES[key] = state
+    return state.copy()
+
+
+def _tensor_digest_bytes(t: torch.Tensor) -> bytes:
+    """str(shape) + little-endian bytes, cached per live tensor and version."""
+    key = id(t)
+    with _FP_LOCK:
+        hit = _TABLE_BYTES.get(key)
+    if hit is not None and hit[0]() is t and hit[1] == t._version and hit[2] == t.data_ptr():
+        return hit[3]
+    cpu = t.detach().contiguous().cpu()
+    data = _shape_bytes(cpu.shape) + cpu.numpy().tobytes()
+    if t.numel() <= (1 << 20):
+        with _FP_LOCK:
+            if len(_TABLE_BYTES) > 256:
+                for k in [k for k, v in _TABLE_BYTES.items() if v[0]() is None]:
+                    del _TABLE_BYTES[k]
+            _TABLE_BYTES[key] = (weakref.ref(t), t._version, t.data_ptr(), data)
+    return data
+
+
+def _coding_fingerprint(indexes: torch.Tensor | None, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,
+                        offsets: torch.Tensor, *, channel_layout: bool = False,
+                        batch: int | None = None, symbols_per_batch: int | None = None) -> str:
+    """SHA-256 of (indexes, cdfs, cdf_sizes, offsets) exactly as the reference computes it.
+
+    ``channel_layout=True`` (the coder verified it, or ``indexes`` is None)
+    takes the index part from the per-shape cache."""
+    if indexes is None or channel_layout:
+        B, N = (batch, symbols_per_batch) if indexes is None else (int(indexes.shape[0]), int(indexes.shape[1]))
+        digest = _channel_layout_state(int(B), int(N), int(cdfs.shape[0]))
+    else:
+        digest = hashlib.sha256()
+        digest.update(_tensor_digest_bytes(indexes))
+    for t in (cdfs, cdf_sizes, offsets):
+        digest.update(_tensor_digest_bytes(t))
+    return digest.hexdigest()
+
+
+def _validate_inputs(symbols, indexes, cdfs, cdf_sizes, offsets, p_ch: int) -> None:
+    """Reference coders/warp_div.py:179-215, except the index range check,
+    which the coder kernels perform on the device (same error)."""
+    if not isinstance(symbols, torch.Tensor) or not isinstance(indexes, torch.Tensor):
+        raise CoderInputError("symbols and indexes must be torch tensors")
+    tensors: Sequence[torch.Tensor] = (symbols, indexes, cdfs, cdf_sizes, offsets)
+    if any(not isinstance(value, torch.Tensor) for value in tensors):
+        raise CoderInputError("indexes, CDFs, CDF sizes, and offsets must be tensors")
+    if type(p_ch) is not int or p_ch <= 0:
+        raise CoderInputError("p_ch must be a positive integer")
+    if symbols.device.type != "cuda" or any(value.device != symbols.device for value in tensors):
+        raise CoderInputError("all coder inputs must be CUDA tensors on the same device")
+    if any(value.dtype != torch.int32 for value in tensors):
+        raise CoderInputError("all warp_div input tensors must use torch.int32")
+    if any(not value.is_contiguous() for value in tensors):
+        raise CoderInputError("all warp_div input tensors must be contiguous")
+    if symbols.ndim != 2 or indexes.shape != symbols.shape:
+        raise CoderInputError("symbols and indexes must have matching [B, N] shape")
+    if cdfs.ndim != 2 or cdf_sizes.ndim != 1 or offsets.ndim != 1:
+        raise CoderInputError("CDF must be [M,L] and CDF sizes/offsets must be [M]")
+    if cdfs.shape[0] <= 0 or cdfs.shape[1] < 2:
+        raise CoderInputError("CDF table cannot be empty")
+    if cdf_sizes.numel() != cdfs.shape[0] or offsets.numel() != cdfs.shape[0]:
+        raise CoderInputError("CDF, CDF sizes, and offsets must have the same table count")
+    if symbols.shape[0] <= 0 or symbols.shape[1] <= 0:
+        raise CoderInputError("empty symbols are not supported by this WarpANS format")
+    if symbols.shape[1] % cdfs.shape[0] != 0:
+        raise CoderInputError("symbols per batch must be divisible by CDF count for WarpANS channel layout")
+    if p_ch > cdfs.shape[0]:
+        raise CoderInputError("p_ch cannot exceed the number of CDF channels")
+
+
+_INDEX_RANGE_MESSAGE = "indexes contain a value outside the CDF table range"
+
+
+def _raise_coder_error(exc: Exception, what: str) -> None:
+    if isinstance(exc, _native.NativeCallError):
+        if exc.code == _native.FCAI_ERR_INDEX_RANGE:
+            raise CoderInputError(_INDEX_RANGE_MESSAGE) from exc
+        if exc.code in (_native.FCAI_ERR_HEADER, _native.FCAI_ERR_ROUNDS):
+            raise CoderInputError(str(exc)) from exc
+    raise CoderInputError(f"warp_div {what} failed: {exc}") from exc
+
+
+class WarpDivBackend:
+    """WarpANS V2 fast-division encoder with V1-compatible decode (B200 kernels)."""
+
+    name = "warp_div"
+    format_id = FORMAT_ID
+    format_version = FORMAT_VERSION
+
+    def __init__(self) -> None:
+        capability = warp_div_capability()
+        if not capability.available:
+            raise CoderDependencyError(f"warp_div unavailable: {capability.reason}")
+        try:
+            self._extension = importlib.import_module("fast_compressai.coders._warp_div")
+            _native.lib()
+        except (ImportError, OSError) as exc:
+            raise CoderDependencyError(f"warp_div extension could not be loaded: {exc}") from exc
+
+    def encode(self, symbols: torch.Tensor, indexes: torch.Tensor, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,
+               offsets: torch.Tensor, *, p_ch: int) -> WarpDivPayload:
+        _validate_inputs(symbols, indexes, cdfs, cdf_sizes, offsets, p_ch)
+        return self._encode(symbols, indexes, cdfs, cdf_sizes, offsets, p_ch)
+
+    def _encode(self, symbols, indexes, cdfs, cdf_sizes, offsets, p_ch: int) -> WarpDivPayload:
+        try:
+            r = self._extension.encode(symbols, indexes, cdfs, cdf_sizes, offsets, int(p_ch))
+        except (_native.NativeCallError, RuntimeError) as exc:
+            _raise_coder_error(exc, "encode")
+        B, N = int(symbols.shape[0]), int(symbols.shape[1])
+        _remember_rounds(r.max_rounds, (r.packed.numel() - r.header_bytes) // 128)
+        fingerprint = _coding_fingerprint(indexes, cdfs, cdf_sizes, offsets, channel_layout=r.index_layout_is_channel,
+                                          batch=B, symbols_per_batch=N)
+        return WarpDivPayload(
+            packed=r.packed,
+            max_rounds=r.max_rounds,
+            header_bytes=r.header_bytes,
+            chunk_len=r.chunk_len,
+            p_ch=r.p_ch,
+            batch=B,
+            symbols_per_batch=N,
+            cdf_count=int(cdfs.shape[0]),
+            coding_fingerprint=fingerprint,
+        )
+
+    def _encode_latent(self, y: torch.Tensor, medians: torch.Tensor, cdfs, cdf_sizes, offsets,
+                       p_ch: int) -> WarpDivPayload:
+        """Quantise ``y`` [B, C, ...] against ``medians`` [C] and encode it
+        with the channel-layout indexes (the codec path)."""
+        try:
+            r = self._extension.encode_latent(y, medians, cdfs, cdf_sizes, offsets, int(p_ch))
+        except (_native.NativeCallError, RuntimeError) as exc:
+            _raise_coder_error(exc, "encode")
+        B = int(y.shape[0])
+        N = int(y.numel() // B)
+        _remember_rounds(r.max_rounds, (r.packed.numel() - r.header_bytes) // 128)
+        return WarpDivPayload(
+            packed=r.packed,
+            max_rounds=r.max_rounds,
+            header_bytes=r.header_bytes,
+            chunk_len=r.chunk_len,
+            p_ch=r.p_ch,
+            batch=B,
+            symbols_per_batch=N,
+            cdf_count=int(cdfs.shape[0]),
+            coding_fingerprint=_coding_fingerprint(None, cdfs, cdf_sizes, offsets, batch=B, symbols_per_batch=N),
+        )
+
+    def _decode_latent(self, payload: WarpDivPayload, cdfs, cdf_sizes, offsets, medians: torch.Tensor,
+                       out: torch.Tensor) -> torch.Tensor:
+        """Decode ``payload`` (channel-layout indexes) into ``out = symbols + medians``."""
+        if not isinstance(payload, WarpDivPayload):
+            raise CoderInputError("warp_div decode expects WarpDivPayload")
+        if cdfs.shape[0] != payload.cdf_count or cdfs.device != payload.packed.device:
+            raise CoderInputError("CDF count or CUDA device does not match payload metadata")
+        if payload.coding_fingerprint is not None and payload.coding_fingerprint != _coding_fingerprint(
+                None, cdfs, cdf_sizes, offsets, batch=payload.batch, symbols_per_batch=payload.symbols_per_batch):
+            raise CoderInputError("coding tables or indexes do not match warp_div payload")
+        if payload.batch >= 32768:
+            raise CoderInputError("warp_div packed header is inconsistent with payload metadata")
+        try:
+            return self._extension.decode_latent(payload.packed, payload.max_rounds, payload.header_bytes,
+                                                 payload.chunk_len, cdfs, cdf_sizes, offsets, medians, out)
+        except (_native.NativeCallError, RuntimeError) as exc:
+            _raise_coder_error(exc, "decode")
+
+    def decode(self, payload: WarpDivPayload, indexes: torch.Tensor, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,
+               offsets: torch.Tensor) -> torch.Tensor:
+        if not isinstance(payload, WarpDivPayload):
+            raise CoderInputError("warp_div decode expects WarpDivPayload")
+        _validate_inputs(indexes, indexes, cdfs, cdf_sizes, offsets, payload.p_ch)
+        if tuple(indexes.shape) != (payload.batch, payload.symbols_per_batch):
+            raise CoderInputError("indexes shape does not match payload metadata")
+        return self._decode(payload, indexes, cdfs, cdf_sizes, offsets)
+
+    def _decode(self, payload: WarpDivPayload, indexes: torch.Tensor | None, cdfs, cdf_sizes, offsets,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        if cdfs.shape[0] != payload.cdf_count or cdfs.device != payload.packed.device:
+            raise CoderInputError("CDF count or CUDA device does not match payload metadata")
+        if payload.batch >= 32768:
+            # the reference compares header word 2 read as int32 with
+            # (batch << 16) | K, which can never match for batch >= 2^15
+            # (coders/warp_div.py:169); kept for drop-in parity
+            raise CoderInputError("warp_div packed header is inconsistent with payload metadata")
+        try:
+            symbols, layout_is_channel = self._extension.decode(
+                payload.packed, payload.max_rounds, payload.header_bytes, payload.chunk_len, indexes, cdfs,
+                cdf_sizes, offsets, batch=payload.batch, symbols_per_batch=payload.symbols_per_batch, out=out,
+                return_layout=True)
+        except (_native.NativeCallError, RuntimeError) as exc:
+            # the reference compares the fingerprint before it reads the
+            # header (coders/warp_div.py:130-132): report a table mismatch first
+            if (isinstance(exc, _native.NativeCallError) and exc.code != _native.FCAI_ERR_INDEX_RANGE
+                    and payload.coding_fingerprint is not None
+                    and payload.coding_fingerprint != _coding_fingerprint(
+                        indexes, cdfs, cdf_sizes, offsets, batch=payload.batch,
+                        symbols_per_batch=payload.symbols_per_batch)):
+                raise CoderInputError("coding tables or indexes do not match warp_div payload") from exc
+            _raise_coder_error(exc, "decode")
+        if payload.coding_fingerprint is not None:
+            actual = _coding_fingerprint(indexes, cdfs, cdf_sizes, offsets, channel_layout=layout_is_channel,
+                                         batch=payload.batch, symbols_per_batch=payload.symbols_per_batch)
+            if payload.coding_fingerprint != actual:
+                raise CoderInputError("coding tables or indexes do not match warp_div payload")
+        return symbols

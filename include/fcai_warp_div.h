@@ -1,0 +1,158 @@
+/*
+ * fcai_warp_div.h -- C ABI of the B200 `warp_div` entropy coder.
+ *
+ * This library replaces the reference's native module
+ * `fast_compressai.coders._warp_div` (coders/cuda/ans_gpu.cpp:25-30), whose
+ * two pybind entry points take and return torch tensors:
+ *
+ *   encode_warp_div(symbols, indexes, cdfs, cdf_sizes, offsets, P)
+ *       -> (packed, max_rounds, header_bytes, chunk_len, P)
+ *       coders/cuda/warp_ans_kernel_v2.cu:183-306
+ *   decode_warp_div(packed, max_rounds, header_bytes, chunk_len, P,
+ *                   indexes, cdfs, cdf_sizes, offsets) -> symbols
+ *       coders/cuda/warp_ans_kernel.cu:477-544
+ *
+ * Here every buffer is a plain device pointer owned by the caller.  The
+ * payload size is only known after encoding, so encode is split in two
+ * calls: fcai_warp_div_encode() codes the symbols into the workspace and
+ * reports the exact payload size (one small device-to-host read, the only
+ * synchronisation of the encode path); fcai_warp_div_encode_pack() then
+ * writes the payload into a buffer of exactly that size.
+ *
+ * Payload layout (bit-exact with the reference, little-endian u32 words):
+ *   h0 = N, h1 = chunk_len, h2 = K | B << 16, h3 = 2 | 32 << 16,
+ *   h4..h7 = 0, then int32 max_rounds[B*K] at byte 32, zero padding to a
+ *   16-byte boundary (header_bytes), then for every chunk (b-major) its
+ *   max_rounds x 32 interleaved words: word r of lane L at r*32 + L.
+ *
+ * All calls enqueue work on `stream` of the current CUDA device; the caller
+ * selects the device.  Inputs are int32 and contiguous.  `indexes` may be
+ * NULL, meaning the channel layout indexes[b, i] = i / (N / C) that
+ * CompressAI's EntropyBottleneck builds; results are identical to passing
+ * that tensor explicitly.
+ *
+ * Workspaces: the first 256 bytes of every workspace are a control block that
+ * must be zero before its first use (e.g. cudaMemset); every call leaves it
+ * zero again.  A workspace must not be used by two calls that can overlap on
+ * the GPU.
+ */
+#ifndef FCAI_WARP_DIV_H
+#define FCAI_WARP_DIV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *fcai_stream_t; /* a cudaStream_t; NULL = default stream */
+
+/* Status codes.  Values 1..7 are caller errors that the Python layer maps
+ * to CoderInputError, as the reference maps TORCH_CHECK failures
+ * (coders/warp_div.py:101-102,148-149). */
+enum {
+    FCAI_OK = 0,
+    FCAI_ERR_INVALID = 1,     /* bad argument, shape or size limit */
+    FCAI_ERR_INDEX_RANGE = 2, /* an index outside [0, C) */
+    FCAI_ERR_TABLE = 3,       /* cdf_size outside [2, L] or a row not strictly increasing in [0, 65536] */
+    FCAI_ERR_HEADER = 4,      /* payload header words inconsistent with the metadata */
+    FCAI_ERR_ROUNDS = 5,      /* header round table differs from max_rounds */
+    FCAI_ERR_CORRUPT = 6,     /* payload length or body inconsistent with the rounds */
+    FCAI_ERR_WORKSPACE = 7,   /* workspace smaller than the plan requires */
+    FCAI_ERR_CUDA = 8         /* a CUDA runtime call failed */
+};
+
+/* Sizes derived from (B, N, C, P), as the reference host code derives them
+ * (coders/cuda/warp_ans_kernel_v2.cu:216-279). */
+typedef struct {
+    int32_t chunks;                 /* K = ceil(C / P) */
+    int32_t chunk_len;              /* P * (N / C) */
+    int64_t header_bytes;           /* align16(32 + 4 * B * K) */
+    int64_t encode_workspace_bytes; /* for fcai_warp_div_encode / _pack */
+    int64_t decode_workspace_bytes; /* for fcai_warp_div_decode */
+    int64_t max_packed_bytes;       /* worst-case payload size */
+} fcai_warp_div_plan;
+
+/* Checks the reference's size preconditions (warp_ans_kernel_v2.cu:198-203:
+ * B, N, C > 0, N % C == 0, 1 <= P <= C, B and C <= 65535, N * C < 2^31 - 1)
+ * and fills `plan`. */
+int fcai_warp_div_plan_create(int32_t B, int32_t N, int32_t C, int32_t P, fcai_warp_div_plan *plan);
+
+typedef struct {
+    int64_t packed_bytes;           /* exact payload size for _pack */
+    int64_t header_bytes;
+    int64_t required_workspace_bytes; /* smallest workspace that holds this
+                                         call's staging (set on success and
+                                         on FCAI_ERR_WORKSPACE) */
+    int32_t chunk_len;
+    int32_t p_ch;
+    int32_t index_layout_is_channel; /* 1 when indexes == channel layout (or NULL) */
+    int32_t reserved;
+} fcai_warp_div_encode_info;
+
+/* Encode symbols[B,N] (replaces encode_with_indexes_warp_v2_cuda,
+ * coders/cuda/warp_ans_kernel_v2.cu:183-306, up to the payload allocation).
+ * Writes max_rounds[B*K] (uint32, device) and fills *info on the host.
+ * Blocks the host until the size is known.  A workspace of
+ * plan.encode_workspace_bytes always suffices; a smaller one works while the
+ * lanes' words fit and otherwise returns FCAI_ERR_WORKSPACE with
+ * info->required_workspace_bytes set, after which the call can be repeated
+ * with a larger workspace. */
+int fcai_warp_div_encode(const int32_t *symbols, const int32_t *indexes, int32_t B, int32_t N,
+                         const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                         const int32_t *offsets, int32_t P, void *workspace, int64_t workspace_bytes,
+                         uint32_t *max_rounds, fcai_warp_div_encode_info *info, fcai_stream_t stream);
+
+/* Write the payload of the last fcai_warp_div_encode on this workspace into
+ * packed[packed_bytes] (the header and pack steps, warp_ans_kernel.cu:178-213,
+ * 343-369).  Asynchronous. */
+int fcai_warp_div_encode_pack(const void *workspace, int64_t workspace_bytes, int32_t B, int32_t N, int32_t C,
+                              int32_t P, uint8_t *packed, int64_t packed_bytes, fcai_stream_t stream);
+
+/* Decode a payload into symbols_out[B,N] (replaces
+ * decode_with_indexes_warp_cuda, coders/cuda/warp_ans_kernel.cu:477-544,
+ * together with the header check of coders/warp_div.py:161-176).  K is
+ * taken from max_rounds' shape as in the reference; the workspace needs
+ * 256 + align256(8 * B * K) bytes.  With check != 0 the call waits for the
+ * GPU and returns FCAI_ERR_HEADER / _ROUNDS / _CORRUPT / _INDEX_RANGE /
+ * _TABLE when the payload or tables are inconsistent (symbols_out then
+ * holds no result) and, if index_layout_is_channel is not NULL, stores
+ * whether indexes equal the channel layout.  With check == 0 the call is
+ * asynchronous and a bad payload leaves symbols_out unspecified. */
+int fcai_warp_div_decode(const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
+                         int64_t header_bytes, int32_t chunk_len, const int32_t *indexes, int32_t B, int32_t N,
+                         const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                         const int32_t *offsets, int32_t *symbols_out, void *workspace, int64_t workspace_bytes,
+                         int32_t check, int32_t *index_layout_is_channel, fcai_stream_t stream);
+
+/* Encode straight from the fp32 latent y[B, C*H*W] of a FactorizedPrior:
+ * symbol = (int32)rint(y - medians[c]) with the channel layout, which is
+ * CompressAI's EntropyBottleneck.quantize(y, "symbols", medians) followed by
+ * the reference codec's encode (coders/factorized.py:46-59) in one pass.
+ * The payload equals fcai_warp_div_encode's for those symbols. */
+int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B, int32_t N, const int32_t *cdfs,
+                                int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets, int32_t P,
+                                void *workspace, int64_t workspace_bytes, uint32_t *max_rounds,
+                                fcai_warp_div_encode_info *info, fcai_stream_t stream);
+
+/* Decode straight to the fp32 dequantised latent y_hat = (float)symbol +
+ * medians[c] (coders/factorized.py:90-101: decode, then
+ * EntropyBottleneck.dequantize), channel layout. */
+int fcai_warp_div_decode_latent(const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
+                                int64_t header_bytes, int32_t chunk_len, int32_t B, int32_t N, const int32_t *cdfs,
+                                int32_t C, int32_t L, const int32_t *cdf_sizes, const int32_t *offsets,
+                                const float *medians, float *y_hat_out, void *workspace, int64_t workspace_bytes,
+                                int32_t check, fcai_stream_t stream);
+
+/* Message of the last error on the calling thread ("" if none). */
+const char *fcai_last_error(void);
+
+/* Library version string. */
+const char *fcai_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FCAI_WARP_DIV_H */
