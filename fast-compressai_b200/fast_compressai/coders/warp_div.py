@@ -43,9 +43,14 @@ _STATS_LOCK = threading.Lock()
 _ROUND_STATS: dict[int, tuple] = {}
 
 
+def _version(t: torch.Tensor) -> int:
+    """In-place version counter; inference tensors have none (-1)."""
+    return -1 if t.is_inference() else t._version
+
+
 def _remember_rounds(max_rounds: torch.Tensor, total_rounds: int) -> None:
     with _STATS_LOCK:
-        _ROUND_STATS[id(max_rounds)] = (weakref.ref(max_rounds), max_rounds._version, max_rounds.data_ptr(),
+        _ROUND_STATS[id(max_rounds)] = (weakref.ref(max_rounds), _version(max_rounds), max_rounds.data_ptr(),
                                         True, int(total_rounds))
         if len(_ROUND_STATS) > 4096:
             for key in [k for k, v in _ROUND_STATS.items() if v[0]() is None]:
@@ -56,7 +61,7 @@ def _round_stats(max_rounds: torch.Tensor) -> tuple[bool, int]:
     """(all rounds >= 2, sum of rounds)."""
     with _STATS_LOCK:
         hit = _ROUND_STATS.get(id(max_rounds))
-    if hit is not None and hit[0]() is max_rounds and hit[1] == max_rounds._version and hit[2] == max_rounds.data_ptr():
+    if hit is not None and hit[0]() is max_rounds and hit[1] == _version(max_rounds) and hit[2] == max_rounds.data_ptr():
         return hit[3], hit[4]
     rounds = max_rounds.to(torch.int64)
     if rounds.numel() == 0:
@@ -151,16 +156,16 @@ def _tensor_digest_bytes(t: torch.Tensor) -> bytes:
     key = id(t)
     with _FP_LOCK:
         hit = _TABLE_BYTES.get(key)
-    if hit is not None and hit[0]() is t and hit[1] == t._version and hit[2] == t.data_ptr():
+    if hit is not None and hit[0]() is t and hit[1] == _version(t) and hit[2] == t.data_ptr():
         return hit[3]
     cpu = t.detach().contiguous().cpu()
     data = _shape_bytes(cpu.shape) + cpu.numpy().tobytes()
-    if t.numel() <= (1 << 20):
+    if t.numel() <= (1 << 20) and not t.is_inference():
         with _FP_LOCK:
             if len(_TABLE_BYTES) > 256:
                 for k in [k for k, v in _TABLE_BYTES.items() if v[0]() is None]:
                     del _TABLE_BYTES[k]
-            _TABLE_BYTES[key] = (weakref.ref(t), t._version, t.data_ptr(), data)
+            _TABLE_BYTES[key] = (weakref.ref(t), _version(t), t.data_ptr(), data)
     return data
 
 
