@@ -300,7 +300,7 @@ __device__ __forceinline__ void put_nibble(uint64_t &x, uint32_t val, LaneWriter
 }
 
 // Escape code of an out-of-range value (warp_ans_kernel_v2.cu:148-164).
-__device__ __noinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter &w) {
+__device__ __forceinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter &w) {
     int n_bypass = raw ? (31 - __clz(raw)) / (int)kBypassBits + 1 : 0;
     for (int j = n_bypass - 1; j >= 0; --j) put_nibble(x, (raw >> (j * kBypassBits)) & kBypassMax, w);
     int rem = n_bypass, n_full = 0;
@@ -390,6 +390,26 @@ struct EncParams {
     uint32_t *max_rounds_out;
 };
 
+constexpr int kPrefetch = 8;  // symbols each lane loads ahead of the coding chain
+
+// Loads lane symbols t0 .. t0+7 (reverse order: position last - 32 t) of one
+// image row, with their indexes in kModeIdx; latent values as float bits.
+template <int kMode>
+__device__ __forceinline__ void load_batch(const EncParams &p, int64_t row0, int last, int t0, int n,
+                                           int32_t (&v)[kPrefetch], int32_t (&iv)[kPrefetch]) {
+#pragma unroll
+    for (int u = 0; u < kPrefetch; ++u) {
+        const int t = t0 + u;
+        v[u] = 0;
+        iv[u] = 0;
+        if (t < n) {
+            const int64_t pos = row0 + last - t * kLanes;
+            v[u] = kMode == kModeLatent ? __float_as_int(__ldg(p.y + pos)) : __ldg(p.sym + pos);
+            if (kMode == kModeIdx) iv[u] = __ldg(p.idx + pos);
+        }
+    }
+}
+
 template <int kMode, bool kSmem>
 __global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
     constexpr bool kIdx = kMode == kModeIdx;
@@ -414,9 +434,10 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
     Tables<kSmem> tab{s_tab, s_ch, nullptr, p.t};
 
     const int lane = threadIdx.x & 31;
-    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
+    const int warps = blockDim.x >> 5;
+    const int64_t warp_stride = (int64_t)gridDim.x * warps;
     unsigned int my_max_used = 0;
-    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
+    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
         const int b = (int)(chunk / p.K);
         const int k = (int)(chunk - (int64_t)b * p.K);
         const int start = k * p.chunk_len;
@@ -425,49 +446,60 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
         LaneWriter w{p.stage + chunk * (int64_t)p.rows_cap * kLanes + lane, p.rows_cap, 0};
         if (first < end) {
             const int n = (end - 1 - first) / kLanes + 1;
-            int i = first + (n - 1) * kLanes;
-            int ct = i / p.HW, rem = i - ct * p.HW;  // channel-layout position tracker
-            const int32_t *srow = kMode == kModeLatent ? nullptr : p.sym + (int64_t)b * p.N;
-            const float *yrow = kMode == kModeLatent ? p.y + (int64_t)b * p.N : nullptr;
-            const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
+            const int last = first + (n - 1) * kLanes;
+            int ct = last / p.HW, rem = last - ct * p.HW;  // channel-layout position tracker
+            const int64_t row0 = (int64_t)b * p.N;
             uint64_t x = kRansL;
-#pragma unroll 2
-            for (int t = 0; t < n; ++t) {
-                int32_t s;
-                if (kMode == kModeLatent) {
-                    // torch.round (half to even) then .int(), both in fp32
-                    s = __float2int_rz(rintf(__ldg(yrow + i) - __ldg(p.medians + ct)));
-                } else {
-                    s = __ldg(srow + i);
-                }
-                int c = ct;
-                if (kIdx) {
-                    const int32_t ci = __ldg(irow + i);
-                    if (ci != ct) flags |= kFlagNonChannel;
-                    if ((unsigned)ci >= (unsigned)C) {
-                        flags |= kFlagIndexRange;
-                        c = 0;
-                    } else {
-                        c = ci;
+            int32_t cur[kPrefetch], icur[kPrefetch];
+            load_batch<kMode>(p, row0, last, 0, n, cur, icur);
+            for (int t0 = 0; t0 < n; t0 += kPrefetch) {
+                // the next batch's loads are in flight while this one is coded
+                int32_t nxt[kPrefetch], inxt[kPrefetch];
+                load_batch<kMode>(p, row0, last, t0 + kPrefetch, n, nxt, inxt);
+#pragma unroll
+                for (int u = 0; u < kPrefetch; ++u) {
+                    if (t0 + u < n) {
+                        int32_t s;
+                        if (kMode == kModeLatent) {
+                            // torch.round (half to even) then .int(), both in fp32
+                            s = __float2int_rz(rintf(__int_as_float(cur[u]) - __ldg(p.medians + ct)));
+                        } else {
+                            s = cur[u];
+                        }
+                        int c = ct;
+                        if (kIdx) {
+                            const int32_t ci = icur[u];
+                            if (ci != ct) flags |= kFlagNonChannel;
+                            if ((unsigned)ci >= (unsigned)C) {
+                                flags |= kFlagIndexRange;
+                                c = 0;
+                            } else {
+                                c = ci;
+                            }
+                        }
+                        const int2 ch = tab.chan(c);
+                        int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
+                        const int32_t maxv = ch.y;
+                        if (value < 0 || value >= maxv) {
+                            // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
+                            uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
+                                                     : ((uint32_t)value - (uint32_t)maxv) * 2u;
+                            put_escape(x, raw, w);
+                            value = maxv;
+                        }
+                        const uint32_t e = tab.entry(c, value, flags);
+                        put_symbol(x, e & 0xFFFFu, (e >> 16) + 1u, w);
+                        rem -= kLanes;
+                        while (rem < 0) {
+                            rem += p.HW;
+                            --ct;
+                        }
                     }
                 }
-                const int2 ch = tab.chan(c);
-                int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
-                const int32_t maxv = ch.y;
-                if (value < 0 || value >= maxv) {
-                    // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
-                    uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
-                                             : ((uint32_t)value - (uint32_t)maxv) * 2u;
-                    put_escape(x, raw, w);
-                    value = maxv;
-                }
-                const uint32_t e = tab.entry(c, value, flags);
-                put_symbol(x, e & 0xFFFFu, (e >> 16) + 1u, w);
-                i -= kLanes;
-                rem -= kLanes;
-                while (rem < 0) {
-                    rem += p.HW;
-                    --ct;
+#pragma unroll
+                for (int u = 0; u < kPrefetch; ++u) {
+                    cur[u] = nxt[u];
+                    icur[u] = inxt[u];
                 }
             }
             w.emit((uint32_t)(x >> 32));  // flush: decode order is low, high, ...
@@ -547,8 +579,9 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(PackParams p) {
         hdr[table_end / 4 + (threadIdx.x - 8)] = 0u;
     const int lane = threadIdx.x & 31;
     uint32_t *body = reinterpret_cast<uint32_t *>(p.packed + p.header_bytes);
-    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
+    const int warps = blockDim.x >> 5;
+    const int64_t warp_stride = (int64_t)gridDim.x * warps;
+    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
         const int rounds = p.rounds[chunk];
         int used = p.used[chunk * kLanes + lane];
         if (used > rows_cap) used = 0;  // overflowed staging: never packed by the host
@@ -616,14 +649,32 @@ struct DecParams {
     int32_t *__restrict__ out;
 };
 
+// The lane's words in decode order, read through a 4-deep look-ahead queue
+// so that a renormalisation never waits on a global load: consuming word k
+// issues the load of word k + 4.
 struct LaneReader {
     const uint32_t *__restrict__ base;  // chunk body + lane
-    int word, rounds;
+    int word, rounds;                   // index of the word q0 holds
     bool bad;
+    uint32_t q0, q1, q2, q3;
+    __device__ __forceinline__ uint32_t fetch(int j) const {
+        return j < rounds ? __ldg(base + (int64_t)j * kLanes) : 0u;
+    }
+    __device__ __forceinline__ void start() {
+        q0 = fetch(0);
+        q1 = fetch(1);
+        q2 = fetch(2);
+        q3 = fetch(3);
+    }
     __device__ __forceinline__ uint32_t next() {
-        if (word < rounds) return __ldg(base + (int64_t)(word++) * kLanes);
-        bad = true;
-        return 0u;
+        const uint32_t v = q0;
+        if (word >= rounds) bad = true;
+        q0 = q1;
+        q1 = q2;
+        q2 = q3;
+        q3 = fetch(word + 4);
+        ++word;
+        return v;
     }
 };
 
@@ -636,7 +687,7 @@ __device__ __forceinline__ uint32_t get_nibble(uint64_t &x, LaneReader &rd) {
 
 // Escape decode (warp_ans_kernel.cu:308-325).  Returns false on a corrupt
 // count (the format never needs more than 8 nibbles).
-__device__ __noinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
+__device__ __forceinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
     uint32_t v = get_nibble(x, rd);
     uint32_t n_bypass = v;
     while (v == kBypassMax && !rd.bad) {
@@ -677,8 +728,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
     Tables<kSmem> tab{s_tab, s_ch, s_lut, p.t};
     const int lane = threadIdx.x & 31;
     const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
-    const int64_t warp_stride = (int64_t)gridDim.x * kWarps;
-    for (int64_t chunk = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); !skip && chunk < p.chunks;
+    const int warps = blockDim.x >> 5;
+    const int64_t warp_stride = (int64_t)gridDim.x * warps;
+    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); !skip && chunk < p.chunks;
          chunk += warp_stride) {
         const int b = (int)(chunk / p.K);
         const int k = (int)(chunk - (int64_t)b * p.K);
@@ -688,43 +740,58 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
         const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
         const int first = start + lane;
         if (first >= end) continue;
-        LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false};
+        LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u};
+        rd.start();
         uint64_t x = (uint64_t)rd.next();
         x |= (uint64_t)rd.next() << 32;
         const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
         int32_t *orow = kMode == kModeLatent ? nullptr : p.out + (int64_t)b * p.N;
         float *yrow = kMode == kModeLatent ? p.y_out + (int64_t)b * p.N : nullptr;
         int ct = first / p.HW, rem = first - ct * p.HW;
-        for (int i = first; i < end; i += kLanes) {
-            int c = ct;
-            if (kIdx) {
-                const int32_t ci = __ldg(irow + i);
-                if (ci != ct) flags |= kFlagNonChannel;
-                if ((unsigned)ci >= (unsigned)C) {
-                    flags |= kFlagIndexRange;
-                    c = 0;
-                } else {
-                    c = ci;
+        const int n = (end - 1 - first) / kLanes + 1;
+        int32_t icur[kPrefetch], inxt[kPrefetch];
+#pragma unroll
+        for (int u = 0; u < kPrefetch; ++u) icur[u] = (kIdx && u < n) ? __ldg(irow + first + u * kLanes) : 0;
+        for (int t0 = 0; t0 < n && !rd.bad; t0 += kPrefetch) {
+#pragma unroll
+            for (int u = 0; u < kPrefetch; ++u)  // next batch of indexes in flight
+                inxt[u] = (kIdx && t0 + kPrefetch + u < n) ? __ldg(irow + first + (t0 + kPrefetch + u) * kLanes) : 0;
+#pragma unroll
+            for (int u = 0; u < kPrefetch; ++u) {
+                if (t0 + u < n && !rd.bad) {
+                    const int i = first + (t0 + u) * kLanes;
+                    int c = ct;
+                    if (kIdx) {
+                        const int32_t ci = icur[u];
+                        if (ci != ct) flags |= kFlagNonChannel;
+                        if ((unsigned)ci >= (unsigned)C) {
+                            flags |= kFlagIndexRange;
+                            c = 0;
+                        } else {
+                            c = ci;
+                        }
+                    }
+                    const int2 ch = tab.chan(c);
+                    const uint32_t slot = (uint32_t)x & 0xFFFFu;
+                    uint32_t e;
+                    int32_t value = tab.search(c, ch.y, slot, e, flags);
+                    x = (uint64_t)((e >> 16) + 1u) * (x >> 16) + (uint64_t)slot - (uint64_t)(e & 0xFFFFu);
+                    if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
+                    if (value == ch.y && !get_escape(x, rd, ch.y, value)) rd.bad = true;
+                    if (!rd.bad) {
+                        const int32_t sym = (int32_t)((uint32_t)value + (uint32_t)ch.x);
+                        if (kMode == kModeLatent) yrow[i] = __int2float_rn(sym) + __ldg(p.medians + c);
+                        else orow[i] = sym;
+                    }
+                    rem += kLanes;
+                    while (rem >= p.HW) {
+                        rem -= p.HW;
+                        ++ct;
+                    }
                 }
             }
-            const int2 ch = tab.chan(c);
-            const uint32_t slot = (uint32_t)x & 0xFFFFu;
-            uint32_t e;
-            int32_t value = tab.search(c, ch.y, slot, e, flags);
-            x = (uint64_t)((e >> 16) + 1u) * (x >> 16) + (uint64_t)slot - (uint64_t)(e & 0xFFFFu);
-            if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
-            if (value == ch.y && !get_escape(x, rd, ch.y, value)) {
-                rd.bad = true;
-                break;
-            }
-            const int32_t sym = (int32_t)((uint32_t)value + (uint32_t)ch.x);
-            if (kMode == kModeLatent) yrow[i] = __int2float_rn(sym) + __ldg(p.medians + c);
-            else orow[i] = sym;
-            rem += kLanes;
-            while (rem >= p.HW) {
-                rem -= p.HW;
-                ++ct;
-            }
+#pragma unroll
+            for (int u = 0; u < kPrefetch; ++u) icur[u] = inxt[u];
         }
         if (rd.bad) flags |= kFlagCorrupt;
     }
@@ -808,14 +875,24 @@ struct LaunchCache {
     int dev;
     int64_t smem_optin;
     int64_t smem_last;
+    int warps_last;
     int occ_last;
 };
 static std::mutex g_launch_mutex;
 static LaunchCache g_launch[64];
 static int g_launch_n = 0;
 
+// Warps per CTA: 8, unless there are too few chunks to give every SM two
+// CTAs' worth, in which case smaller CTAs spread the chunks over more SMs.
+static int warps_for(int64_t chunks) {
+    const int64_t sms = fcai::sm_count();
+    int w = kWarps;
+    while (w > 1 && chunks < (int64_t)w * sms * 2) w >>= 1;
+    return w;
+}
+
 template <typename K>
-static int grid_for(K kernel, int64_t smem, int64_t chunks, int &grid) {
+static int grid_for(K kernel, int64_t smem, int64_t chunks, int warps, int &grid) {
     int dev = 0;
     FCAI_CUDA_TRY(cudaGetDevice(&dev));
     int occ = 0;
@@ -826,24 +903,25 @@ static int grid_for(K kernel, int64_t smem, int64_t chunks, int &grid) {
             if (g_launch[i].fn == (const void *)kernel && g_launch[i].dev == dev) e = &g_launch[i];
         if (!e && g_launch_n < 64) {
             e = &g_launch[g_launch_n++];
-            *e = LaunchCache{(const void *)kernel, dev, 48 * 1024, -1, 0};
+            *e = LaunchCache{(const void *)kernel, dev, 48 * 1024, -1, 0, 0};
         }
-        if (e && e->smem_last == smem) {
+        if (e && e->smem_last == smem && e->warps_last == warps) {
             occ = e->occ_last;
         } else {
             if (smem > (e ? e->smem_optin : 48 * 1024)) {
                 FCAI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
                 if (e) e->smem_optin = smem;
             }
-            FCAI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, (size_t)smem));
+            FCAI_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, warps * kLanes, (size_t)smem));
             if (e) {
                 e->smem_last = smem;
+                e->warps_last = warps;
                 e->occ_last = occ;
             }
         }
     }
     if (occ < 1) occ = 1;
-    int64_t want = (chunks + kWarps - 1) / kWarps;
+    int64_t want = (chunks + warps - 1) / warps;
     int64_t cap = (int64_t)fcai::sm_count() * occ;
     grid = (int)(want < cap ? want : cap);
     if (grid < 1) grid = 1;
@@ -853,8 +931,9 @@ static int grid_for(K kernel, int64_t smem, int64_t chunks, int &grid) {
 template <int kMode, bool kSmem>
 static int launch_encode(const EncParams &p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
-    if ((rc = grid_for(encode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, grid))) return rc;
-    encode_kernel<kMode, kSmem><<<grid, kThreads, kSmem ? smem : 0, stream>>>(p);
+    const int warps = warps_for(p.chunks);
+    if ((rc = grid_for(encode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, warps, grid))) return rc;
+    encode_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
@@ -862,8 +941,9 @@ static int launch_encode(const EncParams &p, int64_t smem, cudaStream_t stream) 
 template <int kMode, bool kSmem>
 static int launch_decode(const DecParams &p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
-    if ((rc = grid_for(decode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, grid))) return rc;
-    decode_kernel<kMode, kSmem><<<grid, kThreads, kSmem ? smem : 0, stream>>>(p);
+    const int warps = warps_for(p.chunks);
+    if ((rc = grid_for(decode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, warps, grid))) return rc;
+    decode_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
