@@ -23,8 +23,9 @@ LIB = LIB_DIR / "libfcai_b200.so"
 
 SOURCES = [
     "warp_div.cu",
+    "conv_tc.cu",
 ]
-HEADERS = ["fcai_common.h"]
+HEADERS = ["fcai_common.h", "tc_ptx.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr"]
 

@@ -1,0 +1,755 @@
+// conv_tc.cu -- FactorizedPrior transform layers as tcgen05 implicit GEMMs
+// (sm_100a) and the C ABI of include/fcai_transforms.h.
+//
+// GEMM view of one layer: rows = output pixels (tiles of 128), columns =
+// output channels (npad <= 256, one tile), K = taps x input channels.
+//   * 5x5 stride-2 convolution: K runs over the 25 taps; for tap (ky, kx) and
+//     a 64-channel block the A tile is one TMA load of an NHWC box whose
+//     x/y element strides are 2, starting at (2*ox0 + kx - 2, 2*oy0 + ky - 2);
+//     the zero padding is the TMA out-of-bounds fill.
+//   * 5x5 stride-2 transposed convolution (padding 2, output padding 1): the
+//     output splits into 4 phases (oy % 2, ox % 2); phase (py, px) is a
+//     stride-1 convolution of the input with the taps ky = py (mod 2),
+//     kx = px (mod 2), input offset ((py + 2 - ky) / 2, (px + 2 - kx) / 2).
+//     Each phase is its own set of tiles, so no output pixel is written twice.
+//   * the first analysis layer (3 input channels, fp32 NCHW image) builds
+//     its A tile (K = 75 padded to 80) with four gather warps instead of TMA.
+// The B tile (weights) is a TMA box of the packed [25][npad][cin] tensor.
+//
+// CTA organisation (persistent, one CTA per SM):
+//   warps 0-3   epilogue: TMEM -> registers, bias, GDN/IGDN, store
+//   warp 4      TMA producer (one lane)
+//   warp 5      MMA issuer (one lane); owns the TMEM allocation
+//   warps 6-9   gather producers (first analysis layer only)
+// A 4-stage shared-memory ring (mbarrier full/empty pairs) feeds the MMAs;
+// two TMEM accumulator buffers let the epilogue of tile j overlap the main
+// loop of tile j + 1.
+//
+// GDN fusion: the epilogue writes x^2 (bf16) of its 128 x 128 tile into
+// shared memory in the MMA operand layout and issues a second GEMM
+// x^2 @ gamma^T into TMEM; then y = x * rsqrt(beta + norm) (x * sqrt(...)
+// for IGDN) is formed from the two accumulators and stored.
+//
+// Every mbarrier wait is bounded (1 s of %globaltimer); on a timeout the
+// CTA records an error code, raises a shared abort flag so the other roles
+// stop, drains its MMAs and frees its TMEM before returning.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/fcai_transforms.h"
+#include "fcai_common.h"
+#include "tc_ptx.h"
+
+namespace ct {
+using namespace tcx;
+
+constexpr int kBM = 128;          // output pixels per tile (MMA M)
+constexpr int kBK = 64;           // bf16 per K block: one 128-byte row
+constexpr int kStages = 4;
+constexpr int kEpiThreads = 128;  // warps 0-3
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kGatherThread0 = 192;  // warps 6-9
+constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
+constexpr uint64_t kWaitNs = 1000000000ull;
+
+enum Epi : int { kEpiBf16 = 0, kEpiGdn = 1, kEpiIgdn = 2, kEpiF32 = 3, kEpiF32Clamp = 4 };
+
+enum Err : int { kErrProducer = 1, kErrMma = 2, kErrEpilogue = 4, kErrGather = 8 };
+
+struct Taps {
+    int n;
+    int8_t dy[25], dx[25];
+    uint8_t w[25];
+};
+
+struct ConvParams {
+    int B, phases, tiles_x, tiles_y, TY, TX, GH, GW;  // per-phase GEMM pixel grid
+    int stride;                                       // input step per GEMM pixel (2 conv, 1 deconv)
+    int cin, cout, cin_blocks;
+    int Hout, Wout, out_step;                         // output tensor size, output step per GEMM pixel
+    int Hin, Win;
+    int tiles_total;
+    uint32_t tmem_cols, buf_stride;
+    Taps taps[4];
+    const float *bias;
+    const float *beta;
+    const float *x_in;   // first layer: fp32 NCHW [B, 3, Hin, Win]
+    const void *wgather; // first layer: packed weight image
+    void *out;
+    int *err;
+};
+
+template <int kNpad, int kEpi, bool kGather>
+struct Layout {
+    static constexpr bool kNorm = kEpi == kEpiGdn || kEpi == kEpiIgdn;
+    static constexpr int kA = kGather ? kBM * kGatherK * 2 : kBM * kBK * 2;
+    static constexpr int kB = kGather ? 0 : kNpad * kBK * 2;
+    static constexpr int kStage = kA + kB;
+    static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
+    static constexpr int kG = kNorm ? kNpad * kNpad * 2 : 0;
+    static constexpr int kX2 = kNorm ? kBM * kNpad * 2 : 0;
+    static constexpr int offW = kStages * kStage;
+    static constexpr int offG = offW + kW;
+    static constexpr int offX2 = offG + kG;
+    static constexpr int offBias = offX2 + kX2;
+    static constexpr int offBeta = offBias + kNpad * 4;
+    static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
+    static constexpr int kBars = 2 * kStages + 7;
+    static constexpr int offSlot = offBar + kBars * 8;
+    static constexpr int kBytes = offSlot + 32;
+    static constexpr int kAlloc = kBytes + 1024;  // base alignment slack
+    static constexpr int kThreads = kGather ? 320 : 192;
+    static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
+    static_assert(kB % 1024 == 0, "B stage alignment");
+    static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
+    static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
+};
+
+__device__ __forceinline__ void tile_coords(const ConvParams &p, int tile, int &b, int &ph, int &gy0, int &gx0) {
+    const int tx = tile % p.tiles_x;
+    int rest = tile / p.tiles_x;
+    const int ty = rest % p.tiles_y;
+    rest /= p.tiles_y;
+    ph = rest % p.phases;
+    b = rest / p.phases;
+    gy0 = ty * p.TY;
+    gx0 = tx * p.TX;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ void fail(const ConvParams &p, volatile int *abort, int code) {
+    *abort = 1;
+    if (p.err) atomicOr(p.err, code);
+}
+
+template <int kNpad, int kEpi, bool kGather>
+__global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmG, const ConvParams p) {
+    using Lay = Layout<kNpad, kEpi, kGather>;
+    constexpr bool kNorm = Lay::kNorm;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lay::offBar);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + kStages;
+    uint64_t *accf = bars + 2 * kStages;
+    uint64_t *acce = accf + 2;
+    uint64_t *g2bar = acce + 2;
+    uint64_t *cbar = g2bar + 1;
+    uint64_t *dbar = cbar + 1;  // abort path: drains this CTA's MMAs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::offSlot);
+    volatile int *abort = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 4);
+    volatile int *epi_ok = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 8);
+    float *s_bias = reinterpret_cast<float *>(smem + Lay::offBias);
+    float *s_beta = reinterpret_cast<float *>(smem + Lay::offBeta);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], kGather ? kEpiThreads : 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], kEpiThreads);
+        }
+        mbar_init(g2bar, 1);
+        mbar_init(cbar, 1);
+        mbar_init(dbar, 2);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    for (int i = threadIdx.x; i < kNpad; i += blockDim.x) {
+        s_bias[i] = i < p.cout ? p.bias[i] : 0.f;
+        if (kNorm) s_beta[i] = i < p.cout ? p.beta[i] : 1.f;
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_slot, p.tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == kProducerWarp) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            if (!kGather) {
+                tma_prefetch_desc(&tmA);
+                tma_prefetch_desc(&tmW);
+            }
+            // one-time operands: gamma (GDN) and the first layer's weights
+            uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
+            if (cbytes) {
+                mbar_arrive_expect_tx(cbar, cbytes);
+                if (kNorm) {
+                    tma_load_3d(smem + Lay::offG, &tmG, cbar, 0, 0, 0);
+                    tma_load_3d(smem + Lay::offG + Lay::kG / 2, &tmG, cbar, kBK, 0, 0);
+                }
+                if (kGather) bulk_load(smem + Lay::offW, p.wgather, Lay::kW, cbar);
+            }
+            if (!kGather) {
+                uint32_t it = 0;
+                int last_round[kStages];
+                for (int s = 0; s < kStages; ++s) last_round[s] = -1;
+                for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x) {
+                    int b, ph, gy0, gx0;
+                    tile_coords(p, tile, b, ph, gy0, gx0);
+                    const Taps &tp = p.taps[ph];
+                    for (int t = 0; t < tp.n && !*abort; ++t) {
+                        const int ix = gx0 * p.stride + tp.dx[t];
+                        const int iy = gy0 * p.stride + tp.dy[t];
+                        for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
+                            const int s = it % kStages;
+                            const uint32_t r = it / kStages;
+                            if (!mbar_wait(&empty[s], (r & 1) ^ 1, abort, kWaitNs)) {
+                                fail(p, abort, kErrProducer);
+                                break;
+                            }
+                            unsigned char *st = smem + s * Lay::kStage;
+                            mbar_arrive_expect_tx(&full[s], Lay::kStage);
+                            tma_load_4d(st, &tmA, &full[s], cb * kBK, ix, iy, b);
+                            tma_load_3d(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
+                            last_round[s] = (int)r;
+                        }
+                    }
+                }
+                if (*abort) {
+                    // let this CTA's loads in flight land before the CTA exits
+                    for (int s = 0; s < kStages; ++s)
+                        if (last_round[s] >= 0) mbar_wait(&full[s], (uint32_t)last_round[s] & 1, nullptr, kWaitNs / 10);
+                }
+            }
+            if (cbytes && *abort) mbar_wait(cbar, 0, nullptr, kWaitNs / 10);
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16(kBM, kNpad);
+            bool consts = !kGather;
+            uint32_t it = 0;
+            int j = 0;
+            for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++j) {
+                if (!consts) {
+                    if (!mbar_wait(cbar, 0, abort, kWaitNs)) {
+                        fail(p, abort, kErrMma);
+                        break;
+                    }
+                    consts = true;
+                }
+                int b, ph, gy0, gx0;
+                tile_coords(p, tile, b, ph, gy0, gx0);
+                const int buf = j & 1;
+                const uint32_t use = j >> 1;
+                if (!mbar_wait(&acce[buf], (use & 1) ^ 1, abort, kWaitNs)) {
+                    fail(p, abort, kErrMma);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + buf * p.buf_stride;
+                const int ksteps = kGather ? 1 : p.taps[ph].n * p.cin_blocks;
+                bool ok = true;
+                for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                    const int s = it % kStages;
+                    const uint32_t r = it / kStages;
+                    if (!mbar_wait(&full[s], r & 1, abort, kWaitNs)) {
+                        fail(p, abort, kErrMma);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(smem + s * Lay::kStage);
+                    if (kGather) {
+                        const uint32_t w0 = smem_u32(smem + Lay::offW);
+#pragma unroll
+                        for (int kk = 0; kk < kGatherK / 16; ++kk)
+                            mma_bf16(d, smem_desc(a0 + kk * 256, 128, 1280, 0), smem_desc(w0 + kk * 256, 128, 1280, 0),
+                                     idesc, kk != 0);
+                    } else {
+                        const uint32_t b0 = a0 + Lay::kA;
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk)
+                            mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
+                                     idesc, (ks | kk) != 0);
+                    }
+                    mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                }
+                if (!ok) break;
+                mma_commit(&accf[buf]);
+            }
+        }
+    } else if (warp < 4) {
+        // ------------------------------------------------------------ epilogue
+        // Thread 0 alone waits on the mbarriers and publishes the outcome in
+        // epi_ok; all 128 threads then meet at named barrier 1, so the group
+        // always takes the same branch and no thread waits at a barrier the
+        // others have left.
+        const int m = threadIdx.x;  // TMEM lane = tile row = output pixel
+        const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+        bool consts = !kNorm;
+        int j = 0;
+        for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++j) {
+            int b, ph, gy0, gx0;
+            tile_coords(p, tile, b, ph, gy0, gx0);
+            const int buf = j & 1;
+            const uint32_t use = j >> 1;
+            if (m == 0) {
+                bool ok = !*abort;
+                if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
+                if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
+                if (!ok) fail(p, abort, kErrEpilogue);
+                *epi_ok = ok ? 1 : 0;
+            }
+            named_barrier_sync(1, kEpiThreads);
+            if (!*epi_ok) break;
+            consts = true;
+            tc_fence_after();
+            const int gy = gy0 + m / p.TX, gx = gx0 + m % p.TX;
+            const bool valid = gy < p.GH && gx < p.GW;
+            const int oy = gy * p.out_step + (p.phases == 4 ? (ph >> 1) : 0);
+            const int ox = gx * p.out_step + (p.phases == 4 ? (ph & 1) : 0);
+            const uint32_t d1 = tmem_base + buf * p.buf_stride + lane_addr;
+            if (kNorm) {
+                // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile
+                const uint32_t x2 = smem_u32(smem + Lay::offX2);
+#pragma unroll 1
+                for (int cc = 0; cc < kNpad / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld32(d1 + cc * 32, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int c = cc * 32 + q * 8 + e * 2;
+                            const float a = __uint_as_float(v[q * 8 + e * 2]) + s_bias[c];
+                            const float bb = __uint_as_float(v[q * 8 + e * 2 + 1]) + s_bias[c + 1];
+                            w[e] = pack_bf16x2(a * a, bb * bb);
+                        }
+                        const int k0 = cc * 32 + q * 8;
+                        const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                        st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
+                                     w[3]);
+                    }
+                }
+                fence_proxy_async_smem();
+                named_barrier_sync(1, kEpiThreads);
+                if (m == 0) {
+                    tc_fence_after();
+                    const uint32_t g0 = smem_u32(smem + Lay::offG);
+                    const uint32_t d2 = tmem_base + buf * p.buf_stride + kNpad;
+                    const uint32_t idesc = idesc_bf16(kBM, kNpad);
+#pragma unroll
+                    for (int kk = 0; kk < kNpad / 16; ++kk) {
+                        const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
+                        const uint32_t goff = (kk / 4) * (kNpad * 128) + (kk % 4) * 32;
+                        mma_bf16(d2, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc,
+                                 kk != 0);
+                    }
+                    mma_commit(g2bar);
+                    const bool ok = mbar_wait(g2bar, j & 1, abort, kWaitNs);
+                    if (!ok) fail(p, abort, kErrEpilogue);
+                    *epi_ok = ok ? 1 : 0;
+                }
+                named_barrier_sync(1, kEpiThreads);
+                if (!*epi_ok) break;
+                tc_fence_after();
+                // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm))
+                __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
+                                      (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
+#pragma unroll 1
+                for (int cc = 0; cc < kNpad / 32; ++cc) {
+                    uint32_t v[32], nv[32];
+                    tmem_ld32(d1 + cc * 32, v);
+                    tmem_ld32(d1 + kNpad + cc * 32, nv);
+                    tmem_wait_ld();
+                    uint32_t o[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int c = cc * 32 + 2 * e;
+                        float r0 = rsqrtf(__uint_as_float(nv[2 * e]) + s_beta[c]);
+                        float r1 = rsqrtf(__uint_as_float(nv[2 * e + 1]) + s_beta[c + 1]);
+                        if (kEpi == kEpiIgdn) {
+                            r0 = (__uint_as_float(nv[2 * e]) + s_beta[c]) * r0;
+                            r1 = (__uint_as_float(nv[2 * e + 1]) + s_beta[c + 1]) * r1;
+                        }
+                        const float x0 = __uint_as_float(v[2 * e]) + s_bias[c];
+                        const float x1 = __uint_as_float(v[2 * e + 1]) + s_bias[c + 1];
+                        o[e] = pack_bf16x2(x0 * r0, x1 * r1);
+                    }
+                    if (valid) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 32);
+                        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                        dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
+                        dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
+                    }
+                }
+            } else if (kEpi == kEpiBf16) {
+                __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
+                                      (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
+#pragma unroll 1
+                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                    uint32_t v[16];
+                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_wait_ld();
+                    uint32_t o[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]) + s_bias[cc * 16 + 2 * e],
+                                           __uint_as_float(v[2 * e + 1]) + s_bias[cc * 16 + 2 * e + 1]);
+                    if (valid) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 16);
+                        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+            } else {
+                // fp32 NCHW: per channel the warp's 32 pixels are contiguous in x
+                float *out = reinterpret_cast<float *>(p.out);
+                const int64_t plane = (int64_t)p.Hout * p.Wout;
+                const int64_t pix = (int64_t)oy * p.Wout + ox;
+#pragma unroll 1
+                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                    uint32_t v[16];
+                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int c = cc * 16 + e;
+                        float y = __uint_as_float(v[e]) + s_bias[c];
+                        if (kEpi == kEpiF32Clamp) y = fminf(fmaxf(y, 0.f), 1.f);
+                        if (valid && c < p.cout) out[((int64_t)b * p.cout + c) * plane + pix] = y;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acce[buf]);
+            // the next tile's epi_ok must not be written before every thread read this one
+            named_barrier_sync(1, kEpiThreads);
+        }
+    } else if (kGather) {
+        // ------------------------------------------------------------ gather (first layer)
+        const int m = threadIdx.x - kGatherThread0;
+        const uint32_t row_off = (m & 7) * 16 + (m >> 3) * 1280;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
+            int b, ph, gy0, gx0;
+            tile_coords(p, tile, b, ph, gy0, gx0);
+            const int s = it % kStages;
+            const uint32_t r = it / kStages;
+            if (!mbar_wait(&empty[s], (r & 1) ^ 1, abort, kWaitNs)) {
+                fail(p, abort, kErrGather);
+                break;
+            }
+            const int gy = gy0 + m / p.TX, gx = gx0 + m % p.TX;
+            const bool valid = gy < p.GH && gx < p.GW;
+            const float *img = p.x_in + (int64_t)b * 3 * p.Hin * p.Win;
+            const uint32_t a0 = smem_u32(smem + s * Lay::kStage) + row_off;
+#pragma unroll
+            for (int kc = 0; kc < kGatherK / 8; ++kc) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int k = kc * 8 + e;
+                    f[e] = 0.f;
+                    if (k < 75) {
+                        const int ci = k / 25, ky = (k % 25) / 5, kx = k % 5;
+                        const int iy = 2 * gy + ky - 2, ix = 2 * gx + kx - 2;
+                        if (valid && iy >= 0 && iy < p.Hin && ix >= 0 && ix < p.Win)
+                            f[e] = __ldg(img + ((int64_t)ci * p.Hin + iy) * p.Win + ix);
+                    }
+                }
+                st_shared_v4(a0 + kc * 128, pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                             pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&full[s]);
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    __syncthreads();
+    if (*abort) {
+        // the two threads that issue MMAs (MMA lane, epilogue thread 0) commit
+        // to dbar; TMEM is freed only once everything they issued completed
+        if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0) mma_commit(dbar);
+        if (warp == kMmaWarp && lane == 0) mbar_wait(dbar, 0, nullptr, kWaitNs / 10);
+        __syncthreads();
+    }
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, p.tmem_cols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+static int make_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+                    const cuuint32_t *box, const cuuint32_t *estrides) {
+    auto fn = encode_fn();
+    if (!fn) return fcai::fail(FCAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(base), dims, strides, box, estrides,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fcai::fail(FCAI_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return FCAI_OK;
+}
+
+// Largest power-of-two tile width (<= 128) that wastes the fewest columns.
+static int pick_tx(int gw) {
+    int best = 8, waste_best = 1 << 30;
+    for (int tx = 8; tx <= 128; tx <<= 1) {
+        int waste = ((gw + tx - 1) / tx) * tx - gw;
+        if (waste < waste_best || (waste == waste_best && tx > best)) {
+            best = tx;
+            waste_best = waste;
+        }
+    }
+    return best;
+}
+
+template <int kNpad, int kEpi, bool kGather>
+static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const ConvParams &p,
+                  cudaStream_t stream) {
+    using Lay = Layout<kNpad, kEpi, kGather>;
+    auto kernel = conv_tc_kernel<kNpad, kEpi, kGather>;
+    static int configured[64] = {0};
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        FCAI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc));
+        configured[dev] = 1;
+    }
+    int grid = p.tiles_total < fcai::sm_count() ? p.tiles_total : fcai::sm_count();
+    kernel<<<grid, Lay::kThreads, Lay::kAlloc, stream>>>(a, w, g, p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+static int dispatch(int npad, int epi, bool gather, const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g,
+                    const ConvParams &p, cudaStream_t stream) {
+    if (gather) {
+        if (npad == 128 && epi == kEpiGdn) return launch<128, kEpiGdn, true>(a, w, g, p, stream);
+        return fcai::fail(FCAI_ERR_INVALID, "first-layer kernel is built for 128 channels with GDN");
+    }
+    switch (npad) {
+        case 128:
+            switch (epi) {
+                case kEpiBf16: return launch<128, kEpiBf16, false>(a, w, g, p, stream);
+                case kEpiGdn: return launch<128, kEpiGdn, false>(a, w, g, p, stream);
+                case kEpiIgdn: return launch<128, kEpiIgdn, false>(a, w, g, p, stream);
+                case kEpiF32: return launch<128, kEpiF32, false>(a, w, g, p, stream);
+                default: break;
+            }
+            break;
+        case 192:
+            if (epi == kEpiF32) return launch<192, kEpiF32, false>(a, w, g, p, stream);
+            if (epi == kEpiBf16) return launch<192, kEpiBf16, false>(a, w, g, p, stream);
+            break;
+        case 16:
+            if (epi == kEpiF32Clamp) return launch<16, kEpiF32Clamp, false>(a, w, g, p, stream);
+            if (epi == kEpiF32) return launch<16, kEpiF32, false>(a, w, g, p, stream);
+            break;
+        default:
+            break;
+    }
+    return fcai::fail(FCAI_ERR_INVALID, "no kernel instance for npad=%d epilogue=%d", npad, epi);
+}
+
+__global__ void nchw_to_nhwc_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out, int C, int HW,
+                                    int64_t total_pix) {
+    // one thread per (pixel, 8-channel group): reads are strided by HW per
+    // channel but coalesced across neighbouring pixels, writes are 16 bytes
+    const int groups = C / 8;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= total_pix * groups) return;
+    const int g = (int)(idx / total_pix);
+    const int64_t pix = idx - (int64_t)g * total_pix;
+    const int64_t b = pix / HW, hw = pix - b * HW;
+    const float *src = in + (b * C + g * 8) * HW + hw;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) w[e] = pack_bf16x2(__ldg(src + (2 * e) * (int64_t)HW), __ldg(src + (2 * e + 1) * (int64_t)HW));
+    *reinterpret_cast<uint4 *>(out + pix * C + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+}  // namespace ct
+
+using namespace ct;
+
+extern "C" {
+
+int fcai_layer_out_size(const fcai_layer *L, int32_t h_in, int32_t w_in, int32_t *h_out, int32_t *w_out) {
+    if (!L || !h_out || !w_out || h_in <= 0 || w_in <= 0) return fcai::fail(FCAI_ERR_INVALID, "invalid layer size query");
+    if (L->kind == FCAI_LAYER_CONV5S2) {
+        *h_out = (h_in + 4 - 5) / 2 + 1;
+        *w_out = (w_in + 4 - 5) / 2 + 1;
+    } else if (L->kind == FCAI_LAYER_DECONV5S2) {
+        *h_out = 2 * h_in;
+        *w_out = 2 * w_in;
+    } else {
+        return fcai::fail(FCAI_ERR_INVALID, "unknown layer kind %d", L->kind);
+    }
+    return FCAI_OK;
+}
+
+int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t w_in, const void *input, void *output,
+                       int32_t *err, fcai_stream_t stream_) {
+    fcai::clear_error();
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!L || !input || !output || !L->weight || !L->bias) return fcai::fail(FCAI_ERR_INVALID, "null layer argument");
+    int32_t ho, wo;
+    int rc = fcai_layer_out_size(L, h_in, w_in, &ho, &wo);
+    if (rc) return rc;
+    if (batch <= 0 || batch > 65535) return fcai::fail(FCAI_ERR_INVALID, "batch out of range");
+    const bool gather = L->in_format == FCAI_FMT_NCHW_F32;
+    const bool deconv = L->kind == FCAI_LAYER_DECONV5S2;
+    const int npad = L->npad;
+    if (npad < L->cout || npad % 16 || npad > 256) return fcai::fail(FCAI_ERR_INVALID, "npad must round cout up to 16");
+    if (gather && (deconv || L->cin != 3)) return fcai::fail(FCAI_ERR_INVALID, "fp32 NCHW input only for the cin=3 conv");
+    if (!gather && L->cin % 64) return fcai::fail(FCAI_ERR_INVALID, "cin must be a multiple of 64");
+    const bool norm = L->epilogue == FCAI_EPI_GDN || L->epilogue == FCAI_EPI_IGDN;
+    if (norm && (!L->gdn_beta || !L->gdn_gamma || L->out_format != FCAI_FMT_NHWC_BF16))
+        return fcai::fail(FCAI_ERR_INVALID, "GDN epilogue needs beta, gamma and a bf16 NHWC output");
+    int epi;
+    if (L->epilogue == FCAI_EPI_GDN) epi = kEpiGdn;
+    else if (L->epilogue == FCAI_EPI_IGDN) epi = kEpiIgdn;
+    else if (L->out_format == FCAI_FMT_NHWC_BF16) epi = kEpiBf16;
+    else epi = L->clamp01 ? kEpiF32Clamp : kEpiF32;
+
+    ConvParams p{};
+    p.B = batch;
+    p.phases = deconv ? 4 : 1;
+    p.GH = deconv ? h_in : ho;
+    p.GW = deconv ? w_in : wo;
+    p.TX = pick_tx(p.GW);
+    p.TY = kBM / p.TX;
+    p.tiles_x = (p.GW + p.TX - 1) / p.TX;
+    p.tiles_y = (p.GH + p.TY - 1) / p.TY;
+    p.stride = deconv ? 1 : 2;
+    p.cin = L->cin;
+    p.cout = L->cout;
+    p.cin_blocks = gather ? 1 : L->cin / kBK;
+    p.Hout = ho;
+    p.Wout = wo;
+    p.out_step = deconv ? 2 : 1;
+    p.Hin = h_in;
+    p.Win = w_in;
+    const int64_t tiles = (int64_t)batch * p.phases * p.tiles_x * p.tiles_y;
+    if (tiles > INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "too many tiles");
+    p.tiles_total = (int)tiles;
+    const int per_buf = npad + (norm ? npad : 0);
+    uint32_t stride = 32;
+    while (stride < (uint32_t)per_buf) stride <<= 1;
+    p.buf_stride = stride;
+    p.tmem_cols = 2 * stride;
+    if (p.tmem_cols > 512) return fcai::fail(FCAI_ERR_INVALID, "accumulators exceed tensor memory");
+    if (deconv) {
+        for (int ph = 0; ph < 4; ++ph) {
+            const int py = ph >> 1, px = ph & 1;
+            int n = 0;
+            for (int ky = py; ky < 5; ky += 2)
+                for (int kx = px; kx < 5; kx += 2) {
+                    p.taps[ph].dy[n] = (int8_t)((py + 2 - ky) / 2);
+                    p.taps[ph].dx[n] = (int8_t)((px + 2 - kx) / 2);
+                    p.taps[ph].w[n] = (uint8_t)(ky * 5 + kx);
+                    ++n;
+                }
+            p.taps[ph].n = n;
+        }
+    } else {
+        int n = 0;
+        for (int ky = 0; ky < 5; ++ky)
+            for (int kx = 0; kx < 5; ++kx) {
+                p.taps[0].dy[n] = (int8_t)(ky - 2);
+                p.taps[0].dx[n] = (int8_t)(kx - 2);
+                p.taps[0].w[n] = (uint8_t)(ky * 5 + kx);
+                ++n;
+            }
+        p.taps[0].n = n;
+    }
+    p.bias = L->bias;
+    p.beta = L->gdn_beta;
+    p.x_in = gather ? static_cast<const float *>(input) : nullptr;
+    p.wgather = gather ? L->weight : nullptr;
+    p.out = output;
+    p.err = err;
+
+    CUtensorMap ma{}, mw{}, mg{};
+    if (!gather) {
+        const int s = p.stride;
+        cuuint64_t dims[4] = {(cuuint64_t)L->cin, (cuuint64_t)w_in, (cuuint64_t)h_in, (cuuint64_t)batch};
+        cuuint64_t strides[3] = {(cuuint64_t)L->cin * 2, (cuuint64_t)w_in * L->cin * 2,
+                                 (cuuint64_t)h_in * w_in * L->cin * 2};
+        cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)(p.TX * s), (cuuint32_t)(p.TY * s), 1};
+        cuuint32_t es[4] = {1, (cuuint32_t)s, (cuuint32_t)s, 1};
+        if ((rc = make_map(&ma, input, 4, dims, strides, box, es))) return rc;
+        cuuint64_t wd[3] = {(cuuint64_t)L->cin, (cuuint64_t)npad, 25};
+        cuuint64_t ws[2] = {(cuuint64_t)L->cin * 2, (cuuint64_t)npad * L->cin * 2};
+        cuuint32_t wb[3] = {(cuuint32_t)kBK, (cuuint32_t)npad, 1};
+        cuuint32_t we[3] = {1, 1, 1};
+        if ((rc = make_map(&mw, L->weight, 3, wd, ws, wb, we))) return rc;
+    }
+    if (norm) {
+        cuuint64_t gd[3] = {(cuuint64_t)npad, (cuuint64_t)npad, 1};
+        cuuint64_t gs[2] = {(cuuint64_t)npad * 2, (cuuint64_t)npad * npad * 2};
+        cuuint32_t gb[3] = {(cuuint32_t)kBK, (cuuint32_t)npad, 1};
+        cuuint32_t ge[3] = {1, 1, 1};
+        if ((rc = make_map(&mg, L->gdn_gamma, 3, gd, gs, gb, ge))) return rc;
+    }
+    return dispatch(npad, epi, gather, ma, mw, mg, p, stream);
+}
+
+int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h, int32_t w,
+                               fcai_stream_t stream_) {
+    fcai::clear_error();
+    if (!input || !output || batch <= 0 || channels <= 0 || channels % 8 || h <= 0 || w <= 0)
+        return fcai::fail(FCAI_ERR_INVALID, "invalid layout conversion arguments");
+    const int64_t pix = (int64_t)batch * h * w;
+    const int64_t total = pix * (channels / 8);
+    const int threads = 256;
+    const int64_t blocks = (total + threads - 1) / threads;
+    nchw_to_nhwc_kernel<<<(unsigned)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+        input, static_cast<__nv_bfloat16 *>(output), channels, h * w, pix);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+}  // extern "C"

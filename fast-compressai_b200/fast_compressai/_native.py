@@ -84,6 +84,9 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _I64, _P, _I32, _I64, _I32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P],
     ),
     "fcai_warp_div_encode_pack": (ctypes.c_int, [_P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P]),
+    "fcai_layer_out_size": (ctypes.c_int, [_P, _I32, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
+    "fcai_layer_forward": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "fcai_nchw_f32_to_nhwc_bf16": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P]),
     "fcai_warp_div_decode": (
         ctypes.c_int,
         [_P, _I64, _P, _I32, _I64, _I32, _P, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _I64, _I32,

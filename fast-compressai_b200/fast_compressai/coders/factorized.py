@@ -105,7 +105,12 @@ class FactorizedWarpDivCodec:
                 end.synchronize()
                 timing["decompress_codec_ms"] = float(start.elapsed_time(end))
                 start.record()
-            result = {"x_hat": self.model.g_s(y_hat).clamp_(0, 1)}
+            g_s = self.model.g_s
+            if getattr(g_s, "fuses_clamp", False):
+                x_hat = g_s(y_hat, clamp=True)  # clamp applied in the last layer's epilogue
+            else:
+                x_hat = g_s(y_hat).clamp_(0, 1)
+            result = {"x_hat": x_hat}
             if timing is not None:
                 end.record()
                 end.synchronize()

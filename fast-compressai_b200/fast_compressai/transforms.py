@@ -1,0 +1,279 @@
+"""B200 tensor-core analysis / synthesis transforms of a FactorizedPrior.
+
+``convert_factorized_prior(model, precision="bf16")`` replaces ``model.g_a``
+and ``model.g_s`` by modules that run each (conv, GDN) or (deconv, IGDN) pair
+as one fused sm_100a kernel (include/fcai_transforms.h):
+
+    g_a: x fp32 NCHW -> [conv+GDN] x3 -> conv -> y fp32 NCHW
+    g_s: y_hat fp32 NCHW -> NHWC bf16 -> [deconv+IGDN] x3 -> deconv -> x_hat fp32 NCHW
+
+Activations between layers are bf16 NHWC.  This is the B200 counterpart of
+the reference's BF16 candidates (backends/pytorch/bf16_operators.py:13-60),
+which cast each module's input and weights to bf16 and call cuDNN; here the
+GDN is fused into the producing convolution's epilogue and the first layer
+reads the fp32 NCHW image directly.
+
+Supported shapes: N = 128 latent-transform channels (the GDN tile width of
+the kernels) and any M that is a multiple of 64 up to 256 (e.g. the
+quality 1-5 FactorizedPrior, N=128, M=192).  Other shapes raise
+``ConfigurationError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from . import _native
+from .config import ConfigurationError
+
+FCAI_LAYER_CONV5S2 = 0
+FCAI_LAYER_DECONV5S2 = 1
+FCAI_EPI_NONE, FCAI_EPI_GDN, FCAI_EPI_IGDN = 0, 1, 2
+FCAI_FMT_NHWC_BF16, FCAI_FMT_NCHW_F32 = 0, 1
+
+
+class FcaiLayer(ctypes.Structure):
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("cin", ctypes.c_int32),
+        ("cout", ctypes.c_int32),
+        ("npad", ctypes.c_int32),
+        ("epilogue", ctypes.c_int32),
+        ("in_format", ctypes.c_int32),
+        ("out_format", ctypes.c_int32),
+        ("clamp01", ctypes.c_int32),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("gdn_beta", ctypes.c_void_p),
+        ("gdn_gamma", ctypes.c_void_p),
+    ]
+
+
+def _round16(v: int) -> int:
+    return (v + 15) // 16 * 16
+
+
+def pack_tma_weight(weight: torch.Tensor, transposed: bool, npad: int) -> torch.Tensor:
+    """[25][npad][cin] bf16: entry [ky*5+kx][n][c] (conv: W[n,c,ky,kx]; deconv: W[c,n,ky,kx])."""
+    w = weight.detach().float()
+    if transposed:  # ConvTranspose2d weight [cin, cout, 5, 5]
+        cin, cout = w.shape[0], w.shape[1]
+        packed = w.permute(2, 3, 1, 0).reshape(25, cout, cin)
+    else:  # Conv2d weight [cout, cin, 5, 5]
+        cout, cin = w.shape[0], w.shape[1]
+        packed = w.permute(2, 3, 0, 1).reshape(25, cout, cin)
+    if npad > cout:
+        packed = torch.cat([packed, packed.new_zeros(25, npad - cout, cin)], dim=1)
+    return packed.to(torch.bfloat16).contiguous()
+
+
+def pack_gather_weight(weight: torch.Tensor, npad: int) -> torch.Tensor:
+    """Operand image of the cin=3 first layer: element (n, k) at
+    (n % 8) * 8 + (n // 8) * 640 + (k // 8) * 64 + k % 8, k = c*25 + ky*5 + kx."""
+    w = weight.detach().float()
+    cout = w.shape[0]
+    flat = torch.zeros(npad, 80, dtype=torch.float32, device=w.device)
+    flat[:cout, :75] = w.reshape(cout, 75)
+    n = torch.arange(npad, device=w.device).reshape(-1, 1)
+    k = torch.arange(80, device=w.device).reshape(1, -1)
+    pos = (n % 8) * 8 + (n // 8) * 640 + (k // 8) * 64 + k % 8
+    image = torch.zeros(npad * 80, dtype=torch.float32, device=w.device)
+    image[pos.reshape(-1)] = flat.reshape(-1)
+    return image.to(torch.bfloat16).contiguous()
+
+
+@dataclass
+class _Layer:
+    desc: FcaiLayer
+    keep: tuple  # tensors the descriptor points into
+    kind: int
+    cout: int
+    npad: int
+    out_format: int
+
+
+def _gdn_params(gdn: nn.Module):
+    if hasattr(gdn, "effective_params"):
+        beta, gamma = gdn.effective_params()
+    else:  # CompressAI-style GDN: beta/gamma behind reparametrisers
+        beta = gdn.beta_reparam(gdn.beta)
+        gamma = gdn.gamma_reparam(gdn.gamma)
+    c = beta.numel()
+    return beta.detach().float().contiguous(), gamma.detach().float().reshape(c, c)
+
+
+def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool) -> _Layer:
+    transposed = isinstance(conv, nn.ConvTranspose2d)
+    if tuple(conv.kernel_size) != (5, 5) or tuple(conv.stride) != (2, 2) or tuple(conv.padding) != (2, 2):
+        raise ConfigurationError("B200 transforms support 5x5 stride-2 padding-2 layers only")
+    if transposed and tuple(conv.output_padding) != (1, 1):
+        raise ConfigurationError("B200 transposed convolutions need output_padding=1")
+    if conv.groups != 1 or tuple(conv.dilation) != (1, 1) or conv.bias is None:
+        raise ConfigurationError("B200 transforms need groups=1, dilation=1 and a bias")
+    cin = conv.in_channels
+    cout = conv.out_channels
+    npad = _round16(cout)
+    if gdn is not None and npad != 128:
+        raise ConfigurationError("B200 GDN fusion is built for 128-channel layers")
+    if first:
+        if cin != 3 or transposed:
+            raise ConfigurationError("the first analysis layer must be a 3-channel convolution")
+        weight = pack_gather_weight(conv.weight, npad)
+    else:
+        if cin % 64:
+            raise ConfigurationError("B200 transforms need input channels divisible by 64")
+        weight = pack_tma_weight(conv.weight, transposed, npad)
+    if npad > 256:
+        raise ConfigurationError("B200 transforms support up to 256 output channels per layer")
+    bias = conv.bias.detach().float().contiguous()
+    keep = [weight, bias]
+    beta_ptr = gamma_ptr = None
+    epi = FCAI_EPI_NONE
+    if gdn is not None:
+        beta, gamma = _gdn_params(gdn)
+        gamma = gamma.to(torch.bfloat16).contiguous()
+        keep += [beta, gamma]
+        beta_ptr, gamma_ptr = beta.data_ptr(), gamma.data_ptr()
+        epi = FCAI_EPI_IGDN if bool(getattr(gdn, "inverse", False)) else FCAI_EPI_GDN
+    out_format = FCAI_FMT_NCHW_F32 if out_f32 else FCAI_FMT_NHWC_BF16
+    desc = FcaiLayer(
+        kind=FCAI_LAYER_DECONV5S2 if transposed else FCAI_LAYER_CONV5S2,
+        cin=cin,
+        cout=cout,
+        npad=npad,
+        epilogue=epi,
+        in_format=FCAI_FMT_NCHW_F32 if first else FCAI_FMT_NHWC_BF16,
+        out_format=out_format,
+        clamp01=1 if clamp else 0,
+        weight=weight.data_ptr(),
+        bias=bias.data_ptr(),
+        gdn_beta=beta_ptr,
+        gdn_gamma=gamma_ptr,
+    )
+    return _Layer(desc, tuple(keep), desc.kind, cout, npad, out_format)
+
+
+def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
+    lib = _native.lib()
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    B = x.shape[0]
+    if first_is_nchw:
+        h, w = x.shape[2], x.shape[3]
+    else:
+        h, w = x.shape[1], x.shape[2]
+    cur = x
+    for layer in layers:
+        ho, wo = (2 * h, 2 * w) if layer.kind == FCAI_LAYER_DECONV5S2 else ((h - 1) // 2 + 1, (w - 1) // 2 + 1)
+        if layer.out_format == FCAI_FMT_NHWC_BF16:
+            out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=x.device)
+        else:
+            out = torch.empty((B, layer.cout, ho, wo), dtype=torch.float32, device=x.device)
+        _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(cur.data_ptr()),
+                                             ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
+        cur, h, w = out, ho, wo
+    return cur
+
+
+class _Packed(nn.Sequential):
+    """A Sequential that keeps the FP32 child modules (so parameter names and
+    state_dict keys do not change) and runs packed tensor-core layers built
+    from them; the packs are rebuilt if a parameter is modified in place."""
+
+    def _signature(self):
+        return tuple((id(t), t._version) for t in self.parameters())
+
+    def _refresh_if_stale(self) -> None:
+        if self._sig != self._signature():
+            with torch.no_grad():
+                self._build()
+            self._sig = self._signature()
+
+
+class B200Analysis(_Packed):
+    """g_a on the tensor cores: fp32 NCHW image -> fp32 NCHW latent."""
+
+    def __init__(self, g_a: nn.Sequential):
+        super().__init__(*list(g_a))
+        if len(self) != 7:
+            raise ConfigurationError("g_a must be conv, GDN, conv, GDN, conv, GDN, conv")
+        self._build()
+        self._sig = self._signature()
+
+    def _build(self) -> None:
+        m = list(self)
+        self._layers = [
+            _make_layer(m[0], m[1], first=True, out_f32=False, clamp=False),
+            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False),
+            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False),
+            _make_layer(m[6], None, first=False, out_f32=True, clamp=False),
+        ]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda or x.dim() != 4 or x.shape[1] != 3:
+            raise ValueError("B200Analysis expects a CUDA [B, 3, H, W] tensor")
+        self._refresh_if_stale()
+        x = x.float().contiguous()
+        with torch.cuda.device(x.device):
+            return _run(self._layers, x, first_is_nchw=True)
+
+
+class B200Synthesis(_Packed):
+    """g_s on the tensor cores: fp32 NCHW latent -> fp32 NCHW image.
+
+    ``forward(y, clamp=True)`` applies the final clamp to [0, 1] inside the
+    last layer (the codec's ``g_s(y_hat).clamp_(0, 1)``)."""
+
+    fuses_clamp = True
+
+    def __init__(self, g_s: nn.Sequential):
+        super().__init__(*list(g_s))
+        if len(self) != 7:
+            raise ConfigurationError("g_s must be deconv, IGDN, deconv, IGDN, deconv, IGDN, deconv")
+        self.channels = self[0].in_channels
+        self._build()
+        self._sig = self._signature()
+
+    def _build(self) -> None:
+        m = list(self)
+        self._layers = [
+            _make_layer(m[0], m[1], first=False, out_f32=False, clamp=False),
+            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False),
+            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False),
+        ]
+        self._last = _make_layer(m[6], None, first=False, out_f32=True, clamp=False)
+        self._last_clamped = _make_layer(m[6], None, first=False, out_f32=True, clamp=True)
+
+    def forward(self, y: torch.Tensor, clamp: bool = False) -> torch.Tensor:
+        if not y.is_cuda or y.dim() != 4 or y.shape[1] != self.channels:
+            raise ValueError("B200Synthesis expects a CUDA [B, M, h, w] tensor")
+        self._refresh_if_stale()
+        y = y.float().contiguous()
+        B, C, h, w = y.shape
+        with torch.cuda.device(y.device):
+            nhwc = torch.empty((B, h, w, C), dtype=torch.bfloat16, device=y.device)
+            stream = torch.cuda.current_stream(y.device).cuda_stream
+            _native.check(_native.lib().fcai_nchw_f32_to_nhwc_bf16(
+                ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(nhwc.data_ptr()), B, C, h, w, ctypes.c_void_p(stream)))
+            return _run(self._layers + [self._last_clamped if clamp else self._last], nhwc, first_is_nchw=False)
+
+
+def convert_factorized_prior(model: nn.Module, precision: str = "bf16") -> nn.Module:
+    """Swap g_a / g_s for the B200 tensor-core modules (in place; returns the model)."""
+    if precision != "bf16":
+        raise ConfigurationError(f"unsupported transform precision {precision!r}")
+    if not torch.cuda.is_available():
+        raise ConfigurationError("B200 transforms require CUDA")
+    dev = next(model.parameters()).device
+    if dev.type != "cuda":
+        raise ConfigurationError("convert the model after moving it to the CUDA device")
+    with torch.no_grad(), torch.cuda.device(dev):
+        g_a = B200Analysis(model.g_a)
+        g_s = B200Synthesis(model.g_s)
+    # the new modules hold the same FP32 children, so state_dict keys are unchanged
+    model.g_a = g_a
+    model.g_s = g_s
+    return model

@@ -1,0 +1,82 @@
+/*
+ * fcai_transforms.h -- C ABI of the B200 analysis/synthesis transform layers
+ * of a FactorizedPrior (bmshj2018-factorized): 5x5 stride-2 convolutions
+ * (g_a) and 5x5 stride-2 transposed convolutions with output padding 1
+ * (g_s), each optionally followed by GDN / inverse GDN, computed as
+ * implicit GEMMs on the sm_100a tensor cores (tcgen05, bf16 operands, fp32
+ * accumulation in tensor memory, TMA tile loads).
+ *
+ * These layers replace the per-layer modules the reference swaps in for
+ * reduced precision (backends/pytorch/bf16_operators.py:13-60:
+ * BF16Conv2d, BF16ConvTranspose2d, BF16GDN), whose math is F.conv2d /
+ * F.conv_transpose2d in bf16 and x * rsqrt(beta + conv1x1(x^2, gamma)).
+ * Here GDN is fused into the convolution's epilogue as a second tensor-core
+ * GEMM over the tile's full channel vector.
+ *
+ * Layouts
+ *   activations  bf16 NHWC [B, H, W, C] (C = the layer's padded width), or
+ *                fp32 NCHW [B, C, H, W] where stated
+ *   weights      packed by the caller:
+ *     TMA layers (cin % 64 == 0): bf16 [25][npad][cin], entry [ky*5+kx][n][c]
+ *       = conv weight[n][c][ky][kx]  (Conv2d, torch layout [cout, cin, 5, 5])
+ *       = deconv weight[c][n][ky][kx] (ConvTranspose2d, [cin, cout, 5, 5]),
+ *       zero for n >= cout.
+ *     first analysis layer (cin == 3, fp32 NCHW input): bf16 image of the
+ *       operand tile, [npad rows][80 k] in 8x8 core matrices:
+ *       element (n, k) at (n % 8) * 8 + (n / 8) * 640 + (k / 8) * 64 + k % 8,
+ *       k = c * 25 + ky * 5 + kx (< 75, zero above).
+ *   gdn_gamma    bf16 [npad][npad]: effective gamma[i][j] (norm_i = beta_i +
+ *                sum_j gamma[i][j] x_j^2), zero padded.
+ *   bias, gdn_beta  fp32 [cout].
+ *
+ * All calls are asynchronous on `stream` of the current device; they use no
+ * workspace and allocate nothing.  `err` (device int, may be NULL) receives a
+ * non-zero code if a pipeline wait timed out (a bug, never expected); the
+ * kernel then stops early instead of waiting forever.
+ */
+#ifndef FCAI_TRANSFORMS_H
+#define FCAI_TRANSFORMS_H
+
+#include <stdint.h>
+
+#include "fcai_warp_div.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { FCAI_LAYER_CONV5S2 = 0, FCAI_LAYER_DECONV5S2 = 1 };
+enum { FCAI_EPI_NONE = 0, FCAI_EPI_GDN = 1, FCAI_EPI_IGDN = 2 };
+enum { FCAI_FMT_NHWC_BF16 = 0, FCAI_FMT_NCHW_F32 = 1 };
+
+typedef struct {
+    int32_t kind;       /* FCAI_LAYER_CONV5S2 or FCAI_LAYER_DECONV5S2 */
+    int32_t cin;        /* input channels (3 with in_format NCHW_F32, else a multiple of 64) */
+    int32_t cout;       /* output channels */
+    int32_t npad;       /* MMA width: cout rounded up to 16 (<= 256; 128 with GDN/IGDN) */
+    int32_t epilogue;   /* FCAI_EPI_* */
+    int32_t in_format;  /* FCAI_FMT_*: NCHW_F32 only for the cin == 3 first analysis layer */
+    int32_t out_format; /* FCAI_FMT_*: NHWC_BF16 stores npad channels; NCHW_F32 stores cout */
+    int32_t clamp01;    /* clamp outputs to [0, 1] (NCHW_F32 output only) */
+    const void *weight; /* packed, see above */
+    const float *bias;
+    const float *gdn_beta;
+    const void *gdn_gamma;
+} fcai_layer;
+
+/* Output spatial size of a layer for an input of h_in x w_in. */
+int fcai_layer_out_size(const fcai_layer *layer, int32_t h_in, int32_t w_in, int32_t *h_out, int32_t *w_out);
+
+/* One layer: output = epilogue(conv(input) + bias). */
+int fcai_layer_forward(const fcai_layer *layer, int32_t batch, int32_t h_in, int32_t w_in, const void *input,
+                       void *output, int32_t *err, fcai_stream_t stream);
+
+/* fp32 NCHW [B, C, H, W] -> bf16 NHWC [B, H, W, C] (C % 8 == 0). */
+int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h,
+                               int32_t w, fcai_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FCAI_TRANSFORMS_H */

@@ -1,0 +1,179 @@
+"""GPU tests of the tcgen05 transform layers (include/fcai_transforms.h).
+
+Per layer, the kernel is compared with a PyTorch fp32 computation of the
+same arithmetic: bf16-rounded input and weights, fp32 accumulation, bias,
+GDN on bf16(x^2) with bf16 gamma, bf16 output.  Tolerance: 1% of each value
+plus 0.1% of the tensor's max magnitude (bf16 output rounding is 0.4%; the
+rest covers fp32 summation order and approximate rsqrt).
+The whole g_a / g_s pair is then compared with the FP32 model.
+"""
+
+from __future__ import annotations
+
+import copy
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from fast_compressai import accelerate
+from fast_compressai.balle import GDN, FactorizedPrior
+from fast_compressai.transforms import (
+    FCAI_FMT_NHWC_BF16,
+    B200Analysis,
+    B200Synthesis,
+    _make_layer,
+    _run,
+)
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(t):
+    return t.to(torch.bfloat16).float()
+
+
+def _ref_layer(x_nchw, conv, gdn, out_bf16=True, clamp=False):
+    xb = _bf(x_nchw)
+    wb = _bf(conv.weight)
+    if isinstance(conv, torch.nn.ConvTranspose2d):
+        acc = F.conv_transpose2d(xb, wb, conv.bias.float(), stride=2, padding=2, output_padding=1)
+    else:
+        acc = F.conv2d(xb, wb, conv.bias.float(), stride=2, padding=2)
+    if gdn is not None:
+        beta, gamma = gdn.effective_params()
+        c = beta.numel()
+        norm = F.conv2d(_bf(acc * acc), _bf(gamma).reshape(c, c, 1, 1), beta.float())
+        acc = acc * (torch.sqrt(norm) if gdn.inverse else torch.rsqrt(norm))
+    if clamp:
+        acc = acc.clamp(0, 1)
+    return _bf(acc) if out_bf16 else acc
+
+
+def _check(mine, ref):
+    err = (mine - ref).abs()
+    bound = 0.01 * ref.abs() + 1e-3 * ref.abs().max()
+    assert bool((err <= bound).all()), f"max err {err.max().item():.4g} vs ref max {ref.abs().max().item():.4g}"
+
+
+def _nhwc(x):
+    return x.permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("H,W", [(64, 96), (40, 72), (33, 47)])
+def test_first_layer_gather_gdn(cuda_device, H, W):
+    torch.manual_seed(1)
+    conv = torch.nn.Conv2d(3, 128, 5, 2, 2).to(cuda_device)
+    gdn = GDN(128).to(cuda_device)
+    with torch.no_grad():
+        gdn.gamma.add_(torch.rand_like(gdn.gamma) * 0.05)
+        x = torch.rand(2, 3, H, W, device=cuda_device)
+        layer = _make_layer(conv, gdn, first=True, out_f32=False, clamp=False)
+        out = _run([layer], x, first_is_nchw=True)
+        torch.cuda.synchronize()
+        mine = out.float().permute(0, 3, 1, 2)
+        _check(mine, _ref_layer(x, conv, gdn))
+
+
+@pytest.mark.parametrize("cin,cout,use_gdn,H,W", [(128, 128, True, 64, 96), (128, 128, True, 37, 50),
+                                                 (128, 192, False, 32, 48), (192, 128, False, 16, 24)])
+def test_conv_layers(cuda_device, cin, cout, use_gdn, H, W):
+    torch.manual_seed(2)
+    conv = torch.nn.Conv2d(cin, cout, 5, 2, 2).to(cuda_device)
+    gdn = GDN(cout).to(cuda_device) if use_gdn else None
+    with torch.no_grad():
+        x = torch.randn(2, cin, H, W, device=cuda_device)
+        out_f32 = not use_gdn and cout == 192
+        layer = _make_layer(conv, gdn, first=False, out_f32=out_f32, clamp=False)
+        out = _run([layer], _nhwc(x), first_is_nchw=False)
+        torch.cuda.synchronize()
+        mine = out if out_f32 else out.float().permute(0, 3, 1, 2)
+        _check(mine, _ref_layer(x, conv, gdn, out_bf16=not out_f32))
+
+
+@pytest.mark.parametrize("cin,cout,use_gdn,H,W", [(192, 128, True, 8, 12), (128, 128, True, 16, 24),
+                                                 (128, 128, True, 9, 13), (128, 3, False, 16, 24)])
+def test_deconv_layers(cuda_device, cin, cout, use_gdn, H, W):
+    torch.manual_seed(3)
+    deconv = torch.nn.ConvTranspose2d(cin, cout, 5, 2, 2, output_padding=1).to(cuda_device)
+    gdn = GDN(cout, inverse=True).to(cuda_device) if use_gdn else None
+    with torch.no_grad():
+        x = torch.randn(2, cin, H, W, device=cuda_device) * 0.5
+        out_f32 = cout == 3
+        for clamp in ((False, True) if out_f32 else (False,)):
+            layer = _make_layer(deconv, gdn, first=False, out_f32=out_f32, clamp=clamp)
+            out = _run([layer], _nhwc(x), first_is_nchw=False)
+            torch.cuda.synchronize()
+            mine = out if out_f32 else out.float().permute(0, 3, 1, 2)
+            assert mine.shape == (2, cout, 2 * H, 2 * W)
+            _check(mine, _ref_layer(x, deconv, gdn, out_bf16=not out_f32, clamp=clamp))
+
+
+def _psnr(a, b):
+    mse = ((a - b) ** 2).mean().item()
+    return 10 * torch.log10(torch.tensor(1.0 / max(mse, 1e-20))).item()
+
+
+def _smooth_images(B, H, W, device, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(B, 3, H, W, generator=g)
+    x = F.avg_pool2d(F.pad(x, (2, 2, 2, 2), mode="reflect"), 5, stride=1)
+    lo = x.amin(dim=(1, 2, 3), keepdim=True)
+    hi = x.amax(dim=(1, 2, 3), keepdim=True)
+    return ((x - lo) / (hi - lo)).to(device)
+
+
+def test_full_transforms_against_fp32(cuda_device):
+    torch.manual_seed(0)
+    model = FactorizedPrior(128, 192).to(cuda_device).eval()
+    x = _smooth_images(2, 128, 192, cuda_device)
+    with torch.no_grad():
+        y_ref = model.g_a(x)
+        ga = B200Analysis(model.g_a)
+        gs = B200Synthesis(model.g_s)
+        y = ga(x)
+        assert y.shape == y_ref.shape and y.dtype == torch.float32
+        rel = (y - y_ref).abs().max() / y_ref.abs().max()
+        # the same model in PyTorch bf16 (the reference's BF16 candidates)
+        y_bf = copy.deepcopy(model.g_a).to(torch.bfloat16)(x.to(torch.bfloat16)).float()
+        rel_bf = (y_bf - y_ref).abs().max() / y_ref.abs().max()
+        assert rel < max(2 * rel_bf, 0.02), (rel.item(), rel_bf.item())
+        x_ref = model.g_s(y_ref)
+        x_mine = gs(y_ref)
+        assert x_mine.shape == x.shape
+        rel_s = (x_mine - x_ref).abs().max() / x_ref.abs().max()
+        assert rel_s < 0.05, rel_s.item()
+        clamped = gs(y_ref, clamp=True)
+        assert torch.equal(clamped, x_mine.clamp(0, 1))
+    torch.cuda.synchronize()
+
+
+def test_accelerate_bf16_end_to_end(cuda_device):
+    torch.manual_seed(0)
+    model = FactorizedPrior(128, 192).to(cuda_device).eval()
+    model.update(force=True)
+    x = _smooth_images(2, 128, 192, cuda_device, seed=3)
+    fast = accelerate(model, P=4, device="cuda:0", transforms="bf16")
+    assert fast.acceleration_report.runtime_status == "applied"
+    assert set(fast.state_dict()) == set(model.state_dict())
+    with torch.inference_mode():
+        out = fast.compress(x)
+        x_hat = fast.decompress(out["strings"], out["shape"])["x_hat"]
+        eb = model.entropy_bottleneck
+        med = eb._get_medians().detach().reshape(1, -1, 1, 1)
+        y_ref = model.g_a(x)
+        x_ref = model.g_s(torch.round(y_ref - med) + med).clamp(0, 1)
+        # decoded symbols are exactly the quantised B200 latent
+        y_fast = fast.model.g_a(x)
+        sym_fast = torch.round(y_fast - med).int()
+        fe = fast.model.entropy_bottleneck
+        idx = fe._build_indexes(sym_fast.shape, device="cuda:0").reshape(2, -1).contiguous()
+        dec = fast._coder.backend.decode(out["strings"][0], idx, fe._quantized_cdf.contiguous(),
+                                         fe._cdf_length.contiguous(), fe._offset.contiguous())
+    assert torch.equal(dec.reshape_as(sym_fast), sym_fast)
+    assert x_hat.shape == x.shape and float(x_hat.min()) >= 0 and float(x_hat.max()) <= 1
+    # the bf16 pipeline stays close to the fp32 reference reconstruction, and
+    # its PSNR against the input drops by at most 0.1 dB
+    assert _psnr(x_hat, x_ref) > 25.0, _psnr(x_hat, x_ref)
+    drop = _psnr(x_ref, x) - _psnr(x_hat, x)
+    assert drop <= 0.1, drop
