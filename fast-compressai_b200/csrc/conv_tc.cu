@@ -58,7 +58,7 @@ constexpr int kGatherThread0 = 192;  // warps 6-9
 constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
 constexpr uint64_t kWaitNs = 1000000000ull;
 
-enum Epi : int { kEpiBf16 = 0, kEpiGdn = 1, kEpiIgdn = 2, kEpiF32 = 3, kEpiF32Clamp = 4 };
+enum Epi : int { kEpiBf16 = 0, kEpiGdn = 1, kEpiIgdn = 2, kEpiF32 = 3, kEpiF32Clamp = 4, kEpiScatter = 5 };
 
 enum Err : int { kErrProducer = 1, kErrMma = 2, kErrEpilogue = 4, kErrGather = 8 };
 
@@ -70,6 +70,8 @@ struct Taps {
 
 struct ConvParams {
     int B, phases, tiles_x, tiles_y, TY, TX, GH, GW;  // per-phase GEMM pixel grid
+    int step_x, step_y;                               // tile origin step (TX/TY, or the scatter core)
+    int clamp;                                        // scatter epilogue: clamp to [0, 1]
     int stride;                                       // input step per GEMM pixel (2 conv, 1 deconv)
     int cin, cout, cin_blocks;
     int Hout, Wout, out_step;                         // output tensor size, output step per GEMM pixel
@@ -94,10 +96,13 @@ struct Layout {
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
     static constexpr int kG = kNorm ? kNpad * kNpad * 2 : 0;
     static constexpr int kX2 = kNorm ? kBM * kNpad * 2 : 0;
+    static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
+    static constexpr int kS = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
     static constexpr int offW = kStages * kStage;
     static constexpr int offG = offW + kW;
     static constexpr int offX2 = offG + kG;
-    static constexpr int offBias = offX2 + kX2;
+    static constexpr int offS = offX2 + kX2;
+    static constexpr int offBias = offS + kS;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
     static constexpr int kBars = 2 * kStages + 7;
@@ -118,8 +123,8 @@ __device__ __forceinline__ void tile_coords(const ConvParams &p, int tile, int &
     rest /= p.tiles_y;
     ph = rest % p.phases;
     b = rest / p.phases;
-    gy0 = ty * p.TY;
-    gx0 = tx * p.TX;
+    gy0 = ty * p.step_y;
+    gx0 = tx * p.step_x;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -328,7 +333,53 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
             const int oy = gy * p.out_step + (p.phases == 4 ? (ph >> 1) : 0);
             const int ox = gx * p.out_step + (p.phases == 4 ? (ph & 1) : 0);
             const uint32_t d1 = tmem_base + buf * p.buf_stride + lane_addr;
-            if (kNorm) {
+            if (kEpi == kEpiScatter) {
+                // Transposed conv with few output channels: row m (an input
+                // pixel of the 8 x 16 tile incl. a 1-pixel halo) holds its
+                // contribution to all 25 taps x cout outputs.  Each output
+                // pixel of the 12 x 28 core block sums the 4-9 contributions
+                // that land on it.
+                float *S = reinterpret_cast<float *>(smem + Lay::offS);
+#pragma unroll 1
+                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                    uint32_t v[16];
+                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + cc * 16 + e] = __uint_as_float(v[e]);
+                }
+                named_barrier_sync(1, kEpiThreads);
+                float *out = reinterpret_cast<float *>(p.out);
+                const int ow = 2 * p.step_x, oh = 2 * p.step_y;
+                const int64_t plane = (int64_t)p.Hout * p.Wout;
+                for (int o = m; o < oh * ow; o += kEpiThreads) {
+                    const int oyl = o / ow, oxl = o - oyl * ow;
+                    const int oy = 2 * gy0 + oyl, ox = 2 * gx0 + oxl;
+                    if (oy >= p.Hout || ox >= p.Wout) continue;
+                    float acc[10];
+#pragma unroll
+                    for (int co = 0; co < 10; ++co) acc[co] = co < p.cout ? s_bias[co] : 0.f;
+                    for (int ky = oyl & 1; ky < 5; ky += 2) {
+                        const int r = (oyl + 4 - ky) >> 1;
+                        for (int kx = oxl & 1; kx < 5; kx += 2) {
+                            const int col = (oxl + 4 - kx) >> 1;
+                            const float *src = S + (r * p.TX + col) * Lay::kSRow + (ky * 5 + kx) * p.cout;
+#pragma unroll
+                            for (int co = 0; co < 10; ++co)
+                                if (co < p.cout) acc[co] += src[co];
+                        }
+                    }
+#pragma unroll
+                    for (int co = 0; co < 10; ++co) {
+                        if (co < p.cout) {
+                            float yv = acc[co];
+                            if (p.clamp) yv = fminf(fmaxf(yv, 0.f), 1.f);
+                            out[((int64_t)b * p.cout + co) * plane + (int64_t)oy * p.Wout + ox] = yv;
+                        }
+                    }
+                }
+                named_barrier_sync(1, kEpiThreads);  // S is rewritten by the next tile
+            } else if (kNorm) {
                 // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile
                 const uint32_t x2 = smem_u32(smem + Lay::offX2);
 #pragma unroll 1
@@ -587,6 +638,9 @@ static int dispatch(int npad, int epi, bool gather, const CUtensorMap &a, const 
             if (epi == kEpiF32Clamp) return launch<16, kEpiF32Clamp, false>(a, w, g, p, stream);
             if (epi == kEpiF32) return launch<16, kEpiF32, false>(a, w, g, p, stream);
             break;
+        case 80:
+            if (epi == kEpiScatter) return launch<80, kEpiScatter, false>(a, w, g, p, stream);
+            break;
         default:
             break;
     }
@@ -648,21 +702,40 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     const bool norm = L->epilogue == FCAI_EPI_GDN || L->epilogue == FCAI_EPI_IGDN;
     if (norm && (!L->gdn_beta || !L->gdn_gamma || L->out_format != FCAI_FMT_NHWC_BF16))
         return fcai::fail(FCAI_ERR_INVALID, "GDN epilogue needs beta, gamma and a bf16 NHWC output");
+    const bool scatter = L->algorithm == FCAI_ALGO_SCATTER;
+    if (scatter && (!deconv || L->cout > 10 || npad != (25 * L->cout + 15) / 16 * 16 || norm ||
+                    L->out_format != FCAI_FMT_NCHW_F32))
+        return fcai::fail(FCAI_ERR_INVALID,
+                          "scatter layers are transposed convolutions with cout <= 10, npad = round16(25 * cout) "
+                          "and an fp32 NCHW output");
     int epi;
-    if (L->epilogue == FCAI_EPI_GDN) epi = kEpiGdn;
+    if (scatter) epi = kEpiScatter;
+    else if (L->epilogue == FCAI_EPI_GDN) epi = kEpiGdn;
     else if (L->epilogue == FCAI_EPI_IGDN) epi = kEpiIgdn;
     else if (L->out_format == FCAI_FMT_NHWC_BF16) epi = kEpiBf16;
     else epi = L->clamp01 ? kEpiF32Clamp : kEpiF32;
 
     ConvParams p{};
     p.B = batch;
-    p.phases = deconv ? 4 : 1;
+    p.phases = deconv && !scatter ? 4 : 1;
     p.GH = deconv ? h_in : ho;
     p.GW = deconv ? w_in : wo;
-    p.TX = pick_tx(p.GW);
-    p.TY = kBM / p.TX;
-    p.tiles_x = (p.GW + p.TX - 1) / p.TX;
-    p.tiles_y = (p.GH + p.TY - 1) / p.TY;
+    if (scatter) {
+        // 8 x 16 input pixels per tile = a 6 x 14 core plus a 1-pixel halo;
+        // the core produces a 12 x 28 output block
+        p.TX = 16;
+        p.TY = 8;
+        p.step_x = 14;
+        p.step_y = 6;
+    } else {
+        p.TX = pick_tx(p.GW);
+        p.TY = kBM / p.TX;
+        p.step_x = p.TX;
+        p.step_y = p.TY;
+    }
+    p.clamp = L->clamp01 ? 1 : 0;
+    p.tiles_x = (p.GW + p.step_x - 1) / p.step_x;
+    p.tiles_y = (p.GH + p.step_y - 1) / p.step_y;
     p.stride = deconv ? 1 : 2;
     p.cin = L->cin;
     p.cout = L->cout;
@@ -681,7 +754,12 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.buf_stride = stride;
     p.tmem_cols = 2 * stride;
     if (p.tmem_cols > 512) return fcai::fail(FCAI_ERR_INVALID, "accumulators exceed tensor memory");
-    if (deconv) {
+    if (scatter) {
+        p.taps[0].n = 1;  // one K pass over the halo tile, all taps are GEMM columns
+        p.taps[0].dy[0] = -1;
+        p.taps[0].dx[0] = -1;
+        p.taps[0].w[0] = 0;
+    } else if (deconv) {
         for (int ph = 0; ph < 4; ++ph) {
             const int py = ph >> 1, px = ph & 1;
             int n = 0;
@@ -721,7 +799,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)(p.TX * s), (cuuint32_t)(p.TY * s), 1};
         cuuint32_t es[4] = {1, (cuuint32_t)s, (cuuint32_t)s, 1};
         if ((rc = make_map(&ma, input, 4, dims, strides, box, es))) return rc;
-        cuuint64_t wd[3] = {(cuuint64_t)L->cin, (cuuint64_t)npad, 25};
+        cuuint64_t wd[3] = {(cuuint64_t)L->cin, (cuuint64_t)npad, (cuuint64_t)(scatter ? 1 : 25)};
         cuuint64_t ws[2] = {(cuuint64_t)L->cin * 2, (cuuint64_t)npad * L->cin * 2};
         cuuint32_t wb[3] = {(cuuint32_t)kBK, (cuuint32_t)npad, 1};
         cuuint32_t we[3] = {1, 1, 1};

@@ -213,12 +213,16 @@ __device__ void validate_tables_global(const TableArgs &t, uint32_t &flags) {
     }
 }
 
+// Full-table accessor (every row of the batch, in shared memory when it
+// fits, else read from global memory).  The division magic comes from the
+// per-device table g_magic.
 template <bool kSmem>
 struct Tables {
     const uint32_t *s_tab;
     const int2 *s_ch;
     const uint16_t *s_lut;
     TableArgs g;
+    const float *med;  // latent medians (global)
 
     __device__ __forceinline__ int2 chan(int c) const {
         if (kSmem) return s_ch[c];
@@ -231,6 +235,8 @@ struct Tables {
         const int32_t *row = g.cdfs + (int64_t)c * g.L;
         return pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
     }
+    __device__ __forceinline__ uint64_t magic(int, int, uint32_t freq) const { return g_magic[freq]; }
+    __device__ __forceinline__ float median(int c) const { return __ldg(med + c); }
     // First s in [0, maxv] with cdf[s+1] > slot (maxv if none); returns the
     // symbol and its entry.
     __device__ __forceinline__ int search(int c, int maxv, uint32_t slot, uint32_t &ent, uint32_t &flags) const {
@@ -255,6 +261,74 @@ struct Tables {
     }
 };
 
+// Group accessor: the rows [c0, c0 + nc) of one chunk group in shared memory,
+// with the division magic of every entry (encode) or the slot buckets
+// (decode) and the medians of the latent modes.
+struct GroupTables {
+    const uint32_t *s_tab;  // [nc][Ls]
+    const uint64_t *s_mag;  // [nc][Ls] (encode)
+    const int2 *s_ch;       // [nc]
+    const uint16_t *s_lut;  // [nc][kLutBuckets] (decode)
+    const float *s_med;     // [nc] (latent modes)
+    int c0, Ls;
+
+    __device__ __forceinline__ int2 chan(int c) const { return s_ch[c - c0]; }
+    __device__ __forceinline__ uint32_t entry(int c, int v, uint32_t &) const { return s_tab[(c - c0) * Ls + v]; }
+    __device__ __forceinline__ uint64_t magic(int c, int v, uint32_t) const { return s_mag[(c - c0) * Ls + v]; }
+    __device__ __forceinline__ float median(int c) const { return s_med[c - c0]; }
+    __device__ __forceinline__ int search(int c, int maxv, uint32_t slot, uint32_t &ent, uint32_t &) const {
+        const int cl = c - c0;
+        int s = s_lut[cl * kLutBuckets + (slot >> kLutShift)];
+        if (s > maxv) s = maxv;
+        const uint32_t *row = s_tab + cl * Ls;
+        uint32_t e = row[s];
+        while (s < maxv && (e & 0xFFFFu) + (e >> 16) + 1u <= slot) e = row[++s];
+        ent = e;
+        return s;
+    }
+};
+
+// Stages rows [c0, c0 + nc) (entries, {offset, maxv}, optional magic, slot
+// buckets and medians) and validates them.  Ends with __syncthreads().
+__device__ void stage_group(const TableArgs &t, int c0, int nc, uint32_t *s_tab, uint64_t *s_mag, int2 *s_ch,
+                            uint16_t *s_lut, float *s_med, const float *medians, uint32_t &flags) {
+    const int Ls = t.L - 1;
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        int32_t size = __ldg(t.sizes + c0 + c);
+        if (size < 2 || size > t.L) {
+            flags |= kFlagTable;
+            size = size < 2 ? 2 : t.L;
+        }
+        s_ch[c] = make_int2(__ldg(t.offs + c0 + c), size - 2);
+        if (s_med) s_med[c] = __ldg(medians + c0 + c);
+    }
+    __syncthreads();
+    const int total = nc * Ls;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        const int c = e / Ls, v = e - c * Ls;
+        const int maxv = s_ch[c].y;
+        uint32_t ent = 0u;
+        if (v <= maxv) {
+            const int32_t *row = t.cdfs + (int64_t)(c0 + c) * t.L;
+            ent = pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
+            if (s_lut) {
+                const int lo = v == 0 ? 0 : (int)(ent & 0xFFFFu);
+                const int hi = v == maxv ? 65536 : (int)(ent & 0xFFFFu) + (int)(ent >> 16) + 1;
+                int u0 = (lo + (1 << kLutShift) - 1) >> kLutShift;
+                int u1 = (hi + (1 << kLutShift) - 1) >> kLutShift;
+                if (u1 > kLutBuckets) u1 = kLutBuckets;
+                for (int u = u0; u < u1; ++u) s_lut[c * kLutBuckets + u] = (uint16_t)v;
+            }
+        }
+        s_tab[e] = ent;
+        if (s_mag) {
+            const uint32_t freq = (ent >> 16) + 1u;  // entries of valid rows have freq in [1, 65536]
+            s_mag[e] = freq >= 2 ? (~0ull) / (uint64_t)freq : 0ull;
+        }
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // rANS primitives (rans64_gpu.cuh:21-55, rans64_gpu_v2.cuh:90-120 semantics)
 // ---------------------------------------------------------------------------
@@ -269,7 +343,8 @@ struct LaneWriter {
     }
 };
 
-__device__ __forceinline__ void put_symbol(uint64_t &x, uint32_t start, uint32_t freq, LaneWriter &w) {
+__device__ __forceinline__ void put_symbol(uint64_t &x, uint32_t start, uint32_t freq, uint64_t magic,
+                                           LaneWriter &w) {
     if (x >= ((uint64_t)freq << 47)) {  // ((L >> 16) << 32) * freq
         w.emit((uint32_t)x);
         x >>= 32;
@@ -280,7 +355,7 @@ __device__ __forceinline__ void put_symbol(uint64_t &x, uint32_t start, uint32_t
         q = freq ? x : 0ull;
         r = freq ? 0u : (uint32_t)x;
     } else {
-        q = __umul64hi(x, g_magic[freq]);  // floor(x / freq) or one less
+        q = __umul64hi(x, magic);  // magic = floor((2^64 - 1) / freq): floor(x / freq) or one less
         uint64_t rr = x - q * (uint64_t)freq;
         if (rr >= freq) {
             ++q;
@@ -410,115 +485,107 @@ __device__ __forceinline__ void load_batch(const EncParams &p, int64_t row0, int
     }
 }
 
-template <int kMode, bool kSmem>
-__global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
+// Codes one chunk: each lane runs its symbols last to first (prefetching the
+// next kPrefetch symbols while coding the current ones), staging its words
+// in emission order, then the warp records used words and max_rounds.
+template <int kMode, class Tab>
+__device__ __forceinline__ void encode_chunk(const EncParams &p, const Tab &tab, int64_t chunk, int lane,
+                                             uint32_t &flags, unsigned int &my_max_used) {
     constexpr bool kIdx = kMode == kModeIdx;
-    extern __shared__ __align__(16) unsigned char smem[];
+    const int C = p.t.C;
+    const int b = (int)(chunk / p.K);
+    const int k = (int)(chunk - (int64_t)b * p.K);
+    const int start = k * p.chunk_len;
+    const int end = min(start + p.chunk_len, p.N);
+    const int first = start + lane;
+    LaneWriter w{p.stage + chunk * (int64_t)p.rows_cap * kLanes + lane, p.rows_cap, 0};
+    if (first < end) {
+        const int n = (end - 1 - first) / kLanes + 1;
+        const int last = first + (n - 1) * kLanes;
+        int ct = last / p.HW, rem = last - ct * p.HW;  // channel-layout position tracker
+        const int64_t row0 = (int64_t)b * p.N;
+        uint64_t x = kRansL;
+        int32_t cur[kPrefetch], icur[kPrefetch];
+        load_batch<kMode>(p, row0, last, 0, n, cur, icur);
+        for (int t0 = 0; t0 < n; t0 += kPrefetch) {
+            // the next batch's loads are in flight while this one is coded
+            int32_t nxt[kPrefetch], inxt[kPrefetch];
+            load_batch<kMode>(p, row0, last, t0 + kPrefetch, n, nxt, inxt);
+#pragma unroll
+            for (int u = 0; u < kPrefetch; ++u) {
+                if (t0 + u < n) {
+                    int32_t s;
+                    if (kMode == kModeLatent) {
+                        // torch.round (half to even) then .int(), both in fp32
+                        s = __float2int_rz(rintf(__int_as_float(cur[u]) - tab.median(ct)));
+                    } else {
+                        s = cur[u];
+                    }
+                    int c = ct;
+                    if (kIdx) {
+                        const int32_t ci = icur[u];
+                        if (ci != ct) flags |= kFlagNonChannel;
+                        if ((unsigned)ci >= (unsigned)C) {
+                            flags |= kFlagIndexRange;
+                            c = 0;
+                        } else {
+                            c = ci;
+                        }
+                    }
+                    const int2 ch = tab.chan(c);
+                    int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
+                    const int32_t maxv = ch.y;
+                    if (value < 0 || value >= maxv) {
+                        // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
+                        uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
+                                                 : ((uint32_t)value - (uint32_t)maxv) * 2u;
+                        put_escape(x, raw, w);
+                        value = maxv;
+                    }
+                    const uint32_t e = tab.entry(c, value, flags);
+                    const uint32_t freq = (e >> 16) + 1u;
+                    put_symbol(x, e & 0xFFFFu, freq, tab.magic(c, value, freq), w);
+                    rem -= kLanes;
+                    while (rem < 0) {
+                        rem += p.HW;
+                        --ct;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kPrefetch; ++u) {
+                cur[u] = nxt[u];
+                icur[u] = inxt[u];
+            }
+        }
+        w.emit((uint32_t)(x >> 32));  // flush: decode order is low, high, ...
+        w.emit((uint32_t)x);
+    }
+    const int used = w.j;
+    int rounds = used;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, o));
+    p.used[chunk * kLanes + lane] = used;
+    if (lane == 0) {
+        p.rounds[chunk] = rounds;
+        p.max_rounds_out[chunk] = (uint32_t)rounds;
+    }
+    if ((unsigned)rounds > my_max_used) my_max_used = (unsigned)rounds;
+}
+
+// CTA summary; the last CTA to finish computes the chunk offsets and the
+// status block the host reads, and re-arms the control block.
+__device__ __forceinline__ void finish_encode(const EncParams &p, uint32_t flags, unsigned int my_max_used) {
     __shared__ uint64_t s_warp[33];
     __shared__ unsigned int s_flags, s_max_used;
     __shared__ int s_last;
+    if (my_max_used > (unsigned)p.rows_cap) flags |= kFlagOverflow;
+    __syncthreads();
     if (threadIdx.x == 0) {
         s_flags = 0;
         s_max_used = 0;
     }
-    uint32_t flags = 0;
-    const int C = p.t.C;
-    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
-    int2 *s_ch = reinterpret_cast<int2 *>(smem + (((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll));
-    if (kSmem) {
-        stage_tables(p.t, s_tab, s_ch, nullptr, flags);
-    } else {
-        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
-        __syncthreads();
-    }
-    Tables<kSmem> tab{s_tab, s_ch, nullptr, p.t};
-
-    const int lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
-    const int64_t warp_stride = (int64_t)gridDim.x * warps;
-    unsigned int my_max_used = 0;
-    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
-        const int b = (int)(chunk / p.K);
-        const int k = (int)(chunk - (int64_t)b * p.K);
-        const int start = k * p.chunk_len;
-        const int end = min(start + p.chunk_len, p.N);
-        const int first = start + lane;
-        LaneWriter w{p.stage + chunk * (int64_t)p.rows_cap * kLanes + lane, p.rows_cap, 0};
-        if (first < end) {
-            const int n = (end - 1 - first) / kLanes + 1;
-            const int last = first + (n - 1) * kLanes;
-            int ct = last / p.HW, rem = last - ct * p.HW;  // channel-layout position tracker
-            const int64_t row0 = (int64_t)b * p.N;
-            uint64_t x = kRansL;
-            int32_t cur[kPrefetch], icur[kPrefetch];
-            load_batch<kMode>(p, row0, last, 0, n, cur, icur);
-            for (int t0 = 0; t0 < n; t0 += kPrefetch) {
-                // the next batch's loads are in flight while this one is coded
-                int32_t nxt[kPrefetch], inxt[kPrefetch];
-                load_batch<kMode>(p, row0, last, t0 + kPrefetch, n, nxt, inxt);
-#pragma unroll
-                for (int u = 0; u < kPrefetch; ++u) {
-                    if (t0 + u < n) {
-                        int32_t s;
-                        if (kMode == kModeLatent) {
-                            // torch.round (half to even) then .int(), both in fp32
-                            s = __float2int_rz(rintf(__int_as_float(cur[u]) - __ldg(p.medians + ct)));
-                        } else {
-                            s = cur[u];
-                        }
-                        int c = ct;
-                        if (kIdx) {
-                            const int32_t ci = icur[u];
-                            if (ci != ct) flags |= kFlagNonChannel;
-                            if ((unsigned)ci >= (unsigned)C) {
-                                flags |= kFlagIndexRange;
-                                c = 0;
-                            } else {
-                                c = ci;
-                            }
-                        }
-                        const int2 ch = tab.chan(c);
-                        int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
-                        const int32_t maxv = ch.y;
-                        if (value < 0 || value >= maxv) {
-                            // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
-                            uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
-                                                     : ((uint32_t)value - (uint32_t)maxv) * 2u;
-                            put_escape(x, raw, w);
-                            value = maxv;
-                        }
-                        const uint32_t e = tab.entry(c, value, flags);
-                        put_symbol(x, e & 0xFFFFu, (e >> 16) + 1u, w);
-                        rem -= kLanes;
-                        while (rem < 0) {
-                            rem += p.HW;
-                            --ct;
-                        }
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < kPrefetch; ++u) {
-                    cur[u] = nxt[u];
-                    icur[u] = inxt[u];
-                }
-            }
-            w.emit((uint32_t)(x >> 32));  // flush: decode order is low, high, ...
-            w.emit((uint32_t)x);
-        }
-        const int used = w.j;
-        int rounds = used;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, o));
-        p.used[chunk * kLanes + lane] = used;
-        if (lane == 0) {
-            p.rounds[chunk] = rounds;
-            p.max_rounds_out[chunk] = (uint32_t)rounds;
-        }
-        if ((unsigned)rounds > my_max_used) my_max_used = (unsigned)rounds;
-    }
-    if (my_max_used > (unsigned)p.rows_cap) flags |= kFlagOverflow;
-
-    // CTA summary, then the last CTA computes offsets and the status block.
+    __syncthreads();
     if (flags) atomicOr(&s_flags, flags);
     if (my_max_used) atomicMax(&s_max_used, my_max_used);
     __syncthreads();
@@ -542,6 +609,84 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
         ctl->max_used = 0;
         ctl->done = 0;
     }
+}
+
+// Explicit indexes: any row can be used by any symbol, so every CTA stages
+// all rows once and its warps take chunks in a grid-stride loop.
+template <bool kSmem>
+__global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t flags = 0;
+    const int C = p.t.C;
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    int2 *s_ch = reinterpret_cast<int2 *>(smem + (((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll));
+    if (kSmem) {
+        stage_tables(p.t, s_tab, s_ch, nullptr, flags);
+    } else {
+        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
+        __syncthreads();
+    }
+    Tables<kSmem> tab{s_tab, s_ch, nullptr, p.t, p.medians};
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t warp_stride = (int64_t)gridDim.x * warps;
+    unsigned int my_max_used = 0;
+    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride)
+        encode_chunk<kModeIdx>(p, tab, chunk, lane, flags, my_max_used);
+    finish_encode(p, flags, my_max_used);
+}
+
+// Shared-memory layout of one chunk group (rows [c0, c0 + P)).
+struct GroupSmem {
+    int64_t mag, tab, ch, med, lut, bytes;
+};
+__host__ __device__ inline GroupSmem group_smem(int P, int L, bool encode) {
+    const int64_t ent = (int64_t)P * (L - 1);
+    GroupSmem g;
+    g.mag = 0;
+    g.tab = encode ? ent * 8 : 0;
+    g.ch = (g.tab + ent * 4 + 7) & ~7ll;
+    g.med = g.ch + (int64_t)P * 8;
+    g.lut = (g.med + (int64_t)P * 4 + 7) & ~7ll;
+    g.bytes = g.lut + (encode ? 0 : (int64_t)P * kLutBuckets * 2);
+    return g;
+}
+
+// Channel-layout indexes: chunk k only uses rows [k*P, k*P + P).  A CTA of
+// W warps takes groups (k, images b0 .. b0+W-1); it stages just those rows,
+// with every entry's division magic, so a symbol costs shared-memory reads
+// only.
+template <int kMode, bool kSmem>
+__global__ void __launch_bounds__(kThreads) encode_group_kernel(EncParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t flags = 0;
+    unsigned int my_max_used = 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int nbb = (p.B + W - 1) / W;
+    const int64_t groups = (int64_t)p.K * nbb;
+    const GroupSmem gs = group_smem(p.P, p.t.L, true);
+    GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), reinterpret_cast<const uint64_t *>(smem + gs.mag),
+                   reinterpret_cast<const int2 *>(smem + gs.ch), nullptr, reinterpret_cast<const float *>(smem + gs.med),
+                   0, p.t.L - 1};
+    Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
+    if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
+    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
+        const int k = (int)(g % p.K), bb = (int)(g / p.K);
+        if (kSmem) {
+            const int c0 = k * p.P, nc = min(p.P, p.t.C - c0);
+            __syncthreads();  // the previous group's rows are no longer read
+            stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), reinterpret_cast<uint64_t *>(smem + gs.mag),
+                        reinterpret_cast<int2 *>(smem + gs.ch), nullptr,
+                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags);
+            gt.c0 = c0;
+        }
+        const int b = bb * W + warp;
+        if (b < p.B) {
+            if (kSmem) encode_chunk<kMode>(p, gt, (int64_t)b * p.K + k, lane, flags, my_max_used);
+            else encode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags, my_max_used);
+        }
+    }
+    finish_encode(p, flags, my_max_used);
 }
 
 struct PackParams {
@@ -704,97 +849,84 @@ __device__ __forceinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t 
     return true;
 }
 
-template <int kMode, bool kSmem>
-__global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
+// Decodes one chunk: each lane reads its state, then its symbols first to
+// last, refilling from a look-ahead queue of its payload words.
+template <int kMode, class Tab>
+__device__ __forceinline__ void decode_chunk(const DecParams &p, const Tab &tab, int64_t chunk, int lane,
+                                             uint32_t &flags) {
     constexpr bool kIdx = kMode == kModeIdx;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ unsigned int s_flags;
-    __shared__ int s_last;
-    if (threadIdx.x == 0) s_flags = 0;
-    uint32_t flags = 0;
-    // prep (or an earlier CTA) found a bad payload or table
-    const bool skip = (*((volatile unsigned int *)&p.ctrl->flags) & ~kFlagNonChannel) != 0;
     const int C = p.t.C;
-    const int64_t tab_bytes = ((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll;
-    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
-    int2 *s_ch = reinterpret_cast<int2 *>(smem + tab_bytes);
-    uint16_t *s_lut = reinterpret_cast<uint16_t *>(smem + tab_bytes + (int64_t)C * 8);
-    if (kSmem) {
-        stage_tables(p.t, s_tab, s_ch, s_lut, flags);
-    } else {
-        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
-        __syncthreads();
-    }
-    Tables<kSmem> tab{s_tab, s_ch, s_lut, p.t};
-    const int lane = threadIdx.x & 31;
     const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
-    const int warps = blockDim.x >> 5;
-    const int64_t warp_stride = (int64_t)gridDim.x * warps;
-    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); !skip && chunk < p.chunks;
-         chunk += warp_stride) {
-        const int b = (int)(chunk / p.K);
-        const int k = (int)(chunk - (int64_t)b * p.K);
-        const int64_t start64 = (int64_t)k * p.chunk_len;
-        if (start64 >= p.N) continue;
-        const int start = (int)start64;
-        const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
-        const int first = start + lane;
-        if (first >= end) continue;
-        LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u};
-        rd.start();
-        uint64_t x = (uint64_t)rd.next();
-        x |= (uint64_t)rd.next() << 32;
-        const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
-        int32_t *orow = kMode == kModeLatent ? nullptr : p.out + (int64_t)b * p.N;
-        float *yrow = kMode == kModeLatent ? p.y_out + (int64_t)b * p.N : nullptr;
-        int ct = first / p.HW, rem = first - ct * p.HW;
-        const int n = (end - 1 - first) / kLanes + 1;
-        int32_t icur[kPrefetch], inxt[kPrefetch];
+    const int b = (int)(chunk / p.K);
+    const int k = (int)(chunk - (int64_t)b * p.K);
+    const int64_t start64 = (int64_t)k * p.chunk_len;
+    if (start64 >= p.N) return;
+    const int start = (int)start64;
+    const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
+    const int first = start + lane;
+    if (first >= end) return;
+    LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u};
+    rd.start();
+    uint64_t x = (uint64_t)rd.next();
+    x |= (uint64_t)rd.next() << 32;
+    const int32_t *irow = kIdx ? p.idx + (int64_t)b * p.N : nullptr;
+    int32_t *orow = kMode == kModeLatent ? nullptr : p.out + (int64_t)b * p.N;
+    float *yrow = kMode == kModeLatent ? p.y_out + (int64_t)b * p.N : nullptr;
+    int ct = first / p.HW, rem = first - ct * p.HW;
+    const int n = (end - 1 - first) / kLanes + 1;
+    int32_t icur[kPrefetch], inxt[kPrefetch];
 #pragma unroll
-        for (int u = 0; u < kPrefetch; ++u) icur[u] = (kIdx && u < n) ? __ldg(irow + first + u * kLanes) : 0;
-        for (int t0 = 0; t0 < n && !rd.bad; t0 += kPrefetch) {
+    for (int u = 0; u < kPrefetch; ++u) icur[u] = (kIdx && u < n) ? __ldg(irow + first + u * kLanes) : 0;
+    for (int t0 = 0; t0 < n && !rd.bad; t0 += kPrefetch) {
 #pragma unroll
-            for (int u = 0; u < kPrefetch; ++u)  // next batch of indexes in flight
-                inxt[u] = (kIdx && t0 + kPrefetch + u < n) ? __ldg(irow + first + (t0 + kPrefetch + u) * kLanes) : 0;
+        for (int u = 0; u < kPrefetch; ++u)  // next batch of indexes in flight
+            inxt[u] = (kIdx && t0 + kPrefetch + u < n) ? __ldg(irow + first + (t0 + kPrefetch + u) * kLanes) : 0;
 #pragma unroll
-            for (int u = 0; u < kPrefetch; ++u) {
-                if (t0 + u < n && !rd.bad) {
-                    const int i = first + (t0 + u) * kLanes;
-                    int c = ct;
-                    if (kIdx) {
-                        const int32_t ci = icur[u];
-                        if (ci != ct) flags |= kFlagNonChannel;
-                        if ((unsigned)ci >= (unsigned)C) {
-                            flags |= kFlagIndexRange;
-                            c = 0;
-                        } else {
-                            c = ci;
-                        }
-                    }
-                    const int2 ch = tab.chan(c);
-                    const uint32_t slot = (uint32_t)x & 0xFFFFu;
-                    uint32_t e;
-                    int32_t value = tab.search(c, ch.y, slot, e, flags);
-                    x = (uint64_t)((e >> 16) + 1u) * (x >> 16) + (uint64_t)slot - (uint64_t)(e & 0xFFFFu);
-                    if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
-                    if (value == ch.y && !get_escape(x, rd, ch.y, value)) rd.bad = true;
-                    if (!rd.bad) {
-                        const int32_t sym = (int32_t)((uint32_t)value + (uint32_t)ch.x);
-                        if (kMode == kModeLatent) yrow[i] = __int2float_rn(sym) + __ldg(p.medians + c);
-                        else orow[i] = sym;
-                    }
-                    rem += kLanes;
-                    while (rem >= p.HW) {
-                        rem -= p.HW;
-                        ++ct;
+        for (int u = 0; u < kPrefetch; ++u) {
+            if (t0 + u < n && !rd.bad) {
+                const int i = first + (t0 + u) * kLanes;
+                int c = ct;
+                if (kIdx) {
+                    const int32_t ci = icur[u];
+                    if (ci != ct) flags |= kFlagNonChannel;
+                    if ((unsigned)ci >= (unsigned)C) {
+                        flags |= kFlagIndexRange;
+                        c = 0;
+                    } else {
+                        c = ci;
                     }
                 }
+                const int2 ch = tab.chan(c);
+                const uint32_t slot = (uint32_t)x & 0xFFFFu;
+                uint32_t e;
+                int32_t value = tab.search(c, ch.y, slot, e, flags);
+                x = (uint64_t)((e >> 16) + 1u) * (x >> 16) + (uint64_t)slot - (uint64_t)(e & 0xFFFFu);
+                if (x < kRansL) x = (x << 32) | (uint64_t)rd.next();
+                if (value == ch.y && !get_escape(x, rd, ch.y, value)) rd.bad = true;
+                if (!rd.bad) {
+                    const int32_t sym = (int32_t)((uint32_t)value + (uint32_t)ch.x);
+                    if (kMode == kModeLatent) yrow[i] = __int2float_rn(sym) + tab.median(c);
+                    else orow[i] = sym;
+                }
+                rem += kLanes;
+                while (rem >= p.HW) {
+                    rem -= p.HW;
+                    ++ct;
+                }
             }
-#pragma unroll
-            for (int u = 0; u < kPrefetch; ++u) icur[u] = inxt[u];
         }
-        if (rd.bad) flags |= kFlagCorrupt;
+#pragma unroll
+        for (int u = 0; u < kPrefetch; ++u) icur[u] = inxt[u];
     }
+    if (rd.bad) flags |= kFlagCorrupt;
+}
+
+__device__ __forceinline__ void finish_decode(const DecParams &p, uint32_t flags) {
+    __shared__ unsigned int s_flags;
+    __shared__ int s_last;
+    __syncthreads();
+    if (threadIdx.x == 0) s_flags = 0;
+    __syncthreads();
     if (flags) atomicOr(&s_flags, flags);
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -810,6 +942,80 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
         ctl->flags = 0;
         ctl->done = 0;
     }
+}
+
+// prep (or an earlier CTA) found a bad payload or table: decode nothing
+__device__ __forceinline__ bool decode_skip(const DecParams &p) {
+    return (*((volatile unsigned int *)&p.ctrl->flags) & ~kFlagNonChannel) != 0;
+}
+
+// All rows staged per CTA (explicit indexes, or a chunk_len that is not a
+// whole number of channels), grid-stride over chunks.
+template <int kMode, bool kSmem>
+__global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t flags = 0;
+    const bool skip = decode_skip(p);
+    const int C = p.t.C;
+    const int64_t tab_bytes = ((int64_t)C * (p.t.L - 1) * 4 + 15) & ~15ll;
+    uint32_t *s_tab = reinterpret_cast<uint32_t *>(smem);
+    int2 *s_ch = reinterpret_cast<int2 *>(smem + tab_bytes);
+    uint16_t *s_lut = reinterpret_cast<uint16_t *>(smem + tab_bytes + (int64_t)C * 8);
+    if (kSmem) {
+        stage_tables(p.t, s_tab, s_ch, s_lut, flags);
+    } else {
+        if (blockIdx.x == 0) validate_tables_global(p.t, flags);
+        __syncthreads();
+    }
+    Tables<kSmem> tab{s_tab, s_ch, s_lut, p.t, p.medians};
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int64_t warp_stride = (int64_t)gridDim.x * warps;
+    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); !skip && chunk < p.chunks;
+         chunk += warp_stride)
+        decode_chunk<kMode>(p, tab, chunk, lane, flags);
+    finish_decode(p, flags);
+}
+
+// Channel-layout indexes: chunk groups with only their rows (and slot
+// buckets) staged, as in encode_group_kernel.
+template <int kMode, bool kSmem>
+__global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int s_skip;
+    uint32_t flags = 0;
+    // one read for the whole CTA: the loop below has barriers, so every
+    // thread must take the same number of iterations
+    if (threadIdx.x == 0) s_skip = decode_skip(p) ? 1 : 0;
+    __syncthreads();
+    const bool skip = s_skip != 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int P = p.chunk_len / p.HW;
+    const int nbb = (p.B + W - 1) / W;
+    const int64_t groups = (int64_t)p.K * nbb;
+    const GroupSmem gs = group_smem(P, p.t.L, false);
+    GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), nullptr, reinterpret_cast<const int2 *>(smem + gs.ch),
+                   reinterpret_cast<const uint16_t *>(smem + gs.lut), reinterpret_cast<const float *>(smem + gs.med), 0,
+                   p.t.L - 1};
+    Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
+    if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
+    for (int64_t g = blockIdx.x; g < groups && !skip; g += gridDim.x) {
+        const int k = (int)(g % p.K), bb = (int)(g / p.K);
+        if (kSmem) {
+            const int c0 = min(k * P, p.t.C), nc = max(0, min(P, p.t.C - c0));
+            __syncthreads();
+            stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), nullptr,
+                        reinterpret_cast<int2 *>(smem + gs.ch), reinterpret_cast<uint16_t *>(smem + gs.lut),
+                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags);
+            gt.c0 = c0;
+        }
+        const int b = bb * W + warp;
+        if (b < p.B) {
+            if (kSmem) decode_chunk<kMode>(p, gt, (int64_t)b * p.K + k, lane, flags);
+            else decode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags);
+        }
+    }
+    finish_decode(p, flags);
 }
 
 // ---------------------------------------------------------------------------
@@ -928,22 +1134,53 @@ static int grid_for(K kernel, int64_t smem, int64_t chunks, int warps, int &grid
     return FCAI_OK;
 }
 
-template <int kMode, bool kSmem>
-static int launch_encode(const EncParams &p, int64_t smem, cudaStream_t stream) {
+// Warps per CTA for chunk groups: up to 8 images per group, fewer when that
+// leaves SMs idle (few chunks per image, e.g. large P).
+static int group_warps(int B, int K) {
+    const int64_t sms = fcai::sm_count();
+    int w = B < kWarps ? B : kWarps;
+    while (w > 1 && (int64_t)K * ((B + w - 1) / w) < sms) w >>= 1;
+    return w < 1 ? 1 : w;
+}
+
+template <bool kSmem>
+static int launch_encode_full(const EncParams &p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
     const int warps = warps_for(p.chunks);
-    if ((rc = grid_for(encode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, warps, grid))) return rc;
-    encode_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
+    if ((rc = grid_for(encode_kernel<kSmem>, kSmem ? smem : 0, p.chunks, warps, grid))) return rc;
+    encode_kernel<kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
 
 template <int kMode, bool kSmem>
-static int launch_decode(const DecParams &p, int64_t smem, cudaStream_t stream) {
+static int launch_encode_group(const EncParams &p, int64_t smem, cudaStream_t stream) {
+    int grid = 1, rc;
+    const int warps = group_warps(p.B, p.K);
+    const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
+    if ((rc = grid_for(encode_group_kernel<kMode, kSmem>, kSmem ? smem : 0, groups * warps, warps, grid))) return rc;
+    encode_group_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+template <int kMode, bool kSmem>
+static int launch_decode_full(const DecParams &p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
     const int warps = warps_for(p.chunks);
     if ((rc = grid_for(decode_kernel<kMode, kSmem>, kSmem ? smem : 0, p.chunks, warps, grid))) return rc;
     decode_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+template <int kMode, bool kSmem>
+static int launch_decode_group(const DecParams &p, int64_t smem, cudaStream_t stream) {
+    int grid = 1, rc;
+    const int warps = group_warps(p.B, p.K);
+    const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
+    if ((rc = grid_for(decode_group_kernel<kMode, kSmem>, kSmem ? smem : 0, groups * warps, warps, grid))) return rc;
+    decode_group_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
@@ -1017,11 +1254,19 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     p.stage = reinterpret_cast<uint32_t *>(ws + el.stage);
     p.max_rounds_out = max_rounds;
 
-    const int64_t smem = encode_smem_bytes(C, L);
-    const bool sm = smem <= kMaxSmemBytes;
-    if (mode == kModeIdx) rc = sm ? launch_encode<kModeIdx, true>(p, smem, stream) : launch_encode<kModeIdx, false>(p, smem, stream);
-    else if (mode == kModeChannel) rc = sm ? launch_encode<kModeChannel, true>(p, smem, stream) : launch_encode<kModeChannel, false>(p, smem, stream);
-    else rc = sm ? launch_encode<kModeLatent, true>(p, smem, stream) : launch_encode<kModeLatent, false>(p, smem, stream);
+    if (mode == kModeIdx) {
+        const int64_t smem = encode_smem_bytes(C, L);
+        rc = smem <= kMaxSmemBytes ? launch_encode_full<true>(p, smem, stream) : launch_encode_full<false>(p, smem, stream);
+    } else {
+        const int64_t smem = group_smem(d.P, L, true).bytes;
+        const bool sm = smem <= kMaxSmemBytes;
+        if (mode == kModeChannel)
+            rc = sm ? launch_encode_group<kModeChannel, true>(p, smem, stream)
+                    : launch_encode_group<kModeChannel, false>(p, smem, stream);
+        else
+            rc = sm ? launch_encode_group<kModeLatent, true>(p, smem, stream)
+                    : launch_encode_group<kModeLatent, false>(p, smem, stream);
+    }
     if (rc) return rc;
     long long status[8];
     FCAI_CUDA_TRY(cudaMemcpyAsync(status, p.ctrl->status, sizeof(status), cudaMemcpyDeviceToHost, stream));
@@ -1091,11 +1336,28 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     p.ctrl = ctrl;
     p.offsets = offs;
     p.out = symbols_out;
-    const int64_t smem = decode_smem_bytes(C, L);
-    const bool sm = smem <= kMaxSmemBytes;
-    if (mode == kModeIdx) rc = sm ? launch_decode<kModeIdx, true>(p, smem, stream) : launch_decode<kModeIdx, false>(p, smem, stream);
-    else if (mode == kModeChannel) rc = sm ? launch_decode<kModeChannel, true>(p, smem, stream) : launch_decode<kModeChannel, false>(p, smem, stream);
-    else rc = sm ? launch_decode<kModeLatent, true>(p, smem, stream) : launch_decode<kModeLatent, false>(p, smem, stream);
+    const int HW = N / C;
+    if (mode == kModeIdx || chunk_len % HW != 0) {
+        const int64_t smem = decode_smem_bytes(C, L);
+        const bool sm = smem <= kMaxSmemBytes;
+        if (mode == kModeIdx)
+            rc = sm ? launch_decode_full<kModeIdx, true>(p, smem, stream) : launch_decode_full<kModeIdx, false>(p, smem, stream);
+        else if (mode == kModeChannel)
+            rc = sm ? launch_decode_full<kModeChannel, true>(p, smem, stream)
+                    : launch_decode_full<kModeChannel, false>(p, smem, stream);
+        else
+            rc = sm ? launch_decode_full<kModeLatent, true>(p, smem, stream)
+                    : launch_decode_full<kModeLatent, false>(p, smem, stream);
+    } else {
+        const int64_t smem = group_smem(chunk_len / HW, L, false).bytes;
+        const bool sm = smem <= kMaxSmemBytes;
+        if (mode == kModeChannel)
+            rc = sm ? launch_decode_group<kModeChannel, true>(p, smem, stream)
+                    : launch_decode_group<kModeChannel, false>(p, smem, stream);
+        else
+            rc = sm ? launch_decode_group<kModeLatent, true>(p, smem, stream)
+                    : launch_decode_group<kModeLatent, false>(p, smem, stream);
+    }
     if (rc) return rc;
     if (!check) return FCAI_OK;
     long long flags = 0;

@@ -95,6 +95,15 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 
+# Kernels launched through this library since import (each C-ABI call
+# launches a known number of kernels; the Python wrappers add them here).
+LAUNCHES = {"kernels": 0}
+
+
+def count_launches(n: int) -> None:
+    LAUNCHES["kernels"] += n
+
+
 def available() -> bool:
     return LIB_PATH.exists()
 

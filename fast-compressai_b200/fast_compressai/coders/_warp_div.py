@@ -107,6 +107,7 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
         for attempt in range(2):
             ws = workspace("encode", dev, stream, nbytes)
             rc = call(lib, ws, max_rounds, info, ctypes.c_void_p(stream))
+            _native.count_launches(1)
             if rc == _native.FCAI_ERR_WORKSPACE and attempt == 0 and info.required_workspace_bytes > ws.numel():
                 nbytes = info.required_workspace_bytes
                 continue
@@ -115,6 +116,7 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
         packed = torch.empty(int(info.packed_bytes), dtype=torch.uint8, device=dev)
         _native.check(lib.fcai_warp_div_encode_pack(_ptr(ws), ws.numel(), B, N, C, int(P), _ptr(packed),
                                                     packed.numel(), ctypes.c_void_p(stream)))
+        _native.count_launches(1)
     return EncodeResult(packed, max_rounds, int(info.header_bytes), int(info.chunk_len), int(info.p_ch),
                         bool(info.index_layout_is_channel))
 
@@ -187,6 +189,7 @@ def decode_latent(packed: torch.Tensor, max_rounds: torch.Tensor, header_bytes: 
             _ptr(packed), packed.numel(), _ptr(max_rounds), K, int(header_bytes), int(chunk_len), B, N, _ptr(cdfs),
             C, L, _ptr(cdf_sizes), _ptr(offsets), _ptr(medians), _ptr(out), _ptr(ws), ws.numel(), 1,
             ctypes.c_void_p(stream))
+        _native.count_launches(2)
         _native.check(rc)
     return out
 
@@ -234,6 +237,7 @@ def decode(packed: torch.Tensor, max_rounds: torch.Tensor, header_bytes: int, ch
             _ptr(packed), packed.numel(), _ptr(rounds32), K, int(header_bytes), int(chunk_len), _ptr(indexes), B,
             N, _ptr(cdfs), C, L, _ptr(cdf_sizes), _ptr(offsets), _ptr(out), _ptr(ws), ws.numel(), 1,
             ctypes.byref(layout), ctypes.c_void_p(stream))
+        _native.count_launches(2)
         _native.check(rc)
     return (out, bool(layout.value)) if return_layout else out
 

@@ -48,10 +48,10 @@ def _version(t: torch.Tensor) -> int:
     return -1 if t.is_inference() else t._version
 
 
-def _remember_rounds(max_rounds: torch.Tensor, total_rounds: int) -> None:
+def _remember_rounds(max_rounds: torch.Tensor, total_rounds: int, all_ok: bool = True) -> None:
     with _STATS_LOCK:
         _ROUND_STATS[id(max_rounds)] = (weakref.ref(max_rounds), _version(max_rounds), max_rounds.data_ptr(),
-                                        True, int(total_rounds))
+                                        bool(all_ok), int(total_rounds))
         if len(_ROUND_STATS) > 4096:
             for key in [k for k, v in _ROUND_STATS.items() if v[0]() is None]:
                 del _ROUND_STATS[key]
@@ -119,6 +119,72 @@ class WarpDivPayload:
             raise CoderInputError("warp_div chunk rounds must include two initial state words")
         if self.header_bytes + total * 32 * 4 != self.packed.numel():
             raise CoderInputError("warp_div packed payload length does not match chunk rounds")
+
+    # -- persistent form ---------------------------------------------------
+    # The reference payload is device-local only (README.md:56,106 of the
+    # reference).  This container makes it a byte string that can be stored
+    # or sent and decoded on any CUDA device:
+    #   magic "FCWD", u32 container version (1), u32 format_version,
+    #   u32 batch, u32 symbols_per_batch, u32 cdf_count, u32 p_ch,
+    #   u32 chunk_len, u64 header_bytes, u64 packed_bytes, u32 has_fingerprint,
+    #   32-byte raw SHA-256 fingerprint (zeros if absent), then the packed
+    #   payload (whose header already holds max_rounds).  Little-endian.
+    _MAGIC = b"FCWD"
+
+    def to_bytes(self) -> bytes:
+        """Serialise (one device-to-host copy of ``packed``)."""
+        return self.container_header() + self.packed.cpu().numpy().tobytes()
+
+    def container_header(self) -> bytes:
+        fp = bytes.fromhex(self.coding_fingerprint) if self.coding_fingerprint else bytes(32)
+        return (self._MAGIC + np.array([1, self.format_version, self.batch, self.symbols_per_batch,
+                                        self.cdf_count, self.p_ch, self.chunk_len], dtype="<u4").tobytes()
+                + np.array([self.header_bytes, self.packed.numel()], dtype="<u8").tobytes()
+                + np.array([1 if self.coding_fingerprint else 0], dtype="<u4").tobytes() + fp)
+
+    @classmethod
+    def from_bytes(cls, data, device="cuda") -> "WarpDivPayload":
+        """Rebuild a payload on ``device`` from ``to_bytes()`` output."""
+        buf = memoryview(data)
+        meta_len = 4 + 7 * 4 + 2 * 8 + 4 + 32
+        if len(buf) < meta_len or bytes(buf[:4]) != cls._MAGIC:
+            raise CoderInputError("not a serialized warp_div payload")
+        u32 = np.frombuffer(buf[4:32], dtype="<u4")
+        u64 = np.frombuffer(buf[32:48], dtype="<u8")
+        has_fp = int(np.frombuffer(buf[48:52], dtype="<u4")[0])
+        if int(u32[0]) != 1:
+            raise CoderInputError("unsupported warp_div container version")
+        packed_len = int(u64[1])
+        if len(buf) != meta_len + packed_len:
+            raise CoderInputError("serialized warp_div payload is truncated")
+        host = torch.frombuffer(bytearray(buf[meta_len:]), dtype=torch.uint8)
+        return cls.from_host_packed(host, batch=int(u32[2]), symbols_per_batch=int(u32[3]), cdf_count=int(u32[4]),
+                                    p_ch=int(u32[5]), chunk_len=int(u32[6]), header_bytes=int(u64[0]),
+                                    coding_fingerprint=bytes(buf[52:84]).hex() if has_fp else None,
+                                    format_version=int(u32[1]), device=device)
+
+    @classmethod
+    def from_host_packed(cls, packed_host: torch.Tensor, *, batch: int, symbols_per_batch: int, cdf_count: int,
+                         p_ch: int, chunk_len: int, header_bytes: int, coding_fingerprint: str | None,
+                         device="cuda", format_version: int = FORMAT_VERSION) -> "WarpDivPayload":
+        """Build a payload from a host copy of ``packed``; ``max_rounds`` is
+        read from the packed header on the host, so no device sync happens."""
+        if packed_host.device.type != "cpu" or packed_host.dtype != torch.uint8:
+            raise CoderInputError("packed_host must be a CPU uint8 tensor")
+        K = (cdf_count + p_ch - 1) // p_ch if p_ch > 0 else 0
+        n = batch * K
+        if n <= 0 or packed_host.numel() < 32 + 4 * n:
+            raise CoderInputError("serialized warp_div header is truncated")
+        rounds = packed_host[32:32 + 4 * n].view(torch.int32).reshape(batch, K)
+        if bool((rounds < 0).any()):
+            raise CoderInputError("warp_div packed header round counts are invalid")
+        dev = torch.device(device)
+        max_rounds = rounds.to(torch.uint32).to(dev, non_blocking=False)
+        packed = packed_host.to(dev)
+        _remember_rounds(max_rounds, int(rounds.to(torch.int64).sum()), all_ok=bool((rounds >= 2).all()))
+        return cls(packed=packed, max_rounds=max_rounds, header_bytes=header_bytes, chunk_len=chunk_len, p_ch=p_ch,
+                   batch=batch, symbols_per_batch=symbols_per_batch, cdf_count=cdf_count,
+                   coding_fingerprint=coding_fingerprint, format_version=format_version)
 
 
 # ---------------------------------------------------------------------------

@@ -34,6 +34,7 @@ FCAI_LAYER_CONV5S2 = 0
 FCAI_LAYER_DECONV5S2 = 1
 FCAI_EPI_NONE, FCAI_EPI_GDN, FCAI_EPI_IGDN = 0, 1, 2
 FCAI_FMT_NHWC_BF16, FCAI_FMT_NCHW_F32 = 0, 1
+FCAI_ALGO_IMPLICIT_GEMM, FCAI_ALGO_SCATTER = 0, 1
 
 
 class FcaiLayer(ctypes.Structure):
@@ -46,6 +47,8 @@ class FcaiLayer(ctypes.Structure):
         ("in_format", ctypes.c_int32),
         ("out_format", ctypes.c_int32),
         ("clamp01", ctypes.c_int32),
+        ("algorithm", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("weight", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("gdn_beta", ctypes.c_void_p),
@@ -86,6 +89,17 @@ def pack_gather_weight(weight: torch.Tensor, npad: int) -> torch.Tensor:
     return image.to(torch.bfloat16).contiguous()
 
 
+def pack_scatter_weight(weight: torch.Tensor, npad: int) -> torch.Tensor:
+    """[npad][cin] bf16 for a transposed conv with few outputs: row
+    (ky*5 + kx)*cout + co holds W[:, co, ky, kx]."""
+    w = weight.detach().float()  # [cin, cout, 5, 5]
+    cin, cout = w.shape[0], w.shape[1]
+    rows = w.permute(2, 3, 1, 0).reshape(25 * cout, cin)
+    if npad > rows.shape[0]:
+        rows = torch.cat([rows, rows.new_zeros(npad - rows.shape[0], cin)], dim=0)
+    return rows.to(torch.bfloat16).contiguous()
+
+
 @dataclass
 class _Layer:
     desc: FcaiLayer
@@ -94,6 +108,26 @@ class _Layer:
     cout: int
     npad: int
     out_format: int
+    name: str = ""
+
+    def flops(self, batch: int, h_in: int, w_in: int) -> float:
+        """Algorithmic FLOPs: 2 * cin * 25 * cout per output (conv) or input
+        (deconv) pixel, plus 2 * cout^2 per output pixel for GDN."""
+        d = self.desc
+        if self.kind == FCAI_LAYER_DECONV5S2:
+            pix_in, pix_out = h_in * w_in, 4 * h_in * w_in
+            f = 2.0 * batch * pix_in * d.cin * d.cout * 25  # the same for the scatter algorithm
+        else:
+            pix_out = ((h_in - 1) // 2 + 1) * ((w_in - 1) // 2 + 1)
+            f = 2.0 * batch * pix_out * d.cin * d.cout * 25
+        if d.epilogue != FCAI_EPI_NONE:
+            f += 2.0 * batch * pix_out * d.cout * d.cout
+        return f
+
+
+# When set to a list, every layer launch appends (name, flops, start, end)
+# CUDA events recorded on the launching stream (used by bench.py).
+LAYER_TIMING: list | None = None
 
 
 def _gdn_params(gdn: nn.Module):
@@ -117,6 +151,9 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
     cin = conv.in_channels
     cout = conv.out_channels
     npad = _round16(cout)
+    scatter = transposed and out_f32 and gdn is None and cout <= 10
+    if scatter:
+        npad = _round16(25 * cout)
     if gdn is not None and npad != 128:
         raise ConfigurationError("B200 GDN fusion is built for 128-channel layers")
     if first:
@@ -126,7 +163,7 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
     else:
         if cin % 64:
             raise ConfigurationError("B200 transforms need input channels divisible by 64")
-        weight = pack_tma_weight(conv.weight, transposed, npad)
+        weight = pack_scatter_weight(conv.weight, npad) if scatter else pack_tma_weight(conv.weight, transposed, npad)
     if npad > 256:
         raise ConfigurationError("B200 transforms support up to 256 output channels per layer")
     bias = conv.bias.detach().float().contiguous()
@@ -149,6 +186,8 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         in_format=FCAI_FMT_NCHW_F32 if first else FCAI_FMT_NHWC_BF16,
         out_format=out_format,
         clamp01=1 if clamp else 0,
+        algorithm=FCAI_ALGO_SCATTER if scatter else FCAI_ALGO_IMPLICIT_GEMM,
+        reserved=0,
         weight=weight.data_ptr(),
         bias=bias.data_ptr(),
         gdn_beta=beta_ptr,
@@ -172,8 +211,16 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
             out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=x.device)
         else:
             out = torch.empty((B, layer.cout, ho, wo), dtype=torch.float32, device=x.device)
+        timing = LAYER_TIMING
+        if timing is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
         _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(cur.data_ptr()),
                                              ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
+        _native.count_launches(1)
+        if timing is not None:
+            ev1.record()
+            timing.append((layer.name, layer.flops(B, h, w), ev0, ev1))
         cur, h, w = out, ho, wo
     return cur
 
@@ -211,6 +258,8 @@ class B200Analysis(_Packed):
             _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False),
             _make_layer(m[6], None, first=False, out_f32=True, clamp=False),
         ]
+        for i, layer in enumerate(self._layers):
+            layer.name = f"g_a.{2 * i}" + ("+gdn" if i < 3 else "")
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not x.is_cuda or x.dim() != 4 or x.shape[1] != 3:
@@ -246,6 +295,9 @@ class B200Synthesis(_Packed):
         ]
         self._last = _make_layer(m[6], None, first=False, out_f32=True, clamp=False)
         self._last_clamped = _make_layer(m[6], None, first=False, out_f32=True, clamp=True)
+        for i, layer in enumerate(self._layers):
+            layer.name = f"g_s.{2 * i}+igdn"
+        self._last.name = self._last_clamped.name = "g_s.6"
 
     def forward(self, y: torch.Tensor, clamp: bool = False) -> torch.Tensor:
         if not y.is_cuda or y.dim() != 4 or y.shape[1] != self.channels:
@@ -258,6 +310,7 @@ class B200Synthesis(_Packed):
             stream = torch.cuda.current_stream(y.device).cuda_stream
             _native.check(_native.lib().fcai_nchw_f32_to_nhwc_bf16(
                 ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(nhwc.data_ptr()), B, C, h, w, ctypes.c_void_p(stream)))
+            _native.count_launches(1)
             return _run(self._layers + [self._last_clamped if clamp else self._last], nhwc, first_is_nchw=False)
 
 

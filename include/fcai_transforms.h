@@ -21,6 +21,8 @@
  *       = conv weight[n][c][ky][kx]  (Conv2d, torch layout [cout, cin, 5, 5])
  *       = deconv weight[c][n][ky][kx] (ConvTranspose2d, [cin, cout, 5, 5]),
  *       zero for n >= cout.
+ *     scatter layers: bf16 [npad][cin], entry [(ky*5+kx)*cout + co][c] =
+ *       deconv weight[c][co][ky][kx], npad = round16(25 * cout), zero above.
  *     first analysis layer (cin == 3, fp32 NCHW input): bf16 image of the
  *       operand tile, [npad rows][80 k] in 8x8 core matrices:
  *       element (n, k) at (n % 8) * 8 + (n / 8) * 640 + (k / 8) * 64 + k % 8,
@@ -48,6 +50,12 @@ extern "C" {
 enum { FCAI_LAYER_CONV5S2 = 0, FCAI_LAYER_DECONV5S2 = 1 };
 enum { FCAI_EPI_NONE = 0, FCAI_EPI_GDN = 1, FCAI_EPI_IGDN = 2 };
 enum { FCAI_FMT_NHWC_BF16 = 0, FCAI_FMT_NCHW_F32 = 1 };
+/* FCAI_ALGO_IMPLICIT_GEMM: GEMM over output pixels x output channels.
+ * FCAI_ALGO_SCATTER: transposed convolutions with cout <= 10 (the last
+ *   synthesis layer): GEMM over input pixels x (25 taps * cout) columns on
+ *   halo tiles, each output pixel summing its taps in the epilogue, so the
+ *   input is read about 1.5x instead of once per tap. */
+enum { FCAI_ALGO_IMPLICIT_GEMM = 0, FCAI_ALGO_SCATTER = 1 };
 
 typedef struct {
     int32_t kind;       /* FCAI_LAYER_CONV5S2 or FCAI_LAYER_DECONV5S2 */
@@ -58,6 +66,8 @@ typedef struct {
     int32_t in_format;  /* FCAI_FMT_*: NCHW_F32 only for the cin == 3 first analysis layer */
     int32_t out_format; /* FCAI_FMT_*: NHWC_BF16 stores npad channels; NCHW_F32 stores cout */
     int32_t clamp01;    /* clamp outputs to [0, 1] (NCHW_F32 output only) */
+    int32_t algorithm;  /* FCAI_ALGO_* */
+    int32_t reserved;
     const void *weight; /* packed, see above */
     const float *bias;
     const float *gdn_beta;

@@ -92,7 +92,8 @@ def test_conv_layers(cuda_device, cin, cout, use_gdn, H, W):
 
 
 @pytest.mark.parametrize("cin,cout,use_gdn,H,W", [(192, 128, True, 8, 12), (128, 128, True, 16, 24),
-                                                 (128, 128, True, 9, 13), (128, 3, False, 16, 24)])
+                                                 (128, 128, True, 9, 13), (128, 3, False, 16, 24),
+                                                 (128, 3, False, 9, 13), (128, 3, False, 31, 47)])
 def test_deconv_layers(cuda_device, cin, cout, use_gdn, H, W):
     torch.manual_seed(3)
     deconv = torch.nn.ConvTranspose2d(cin, cout, 5, 2, 2, output_padding=1).to(cuda_device)
