@@ -51,10 +51,15 @@ using namespace tcx;
 constexpr int kBM = 128;          // output pixels per tile (MMA M)
 constexpr int kBK = 64;           // bf16 per K block: one 128-byte row
 constexpr int kStages = 4;
-constexpr int kEpiThreads = 128;  // warps 0-3
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kGatherThread0 = 192;  // warps 6-9
+constexpr int kEpiWarps = 8;      // warps 0-7: two per TMEM lane quarter, one per column half
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kGatherThread0 = 320;  // warps 10-13
+constexpr int kGatherThreads = 128;
+// scatter layers: 8 x 16 input pixels per tile, of which the 6 x 14 core
+// produces a 12 x 28 output block; cout = 3 (25 taps x 3 = 75 -> npad 80)
+constexpr int kScatterTY = 8, kScatterTX = 16, kScatterCoreH = 6, kScatterCoreW = 14, kScatterCout = 3;
 constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
 constexpr uint64_t kWaitNs = 1000000000ull;
 
@@ -109,7 +114,10 @@ struct Layout {
     static constexpr int offSlot = offBar + kBars * 8;
     static constexpr int kBytes = offSlot + 32;
     static constexpr int kAlloc = kBytes + 1024;  // base alignment slack
-    static constexpr int kThreads = kGather ? 320 : 192;
+    static constexpr int kThreads = kGather ? 448 : 320;
+    // column split between the two epilogue warps of a lane quarter
+    static constexpr int kSplit = kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
+    static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
@@ -169,7 +177,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], kGather ? kEpiThreads : 1);
+            mbar_init(&full[s], kGather ? kGatherThreads : 1);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -302,14 +310,17 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 mma_commit(&accf[buf]);
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < kEpiWarps) {
         // ------------------------------------------------------------ epilogue
+        // Warp w reads TMEM lanes 32*(w%4).. (tile rows) and column half w/4.
         // Thread 0 alone waits on the mbarriers and publishes the outcome in
-        // epi_ok; all 128 threads then meet at named barrier 1, so the group
-        // always takes the same branch and no thread waits at a barrier the
-        // others have left.
-        const int m = threadIdx.x;  // TMEM lane = tile row = output pixel
-        const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+        // epi_ok; all epilogue threads then meet at named barrier 1, so the
+        // group always takes the same branch and no thread waits at a barrier
+        // the others have left.
+        const int m = threadIdx.x & 127;  // TMEM lane = tile row = output pixel
+        const int half = threadIdx.x >> 7;
+        const int c_lo = half ? Lay::kSplit : 0, c_hi = half ? kNpad : Lay::kSplit;
+        const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         bool consts = !kNorm;
         int j = 0;
         for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++j) {
@@ -317,7 +328,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
             tile_coords(p, tile, b, ph, gy0, gx0);
             const int buf = j & 1;
             const uint32_t use = j >> 1;
-            if (m == 0) {
+            if (threadIdx.x == 0) {
                 bool ok = !*abort;
                 if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
                 if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
@@ -336,68 +347,77 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
             if (kEpi == kEpiScatter) {
                 // Transposed conv with few output channels: row m (an input
                 // pixel of the 8 x 16 tile incl. a 1-pixel halo) holds its
-                // contribution to all 25 taps x cout outputs.  Each output
-                // pixel of the 12 x 28 core block sums the 4-9 contributions
-                // that land on it.
+                // contribution to all 25 taps x 3 outputs.  Each output pixel
+                // of the 12 x 28 core block sums the 4-9 contributions that
+                // land on it; one work item = one output pixel.
                 float *S = reinterpret_cast<float *>(smem + Lay::offS);
 #pragma unroll 1
-                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                for (int c = c_lo; c < c_hi; c += 16) {
                     uint32_t v[16];
-                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_ld16(d1 + c, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + cc * 16 + e] = __uint_as_float(v[e]);
+                    for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + c + e] = __uint_as_float(v[e]);
                 }
                 named_barrier_sync(1, kEpiThreads);
                 float *out = reinterpret_cast<float *>(p.out);
-                const int ow = 2 * p.step_x, oh = 2 * p.step_y;
                 const int64_t plane = (int64_t)p.Hout * p.Wout;
-                for (int o = m; o < oh * ow; o += kEpiThreads) {
-                    const int oyl = o / ow, oxl = o - oyl * ow;
-                    const int oy = 2 * gy0 + oyl, ox = 2 * gx0 + oxl;
-                    if (oy >= p.Hout || ox >= p.Wout) continue;
-                    float acc[10];
+                const float b0 = s_bias[0], b1 = s_bias[1], b2 = s_bias[2];
+                for (int item = threadIdx.x; item < kScatterCoreH * kScatterCoreW * 4; item += kEpiThreads) {
+                    const int core = item >> 2, py = (item >> 1) & 1, px = item & 1;
+                    const int ci = core / kScatterCoreW, cj = core - ci * kScatterCoreW;
+                    const int oyv = 2 * (gy0 + ci) + py, oxv = 2 * (gx0 + cj) + px;
+                    if (oyv >= p.Hout || oxv >= p.Wout) continue;
+                    float a0 = b0, a1 = b1, a2 = b2;
 #pragma unroll
-                    for (int co = 0; co < 10; ++co) acc[co] = co < p.cout ? s_bias[co] : 0.f;
-                    for (int ky = oyl & 1; ky < 5; ky += 2) {
-                        const int r = (oyl + 4 - ky) >> 1;
-                        for (int kx = oxl & 1; kx < 5; kx += 2) {
-                            const int col = (oxl + 4 - kx) >> 1;
-                            const float *src = S + (r * p.TX + col) * Lay::kSRow + (ky * 5 + kx) * p.cout;
+                    for (int ty = 0; ty < 3; ++ty) {
+                        const int ky = py + 2 * ty;
+                        if (ky < 5) {
+                            const int r = ci + 1 + ((py + 2 - ky) >> 1);
 #pragma unroll
-                            for (int co = 0; co < 10; ++co)
-                                if (co < p.cout) acc[co] += src[co];
+                            for (int tx = 0; tx < 3; ++tx) {
+                                const int kx = px + 2 * tx;
+                                if (kx < 5) {
+                                    const int col = cj + 1 + ((px + 2 - kx) >> 1);
+                                    const float *src =
+                                        S + (r * kScatterTX + col) * Lay::kSRow + (ky * 5 + kx) * kScatterCout;
+                                    a0 += src[0];
+                                    a1 += src[1];
+                                    a2 += src[2];
+                                }
+                            }
                         }
                     }
-#pragma unroll
-                    for (int co = 0; co < 10; ++co) {
-                        if (co < p.cout) {
-                            float yv = acc[co];
-                            if (p.clamp) yv = fminf(fmaxf(yv, 0.f), 1.f);
-                            out[((int64_t)b * p.cout + co) * plane + (int64_t)oy * p.Wout + ox] = yv;
-                        }
+                    if (p.clamp) {
+                        a0 = fminf(fmaxf(a0, 0.f), 1.f);
+                        a1 = fminf(fmaxf(a1, 0.f), 1.f);
+                        a2 = fminf(fmaxf(a2, 0.f), 1.f);
                     }
+                    float *o = out + (int64_t)b * kScatterCout * plane + (int64_t)oyv * p.Wout + oxv;
+                    o[0] = a0;
+                    o[plane] = a1;
+                    o[2 * plane] = a2;
                 }
                 named_barrier_sync(1, kEpiThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
                 // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile
                 const uint32_t x2 = smem_u32(smem + Lay::offX2);
 #pragma unroll 1
-                for (int cc = 0; cc < kNpad / 32; ++cc) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
                     uint32_t v[32];
-                    tmem_ld32(d1 + cc * 32, v);
+                    tmem_ld32(d1 + c0, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         uint32_t w[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const int c = cc * 32 + q * 8 + e * 2;
+                            const int c = c0 + q * 8 + e * 2;
                             const float a = __uint_as_float(v[q * 8 + e * 2]) + s_bias[c];
                             const float bb = __uint_as_float(v[q * 8 + e * 2 + 1]) + s_bias[c + 1];
                             w[e] = pack_bf16x2(a * a, bb * bb);
                         }
-                        const int k0 = cc * 32 + q * 8;
+                        const int k0 = c0 + q * 8;
                         const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
                         st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
                                      w[3]);
@@ -405,7 +425,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 }
                 fence_proxy_async_smem();
                 named_barrier_sync(1, kEpiThreads);
-                if (m == 0) {
+                if (threadIdx.x == 0) {
                     tc_fence_after();
                     const uint32_t g0 = smem_u32(smem + Lay::offG);
                     const uint32_t d2 = tmem_base + buf * p.buf_stride + kNpad;
@@ -429,48 +449,47 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
                                       (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
 #pragma unroll 1
-                for (int cc = 0; cc < kNpad / 32; ++cc) {
-                    uint32_t v[32], nv[32];
-                    tmem_ld32(d1 + cc * 32, v);
-                    tmem_ld32(d1 + kNpad + cc * 32, nv);
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+                    uint32_t v[16], nv[16];
+                    tmem_ld16(d1 + c0, v);
+                    tmem_ld16(d1 + kNpad + c0, nv);
                     tmem_wait_ld();
-                    uint32_t o[16];
+                    uint32_t o[8];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int c = cc * 32 + 2 * e;
-                        float r0 = rsqrtf(__uint_as_float(nv[2 * e]) + s_beta[c]);
-                        float r1 = rsqrtf(__uint_as_float(nv[2 * e + 1]) + s_beta[c + 1]);
+                    for (int e = 0; e < 8; ++e) {
+                        const int c = c0 + 2 * e;
+                        const float n0 = __uint_as_float(nv[2 * e]) + s_beta[c];
+                        const float n1 = __uint_as_float(nv[2 * e + 1]) + s_beta[c + 1];
+                        float r0 = rsqrtf(n0), r1 = rsqrtf(n1);
                         if (kEpi == kEpiIgdn) {
-                            r0 = (__uint_as_float(nv[2 * e]) + s_beta[c]) * r0;
-                            r1 = (__uint_as_float(nv[2 * e + 1]) + s_beta[c + 1]) * r1;
+                            r0 *= n0;  // sqrt(n) = n * rsqrt(n)
+                            r1 *= n1;
                         }
                         const float x0 = __uint_as_float(v[2 * e]) + s_bias[c];
                         const float x1 = __uint_as_float(v[2 * e + 1]) + s_bias[c + 1];
                         o[e] = pack_bf16x2(x0 * r0, x1 * r1);
                     }
                     if (valid) {
-                        uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 32);
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
                         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
                         dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                        dst[2] = make_uint4(o[8], o[9], o[10], o[11]);
-                        dst[3] = make_uint4(o[12], o[13], o[14], o[15]);
                     }
                 }
             } else if (kEpi == kEpiBf16) {
                 __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
                                       (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
 #pragma unroll 1
-                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     uint32_t v[16];
-                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_ld16(d1 + c0, v);
                     tmem_wait_ld();
                     uint32_t o[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]) + s_bias[cc * 16 + 2 * e],
-                                           __uint_as_float(v[2 * e + 1]) + s_bias[cc * 16 + 2 * e + 1]);
+                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]) + s_bias[c0 + 2 * e],
+                                           __uint_as_float(v[2 * e + 1]) + s_bias[c0 + 2 * e + 1]);
                     if (valid) {
-                        uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 16);
+                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
                         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
                         dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
                     }
@@ -481,13 +500,13 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 const int64_t plane = (int64_t)p.Hout * p.Wout;
                 const int64_t pix = (int64_t)oy * p.Wout + ox;
 #pragma unroll 1
-                for (int cc = 0; cc < kNpad / 16; ++cc) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     uint32_t v[16];
-                    tmem_ld16(d1 + cc * 16, v);
+                    tmem_ld16(d1 + c0, v);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const int c = cc * 16 + e;
+                        const int c = c0 + e;
                         float y = __uint_as_float(v[e]) + s_bias[c];
                         if (kEpi == kEpiF32Clamp) y = fminf(fmaxf(y, 0.f), 1.f);
                         if (valid && c < p.cout) out[((int64_t)b * p.cout + c) * plane + pix] = y;
@@ -723,10 +742,10 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     if (scatter) {
         // 8 x 16 input pixels per tile = a 6 x 14 core plus a 1-pixel halo;
         // the core produces a 12 x 28 output block
-        p.TX = 16;
-        p.TY = 8;
-        p.step_x = 14;
-        p.step_y = 6;
+        p.TX = kScatterTX;
+        p.TY = kScatterTY;
+        p.step_x = kScatterCoreW;
+        p.step_y = kScatterCoreH;
     } else {
         p.TX = pick_tx(p.GW);
         p.TY = kBM / p.TX;

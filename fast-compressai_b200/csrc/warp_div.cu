@@ -465,7 +465,7 @@ struct EncParams {
     uint32_t *max_rounds_out;
 };
 
-constexpr int kPrefetch = 8;  // symbols each lane loads ahead of the coding chain
+constexpr int kPrefetch = 16;  // symbols each lane loads ahead of the coding chain
 
 // Loads lane symbols t0 .. t0+7 (reverse order: position last - 32 t) of one
 // image row, with their indexes in kModeIdx; latent values as float bits.
