@@ -375,7 +375,7 @@ __device__ __forceinline__ void put_nibble(uint64_t &x, uint32_t val, LaneWriter
 }
 
 // Escape code of an out-of-range value (warp_ans_kernel_v2.cu:148-164).
-__device__ __forceinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter &w) {
+__device__ __forceinline__ void put_escape_inl(uint64_t &x, uint32_t raw, LaneWriter &w) {
     int n_bypass = raw ? (31 - __clz(raw)) / (int)kBypassBits + 1 : 0;
     for (int j = n_bypass - 1; j >= 0; --j) put_nibble(x, (raw >> (j * kBypassBits)) & kBypassMax, w);
     int rem = n_bypass, n_full = 0;
@@ -385,6 +385,23 @@ __device__ __forceinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter
     }
     put_nibble(x, (uint32_t)rem, w);
     for (int k = 0; k < n_full; ++k) put_nibble(x, kBypassMax, w);
+}
+
+// Out-of-line escape (rare path): state in and out by value, so the hot
+// loop keeps x and the writer in registers and stays small.
+struct EscOut {
+    uint64_t x;
+    int j;
+};
+__device__ __noinline__ EscOut put_escape_call(uint64_t x, uint32_t raw, uint32_t *rows, int cap, int j) {
+    LaneWriter w{rows, cap, j};
+    put_escape_inl(x, raw, w);
+    return EscOut{x, w.j};
+}
+__device__ __forceinline__ void put_escape(uint64_t &x, uint32_t raw, LaneWriter &w) {
+    const EscOut r = put_escape_call(x, raw, w.rows, w.cap, w.j);
+    x = r.x;
+    w.j = r.j;
 }
 
 // ---------------------------------------------------------------------------
@@ -832,7 +849,7 @@ __device__ __forceinline__ uint32_t get_nibble(uint64_t &x, LaneReader &rd) {
 
 // Escape decode (warp_ans_kernel.cu:308-325).  Returns false on a corrupt
 // count (the format never needs more than 8 nibbles).
-__device__ __forceinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
+__device__ __forceinline__ bool get_escape_inl(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
     uint32_t v = get_nibble(x, rd);
     uint32_t n_bypass = v;
     while (v == kBypassMax && !rd.bad) {
@@ -847,6 +864,27 @@ __device__ __forceinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t 
     else val = (int32_t)((uint32_t)val + (uint32_t)maxv);
     value = val;
     return true;
+}
+
+struct EscIn {
+    uint64_t x;
+    LaneReader rd;
+    int32_t value;
+    bool ok;
+};
+__device__ __noinline__ EscIn get_escape_call(uint64_t x, LaneReader rd, int32_t maxv) {
+    EscIn r;
+    r.ok = get_escape_inl(x, rd, maxv, r.value);
+    r.x = x;
+    r.rd = rd;
+    return r;
+}
+__device__ __forceinline__ bool get_escape(uint64_t &x, LaneReader &rd, int32_t maxv, int32_t &value) {
+    const EscIn r = get_escape_call(x, rd, maxv);
+    x = r.x;
+    rd = r.rd;
+    value = r.value;
+    return r.ok;
 }
 
 // Decodes one chunk: each lane reads its state, then its symbols first to
