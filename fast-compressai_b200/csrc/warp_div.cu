@@ -1247,6 +1247,33 @@ static int flags_to_status(long long flags, bool encode) {
     return FCAI_OK;
 }
 
+// Encode scratch of fcai_warp_div_encode_noalloc.  Module-scope __device__
+// storage exists once in each device's context from the moment this library's
+// module is loaded there, so that entry point needs no device allocation.
+// Every call on a device shares it (see the header on overlapping calls).
+constexpr int64_t kScratchBytes = FCAI_WARP_DIV_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_encode_scratch[kScratchBytes];
+
+static std::mutex g_scratch_mutex;
+static void *g_scratch_ptr[64];
+
+// Device address of g_encode_scratch on the current device: looked up once
+// per device, with that device current, and cached.
+static int encode_scratch(void **out) {
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fcai::fail(FCAI_ERR_CUDA, "device ordinal %d unsupported", dev);
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_ptr[dev]) {
+        void *ptr = nullptr;
+        FCAI_CUDA_TRY(cudaGetSymbolAddress((void **)&ptr, g_encode_scratch));
+        if (!ptr) return fcai::fail(FCAI_ERR_CUDA, "cudaGetSymbolAddress returned a null scratch address");
+        g_scratch_ptr[dev] = ptr;
+    }
+    *out = g_scratch_ptr[dev];
+    return FCAI_OK;
+}
+
 // Shared body of the encode entry points.
 static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes, const float *y,
                        const float *medians, int32_t B, int32_t N, const int32_t *cdfs, int32_t C, int32_t L,
@@ -1484,6 +1511,39 @@ int fcai_warp_div_encode_pack(const void *workspace, int64_t workspace_bytes, in
     pack_kernel<<<grid, kThreads, 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
+}
+
+int fcai_warp_div_encode_noalloc(const int32_t *symbols, const int32_t *indexes, int32_t B, int32_t N,
+                                 const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                                 const int32_t *offsets, int32_t P, uint8_t *packed, int64_t packed_capacity,
+                                 uint32_t *max_rounds, fcai_warp_div_encode_info *info, fcai_stream_t stream_) {
+    fcai::clear_error();
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    Dims d;
+    int rc = make_dims(B, N, C, P, d);
+    if (rc) return rc;
+    if (!packed || !info) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    // The worst-case workspace, so the staging can never overflow.
+    const int64_t need = enc_layout(d.chunks).fixed_bytes + d.chunks * rows_worst(d) * kLanes * 4;
+    if (need > kScratchBytes) {
+        info->required_workspace_bytes = need;
+        return fcai::fail(FCAI_ERR_WORKSPACE,
+                          "encode of %d x %d symbols (P_ch=%d) needs %lld workspace bytes, more than the %lld-byte "
+                          "static scratch of fcai_warp_div_encode_noalloc",
+                          (int)B, (int)N, (int)P, (long long)need, (long long)kScratchBytes);
+    }
+    void *scratch = nullptr;
+    if ((rc = encode_scratch(&scratch))) return rc;
+    // The array keeps the previous call's contents; the control block must
+    // start at zero (a call that stopped early may have left it set).
+    FCAI_CUDA_TRY(cudaMemsetAsync(scratch, 0, kCtrlBytes, stream));
+    rc = encode_impl(indexes ? kModeIdx : kModeChannel, symbols, indexes, nullptr, nullptr, B, N, cdfs, C, L,
+                     cdf_sizes, offsets, P, scratch, need, max_rounds, info, stream);
+    if (rc) return rc;
+    if (info->packed_bytes > packed_capacity)
+        return fcai::fail(FCAI_ERR_INVALID, "packed buffer of %lld bytes cannot hold the %lld-byte payload",
+                          (long long)packed_capacity, (long long)info->packed_bytes);
+    return fcai_warp_div_encode_pack(scratch, need, B, N, C, P, packed, info->packed_bytes, stream_);
 }
 
 int fcai_warp_div_decode(const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,

@@ -23,6 +23,10 @@ FCAI_ERR_CORRUPT = 6
 FCAI_ERR_WORKSPACE = 7
 FCAI_ERR_CUDA = 8
 
+# Size of the static device scratch of fcai_warp_div_encode_noalloc
+# (FCAI_WARP_DIV_SCRATCH_BYTES in include/fcai_warp_div.h).
+WARP_DIV_SCRATCH_BYTES = 16 * 1024 * 1024
+
 
 class NativeLibraryError(ImportError):
     """The native library is missing or failed to load."""
@@ -84,6 +88,10 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _I64, _P, _I32, _I64, _I32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P],
     ),
     "fcai_warp_div_encode_pack": (ctypes.c_int, [_P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P]),
+    "fcai_warp_div_encode_noalloc": (
+        ctypes.c_int,
+        [_P, _P, _I32, _I32, _P, _I32, _I32, _P, _P, _I32, _P, _I64, _P, ctypes.POINTER(WarpDivEncodeInfo), _P],
+    ),
     "fcai_layer_out_size": (ctypes.c_int, [_P, _I32, _I32, ctypes.POINTER(_I32), ctypes.POINTER(_I32)]),
     "fcai_layer_forward": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
     "fcai_nchw_f32_to_nhwc_bf16": (ctypes.c_int, [_P, _P, _I32, _I32, _I32, _I32, _P]),

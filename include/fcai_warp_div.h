@@ -136,6 +136,41 @@ int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B,
                                 void *workspace, int64_t workspace_bytes, uint32_t *max_rounds,
                                 fcai_warp_div_encode_info *info, fcai_stream_t stream);
 
+/* Encode without a caller workspace and without allocating: the work of
+ * fcai_warp_div_encode followed by fcai_warp_div_encode_pack, with the
+ * encode workspace taken from a static device array of
+ * FCAI_WARP_DIV_SCRATCH_BYTES (16 MiB) that this library holds on each
+ * device it runs on.  No counterpart in the reference, whose encode
+ * allocates its staging and payload tensors on every call.
+ *
+ * Meant for callers that cannot allocate device memory on the encode path:
+ * a host-language binding (cgo, JNI, ctypes) that holds device pointers but
+ * no device allocator of its own; a process whose device memory is already
+ * held by another allocator (a caching allocator that owns the GPU), where
+ * a cudaMalloc would fail; and a stream of queued work that a cudaMalloc or
+ * cudaFree would stall by synchronising the device.
+ *
+ * Limit: sizes whose worst-case workspace (plan.encode_workspace_bytes)
+ * exceeds FCAI_WARP_DIV_SCRATCH_BYTES are rejected with FCAI_ERR_WORKSPACE
+ * and info->required_workspace_bytes set; use fcai_warp_div_encode with a
+ * workspace of that size instead.  The payload goes to packed (device,
+ * packed_capacity bytes; plan.max_packed_bytes always suffices) and its
+ * size to info->packed_bytes; FCAI_ERR_INVALID if it does not fit.  Writes
+ * max_rounds[B*K] like fcai_warp_div_encode and blocks the host until the
+ * size is known; the payload write is then asynchronous on `stream`.
+ *
+ * All calls on a device share the one array, which keeps the previous
+ * call's contents; each call clears the part that must start at zero.
+ * Calls whose GPU work overlaps (issued on different streams, or from
+ * different threads, with nothing ordering them) race on the array and
+ * corrupt each other's payloads: issue them on one stream or serialise
+ * them. */
+#define FCAI_WARP_DIV_SCRATCH_BYTES (16 * 1024 * 1024)
+int fcai_warp_div_encode_noalloc(const int32_t *symbols, const int32_t *indexes, int32_t B, int32_t N,
+                                 const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                                 const int32_t *offsets, int32_t P, uint8_t *packed, int64_t packed_capacity,
+                                 uint32_t *max_rounds, fcai_warp_div_encode_info *info, fcai_stream_t stream);
+
 /* Decode straight to the fp32 dequantised latent y_hat = (float)symbol +
  * medians[c] (coders/factorized.py:90-101: decode, then
  * EntropyBottleneck.dequantize), channel layout. */
