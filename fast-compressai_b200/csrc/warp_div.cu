@@ -136,7 +136,7 @@ __device__ uint64_t g_magic[65537];
 
 __global__ void init_magic_kernel() {
     int f = blockIdx.x * blockDim.x + threadIdx.x;
-    if (f <= 65536) g_magic[f] = f >= 2 ? (~0ull) / (uint64_t)f : 0ull;
+    if (f <= 65536) g_magic[f] = f >= 1 ? (~0ull) / (uint64_t)f : 0ull;
 }
 
 // ---------------------------------------------------------------------------
@@ -323,7 +323,7 @@ __device__ void stage_group(const TableArgs &t, int c0, int nc, uint32_t *s_tab,
         s_tab[e] = ent;
         if (s_mag) {
             const uint32_t freq = (ent >> 16) + 1u;  // entries of valid rows have freq in [1, 65536]
-            s_mag[e] = freq >= 2 ? (~0ull) / (uint64_t)freq : 0ull;
+            s_mag[e] = (~0ull) / (uint64_t)freq;
         }
     }
     __syncthreads();
@@ -349,21 +349,16 @@ __device__ __forceinline__ void put_symbol(uint64_t &x, uint32_t start, uint32_t
         w.emit((uint32_t)x);
         x >>= 32;
     }
-    uint64_t q;
-    uint32_t r;
-    if (freq <= 1u) {
-        q = freq ? x : 0ull;
-        r = freq ? 0u : (uint32_t)x;
-    } else {
-        q = __umul64hi(x, magic);  // magic = floor((2^64 - 1) / freq): floor(x / freq) or one less
-        uint64_t rr = x - q * (uint64_t)freq;
-        if (rr >= freq) {
-            ++q;
-            rr -= freq;
-        }
-        r = (uint32_t)rr;
+    // magic = floor((2^64 - 1) / freq), freq in [1, 65536]: q is floor(x / freq)
+    // or one less (x < 2^63 after renormalisation), fixed by one correction.
+    // freq = 1 gives q = x - 1, corrected to x, r = 0.
+    uint64_t q = __umul64hi(x, magic);
+    uint64_t rr = x - q * (uint64_t)freq;
+    if (rr >= freq) {
+        ++q;
+        rr -= freq;
     }
-    x = (q << 16) + (uint64_t)(r + start);
+    x = (q << 16) + (uint64_t)((uint32_t)rr + start);
 }
 
 __device__ __forceinline__ void put_nibble(uint64_t &x, uint32_t val, LaneWriter &w) {
@@ -483,6 +478,7 @@ struct EncParams {
 };
 
 constexpr int kPrefetch = 16;  // symbols each lane loads ahead of the coding chain
+constexpr int kBatch = 8;      // symbols whose table lookups are issued together
 
 // Loads lane symbols t0 .. t0+7 (reverse order: position last - 32 t) of one
 // image row, with their indexes in kModeIdx; latent values as float bits.
@@ -529,43 +525,66 @@ __device__ __forceinline__ void encode_chunk(const EncParams &p, const Tab &tab,
             int32_t nxt[kPrefetch], inxt[kPrefetch];
             load_batch<kMode>(p, row0, last, t0 + kPrefetch, n, nxt, inxt);
 #pragma unroll
-            for (int u = 0; u < kPrefetch; ++u) {
-                if (t0 + u < n) {
+            for (int h = 0; h < kPrefetch; h += kBatch) {
+                // Phase A: everything that does not depend on the coder
+                // state, for kBatch symbols (their shared-memory reads are
+                // independent and overlap).
+                uint32_t ent[kBatch], raw[kBatch];
+                uint64_t mag[kBatch];
+                uint32_t esc = 0u;
+                const int nrem = n - (t0 + h);  // symbols left from this batch on (may be <= 0)
+                const int nb = min(kBatch, nrem);
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) {
                     int32_t s;
                     if (kMode == kModeLatent) {
                         // torch.round (half to even) then .int(), both in fp32
-                        s = __float2int_rz(rintf(__int_as_float(cur[u]) - tab.median(ct)));
+                        s = __float2int_rz(rintf(__int_as_float(cur[h + u]) - tab.median(ct)));
                     } else {
-                        s = cur[u];
+                        s = cur[h + u];
                     }
                     int c = ct;
                     if (kIdx) {
-                        const int32_t ci = icur[u];
-                        if (ci != ct) flags |= kFlagNonChannel;
-                        if ((unsigned)ci >= (unsigned)C) {
-                            flags |= kFlagIndexRange;
-                            c = 0;
-                        } else {
-                            c = ci;
+                        const int32_t ci = icur[h + u];
+                        if (u < nb) {
+                            if (ci != ct) flags |= kFlagNonChannel;
+                            if ((unsigned)ci >= (unsigned)C) flags |= kFlagIndexRange;
                         }
+                        c = (unsigned)ci < (unsigned)C ? ci : 0;
                     }
                     const int2 ch = tab.chan(c);
                     int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.x);
                     const int32_t maxv = ch.y;
-                    if (value < 0 || value >= maxv) {
-                        // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
-                        uint32_t raw = value < 0 ? 0u - 2u * (uint32_t)value - 1u
-                                                 : ((uint32_t)value - (uint32_t)maxv) * 2u;
-                        put_escape(x, raw, w);
-                        value = maxv;
+                    // negative: raw = -2v - 1; at/above max: raw = 2(v - max)
+                    raw[u] = value < 0 ? 0u - 2u * (uint32_t)value - 1u : ((uint32_t)value - (uint32_t)maxv) * 2u;
+                    const bool out_of_range = value < 0 || value >= maxv;
+                    if (out_of_range && u < nb) esc |= 1u << u;
+                    value = out_of_range ? maxv : value;
+                    uint32_t tf = 0u;
+                    ent[u] = tab.entry(c, value, u < nb ? flags : tf);
+                    mag[u] = tab.magic(c, value, (ent[u] >> 16) + 1u);
+                    // step to the next symbol's channel only when one follows,
+                    // so that ct always names a row this chunk stages
+                    if (u + 1 < nrem) {
+                        rem -= kLanes;
+                        while (rem < 0) {
+                            rem += p.HW;
+                            --ct;
+                        }
                     }
-                    const uint32_t e = tab.entry(c, value, flags);
-                    const uint32_t freq = (e >> 16) + 1u;
-                    put_symbol(x, e & 0xFFFFu, freq, tab.magic(c, value, freq), w);
-                    rem -= kLanes;
-                    while (rem < 0) {
-                        rem += p.HW;
-                        --ct;
+                }
+                // Phase B: the coder chain.
+                if (nb >= kBatch && esc == 0u) {
+#pragma unroll
+                    for (int u = 0; u < kBatch; ++u)
+                        put_symbol(x, ent[u] & 0xFFFFu, (ent[u] >> 16) + 1u, mag[u], w);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < kBatch; ++u) {
+                        if (u < nb) {
+                            if ((esc >> u) & 1u) put_escape(x, raw[u], w);
+                            put_symbol(x, ent[u] & 0xFFFFu, (ent[u] >> 16) + 1u, mag[u], w);
+                        }
                     }
                 }
             }
@@ -811,31 +830,43 @@ struct DecParams {
     int32_t *__restrict__ out;
 };
 
-// The lane's words in decode order, read through a 4-deep look-ahead queue
-// so that a renormalisation never waits on a global load: consuming word k
-// issues the load of word k + 4.
+// The lane's words in decode order, read four at a time: r0..r3 hold words
+// 4m .. 4m+3 (loaded), f0..f3 words 4m+4 .. 4m+7 (in flight).  Consuming the
+// last ready word moves the in-flight quad in and issues the next one, so a
+// register move only ever waits on loads issued four refills earlier.
 struct LaneReader {
     const uint32_t *__restrict__ base;  // chunk body + lane
-    int word, rounds;                   // index of the word q0 holds
+    int word, rounds;                   // index of the next word
     bool bad;
-    uint32_t q0, q1, q2, q3;
+    uint32_t r0, r1, r2, r3, f0, f1, f2, f3;
     __device__ __forceinline__ uint32_t fetch(int j) const {
         return j < rounds ? __ldg(base + (int64_t)j * kLanes) : 0u;
     }
     __device__ __forceinline__ void start() {
-        q0 = fetch(0);
-        q1 = fetch(1);
-        q2 = fetch(2);
-        q3 = fetch(3);
+        r0 = fetch(0);
+        r1 = fetch(1);
+        r2 = fetch(2);
+        r3 = fetch(3);
+        f0 = fetch(4);
+        f1 = fetch(5);
+        f2 = fetch(6);
+        f3 = fetch(7);
     }
     __device__ __forceinline__ uint32_t next() {
-        const uint32_t v = q0;
         if (word >= rounds) bad = true;
-        q0 = q1;
-        q1 = q2;
-        q2 = q3;
-        q3 = fetch(word + 4);
+        const int k = word & 3;
+        const uint32_t v = k == 0 ? r0 : k == 1 ? r1 : k == 2 ? r2 : r3;
         ++word;
+        if (k == 3) {
+            r0 = f0;
+            r1 = f1;
+            r2 = f2;
+            r3 = f3;
+            f0 = fetch(word + 4);
+            f1 = fetch(word + 5);
+            f2 = fetch(word + 6);
+            f3 = fetch(word + 7);
+        }
         return v;
     }
 };
@@ -903,7 +934,7 @@ __device__ __forceinline__ void decode_chunk(const DecParams &p, const Tab &tab,
     const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
     const int first = start + lane;
     if (first >= end) return;
-    LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u};
+    LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
     rd.start();
     uint64_t x = (uint64_t)rd.next();
     x |= (uint64_t)rd.next() << 32;
