@@ -52,6 +52,12 @@ def parse_args(argv=None):
     ap.add_argument("--transforms", choices=("bf16", "fp32"), default="bf16")
     ap.add_argument("--cpu-sample", type=int, default=1, help="images in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-images", type=int, default=4,
+                    help="images per upload / download chunk of the end-to-end (host buffers) measurement")
+    ap.add_argument("--ans-sweep", action="store_true",
+                    help="BASELINE config 3 instead: the coder alone on 64 x 192 x 32 x 48 Laplacian symbols, "
+                         "P in {1, 2, 4, 8, 16, 48, 192}")
+    ap.add_argument("--sweep-p", type=str, default="1,2,4,8,16,48,192")
     return ap.parse_args(argv)
 
 
@@ -174,24 +180,69 @@ def run_reference(args):
 # clocks during the timed region
 # --------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU, sampled through NVML every
+    2 ms on a background thread while the timed region runs (read-only
+    queries; one sample is also taken at start and at stop, so even a short
+    region has some).  Falls back to ``nvidia-smi -lms`` when NVML is absent."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index):
+    def __init__(self, device_index, period_s=0.002):
+        import threading
+
         import torch
 
-        self.proc = None
+        self.samples, self.reason_bits, self.smax = [], 0, None
+        self.proc = self.thread = None
+        uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        self.ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
         try:
-            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
-            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(self.ident.encode())
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.stop_flag = threading.Event()
+            self._sample()
+            self.thread = threading.Thread(target=self._loop, args=(period_s,), daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.nvml = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                     "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self.proc = None
+
+    def _sample(self):
+        n = self.nvml
+        self.samples.append(float(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)))
+        try:
+            self.reason_bits |= int(n.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        except AttributeError:
+            self.reason_bits |= int(n.nvmlDeviceGetCurrentClocksThrottleReasons(self.handle))
+
+    def _loop(self, period_s):
+        while not self.stop_flag.wait(period_s):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag.set()
+            self.thread.join()
+            self._sample()
+            reasons = sorted(name for bit, name in self.REASONS.items() if self.reason_bits & bit)
+            return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.smax, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 2 ms period"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -215,7 +266,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 20 ms period"}
 
 
 # --------------------------------------------------------------------------
@@ -234,9 +285,10 @@ def read_traffic():
     out = {}
     if path.exists():
         for line in path.read_text().splitlines():
-            if line.startswith("#") or "=" not in line:
+            line = line.split("#", 1)[0]
+            if "=" not in line:
                 continue
-            parts = dict(kv.split("=", 1) for kv in line.split())
+            parts = dict(kv.split("=", 1) for kv in line.split() if "=" in kv)
             if "layer" in parts and "dram_bytes_per_launch_b24" in parts:
                 out[parts["layer"]] = float(parts["dram_bytes_per_launch_b24"])
     return out
@@ -247,7 +299,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     import fast_compressai
-    from fast_compressai import _native, transforms
+    from fast_compressai import _native, sharding, transforms
     from fast_compressai.coders import WarpDivPayload
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -322,8 +374,8 @@ def run_b200(args):
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            xd = x_host.to(dev, non_blocking=True)
-            out = fast.compress(xd)
+            # upload overlapped with g_a, one payload for the batch
+            out = fast.compress_host(x_host, chunk_images=args.chunk_images)
             p = out["strings"][0]
             n = p.packed.numel()
             if n > packed_host.numel():
@@ -334,14 +386,14 @@ def run_b200(args):
                                                 cdf_count=p.cdf_count, p_ch=p.p_ch, chunk_len=p.chunk_len,
                                                 header_bytes=p.header_bytes, coding_fingerprint=p.coding_fingerprint,
                                                 device=dev)
-            xh = fast.decompress([q], out["shape"])["x_hat"]
-            xhat_host.copy_(xh, non_blocking=True)
+            # download of each reconstructed chunk overlapped with the next chunk's g_s
+            xh = fast.decompress_host([q], out["shape"], xhat_host, chunk_images=args.chunk_images)["x_hat"]
             e1.record()
             torch.cuda.synchronize()
             if i >= args.warmup:
                 e2e_ms.append(e0.elapsed_time(e1))
                 h2d = in_bytes + n + p.max_rounds.numel() * 4
-                d2h = n + xh.numel() * 4
+                d2h = n + xh.numel() * xh.element_size()
         t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -383,13 +435,8 @@ def run_b200(args):
         psnr_drop = psnr(x_ref, xs) - psnr(x_hat[:nq], xs)
 
     # ---- payload-size gather (the only collective of the path) --------------
-    sizes = torch.tensor([packed_bytes], dtype=torch.int64, device=dev)
-    if world > 1:
-        gathered = [torch.zeros_like(sizes) for _ in range(world)]
-        dist.all_gather(gathered, sizes)
-        total_payload = int(sum(int(g) for g in gathered))
-    else:
-        total_payload = packed_bytes
+    gathered = sharding.gather_payload_stats(sharding.payload_stats(payload), device=dev)
+    total_payload = gathered["packed_bytes"]
 
     # ---- roofline of the dominant kernel ------------------------------------
     per_layer = {}
@@ -481,10 +528,79 @@ def run_b200(args):
     return 0
 
 
+def run_ans_sweep(args):
+    """encode / decode of int32 symbols [64, 192*32*48] (channel layout, as the codec
+    calls it, and with explicit indexes, as WarpDivBackend.encode is called), per P.  Times are host-call
+    times with CUDA events (launches, the encode's size read-back and the decode's check included), L2
+    flushed before each call; GB/s counts 4 B per symbol plus the payload bytes (read + write)."""
+    import numpy as np
+    import torch
+
+    from fast_compressai.coders import _warp_div as ext
+    from tests.coder_inputs import channel_indexes, laplacian_symbols, laplacian_tables
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    B, C, HW = 64, 192, 32 * 48
+    cdfs, sizes, offs, scales = laplacian_tables(C, seed=0)
+    sym = torch.from_numpy(laplacian_symbols(B, C, HW, scales, seed=0)).to(dev)
+    idx = torch.from_numpy(channel_indexes(B, C, HW)).to(dev)
+    cd, sz, of = (torch.from_numpy(a).to(dev) for a in (cdfs, sizes, offs))
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    hbm = read_peaks().get("hbm_gbs", 6650.0)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    rows = []
+    for P in (int(v) for v in args.sweep_p.split(",")):
+        r = ext.encode(sym, None, cd, sz, of, P)
+        dec = ext.decode(r.packed, r.max_rounds, r.header_bytes, r.chunk_len, None, cd, sz, of, batch=B,
+                         symbols_per_batch=C * HW)
+        torch.cuda.synchronize()
+        if not torch.equal(dec, sym):
+            raise SystemExit(f"round trip failed at P={P}")
+        nbytes = sym.numel() * 4 + r.packed.numel()
+        enc = timed(lambda: ext.encode(sym, None, cd, sz, of, P))
+        enc_i = timed(lambda: ext.encode(sym, idx, cd, sz, of, P))
+        dcm = timed(lambda: ext.decode(r.packed, r.max_rounds, r.header_bytes, r.chunk_len, None, cd, sz, of,
+                                       batch=B, symbols_per_batch=C * HW))
+        dci = timed(lambda: ext.decode(r.packed, r.max_rounds, r.header_bytes, r.chunk_len, idx, cd, sz, of))
+        rows.append({"p_ch": P, "chunks": int(r.max_rounds.numel()), "payload_bytes": int(r.packed.numel()),
+                     "bits_per_symbol": r.packed.numel() * 8 / sym.numel(),
+                     "encode_ms": enc, "encode_indexes_ms": enc_i, "decode_ms": dcm, "decode_indexes_ms": dci,
+                     "encode_gbs": nbytes / enc / 1e6, "decode_gbs": nbytes / dcm / 1e6,
+                     "encode_frac": nbytes / enc / 1e6 / hbm, "decode_frac": nbytes / dcm / 1e6 / hbm})
+    line = {
+        "metric": "warp_div encode / decode GB/s (int32 symbols + payload bytes), BASELINE config 3",
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "int32", "data": "synthetic: seeded discretised-Laplacian symbols and 16-bit CDFs (config 3)",
+        "config": {"workload": "ANS sweep", "symbols": [B, C * HW], "l2": "flushed before each call (256 MB write)"},
+        "hbm_peak_gbs": hbm, "sweep": rows,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.ans_sweep:
+        return run_ans_sweep(args)
     return run_b200(args)
 
 

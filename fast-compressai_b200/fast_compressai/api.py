@@ -227,6 +227,20 @@ class FastModel(nn.Module):
             return coder.decompress(*args, **kwargs)
         return self.model.decompress(*args, **kwargs)
 
+    def compress_host(self, x, **kwargs: Any) -> Any:
+        """compress() of a host batch, its upload overlapped with g_a (warp_div coder only)."""
+        return self._host_coder("compress_host").compress_host(x, **kwargs)
+
+    def decompress_host(self, strings, shape, out=None, **kwargs: Any) -> Any:
+        """decompress() into host memory, the download overlapped with g_s (warp_div coder only)."""
+        return self._host_coder("decompress_host").decompress_host(strings, shape, out, **kwargs)
+
+    def _host_coder(self, name: str):
+        coder = self.__dict__.get("_coder")
+        if coder is None or not hasattr(coder, name):
+            raise ConfigurationError(f"{name} needs a model accelerated with coder='warp_div'")
+        return coder
+
     def update(self, *args: Any, **kwargs: Any) -> Any:
         result = self.model.update(*args, **kwargs)
         self._report = replace(self._report, update_called=True)

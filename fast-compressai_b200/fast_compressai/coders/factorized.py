@@ -21,6 +21,23 @@ import torch
 from .errors import CoderInputError
 from .warp_div import WarpDivBackend, WarpDivPayload
 
+# One copy stream per device for the host-batch entry points.
+_COPY_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _copy_stream(device: torch.device) -> torch.cuda.Stream:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    stream = _COPY_STREAMS.get(index)
+    if stream is None:
+        stream = _COPY_STREAMS[index] = torch.cuda.Stream(device=index)
+    return stream
+
+
+def _chunks(batch: int, chunk_images: int):
+    if chunk_images <= 0:
+        raise CoderInputError("chunk_images must be positive")
+    return [(i, min(i + chunk_images, batch)) for i in range(0, batch, chunk_images)]
+
 
 class FactorizedWarpDivCodec:
     """Keep Balle's transforms and quantiser; code the latent with warp_div."""
@@ -75,7 +92,79 @@ class FactorizedWarpDivCodec:
                 timing["compress_codec_ms"] = float(start.elapsed_time(end))
             return {"strings": [payload], "shape": tuple(y.shape[-2:])}
 
-    def decompress(self, strings, shape, timing: dict[str, float] | None = None):
+    def _device(self) -> torch.device:
+        return self.model.entropy_bottleneck._quantized_cdf.device
+
+    def compress_host(self, x: torch.Tensor, *, chunk_images: int = 4):
+        """``compress`` of a batch held in host memory.
+
+        The batch is uploaded in chunks of ``chunk_images`` images on a copy
+        stream while g_a runs on the chunks already on the device (the
+        transforms treat images independently), then the whole latent is
+        coded as one payload, so the result is the payload of
+        ``compress(x.cuda())``.  The upload only overlaps the transform when
+        ``x`` is in pinned memory.
+        """
+        if not isinstance(x, torch.Tensor) or x.device.type != "cpu" or x.ndim != 4:
+            raise CoderInputError("compress_host expects a host (CPU) NCHW tensor")
+        dev = self._device()
+        with torch.no_grad(), torch.cuda.device(dev):
+            compute = torch.cuda.current_stream(dev)
+            copy = _copy_stream(dev)
+            x = x.float().contiguous()
+            x_dev = torch.empty(x.shape, dtype=torch.float32, device=dev)
+            copy.wait_stream(compute)  # x_dev's memory is free for the copies
+            parts = []
+            for i0, i1 in _chunks(x.shape[0], chunk_images):
+                with torch.cuda.stream(copy):
+                    x_dev[i0:i1].copy_(x[i0:i1], non_blocking=True)
+                    uploaded = torch.cuda.Event()
+                    uploaded.record(copy)
+                compute.wait_event(uploaded)
+                parts.append(self.model.g_a(x_dev[i0:i1]))
+            x_dev.record_stream(copy)
+            y = parts[0] if len(parts) == 1 else torch.cat(parts)
+            entropy = self.model.entropy_bottleneck
+            if y.size(1) != entropy.channels:
+                raise CoderInputError("latent channel count does not match entropy bottleneck")
+            cdfs, lengths, offsets = self._tables(entropy)
+            payload = self.backend._encode_latent(y.float().contiguous(), self._medians(entropy), cdfs, lengths,
+                                                  offsets, self.p_ch)
+            return {"strings": [payload], "shape": tuple(y.shape[-2:])}
+
+    def decompress_host(self, strings, shape, out: torch.Tensor | None = None, *, chunk_images: int = 4):
+        """``decompress`` into host memory.
+
+        The latent is decoded at once; g_s then runs in chunks of
+        ``chunk_images`` images and each chunk's reconstruction is copied to
+        ``out`` (a pinned host tensor [B, 3, H, W], allocated if None) on a
+        copy stream while the next chunk is synthesised.  The copies are
+        ordered before later work on the current stream: synchronise it (or
+        the device) before reading ``out``.
+        """
+        y_hat = self._decode_latent(strings, shape)
+        dev = y_hat.device
+        with torch.no_grad(), torch.cuda.device(dev):
+            compute = torch.cuda.current_stream(dev)
+            copy = _copy_stream(dev)
+            g_s = self.model.g_s
+            fused = getattr(g_s, "fuses_clamp", False)
+            for i0, i1 in _chunks(y_hat.shape[0], chunk_images):
+                part = g_s(y_hat[i0:i1], clamp=True) if fused else g_s(y_hat[i0:i1]).clamp_(0, 1)
+                if out is None:
+                    out = torch.empty((y_hat.shape[0], *part.shape[1:]), dtype=part.dtype, pin_memory=True)
+                elif out.device.type != "cpu" or out.shape[0] != y_hat.shape[0] or out.shape[1:] != part.shape[1:]:
+                    raise CoderInputError("out must be a host tensor of the reconstruction's shape")
+                done = torch.cuda.Event()
+                done.record(compute)
+                with torch.cuda.stream(copy):
+                    copy.wait_event(done)
+                    out[i0:i1].copy_(part, non_blocking=True)
+                part.record_stream(copy)
+            compute.wait_stream(copy)
+            return {"x_hat": out}
+
+    def _decode_latent(self, strings, shape) -> torch.Tensor:
         if (not isinstance(strings, (list, tuple)) or len(strings) != 1
                 or not isinstance(strings[0], WarpDivPayload)):
             raise CoderInputError("warp_div decompress expects strings=[WarpDivPayload]")
@@ -93,13 +182,18 @@ class FactorizedWarpDivCodec:
         if payload.packed.device != cdfs.device:
             raise CoderInputError("payload and entropy model must be on the same CUDA device")
         with torch.no_grad():
+            medians = self._medians(entropy)
+            y_hat = torch.empty((payload.batch, channels, *shape), dtype=medians.dtype, device=cdfs.device)
+            self.backend._decode_latent(payload, cdfs, lengths, offsets, medians, y_hat)
+        return y_hat
+
+    def decompress(self, strings, shape, timing: dict[str, float] | None = None):
+        with torch.no_grad():
             start = torch.cuda.Event(enable_timing=True) if timing is not None else None
             end = torch.cuda.Event(enable_timing=True) if timing is not None else None
             if timing is not None:
                 start.record()
-            medians = self._medians(entropy)
-            y_hat = torch.empty((payload.batch, channels, *shape), dtype=medians.dtype, device=cdfs.device)
-            self.backend._decode_latent(payload, cdfs, lengths, offsets, medians, y_hat)
+            y_hat = self._decode_latent(strings, shape)
             if timing is not None:
                 end.record()
                 end.synchronize()

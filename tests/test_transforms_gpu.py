@@ -18,6 +18,7 @@ import torch.nn.functional as F
 
 from fast_compressai import accelerate
 from fast_compressai.balle import GDN, FactorizedPrior
+from fast_compressai.coders.errors import CoderInputError
 from fast_compressai.transforms import (
     FCAI_FMT_NHWC_BF16,
     B200Analysis,
@@ -178,3 +179,41 @@ def test_accelerate_bf16_end_to_end(cuda_device):
     assert _psnr(x_hat, x_ref) > 25.0, _psnr(x_hat, x_ref)
     drop = _psnr(x_ref, x) - _psnr(x_hat, x)
     assert drop <= 0.1, drop
+
+
+@pytest.mark.parametrize("transforms", ["bf16", "fp32"])
+def test_host_batch_entry_points_match_device_ones(cuda_device, transforms):
+    # compress_host / decompress_host overlap the PCIe copies with the
+    # transforms chunk by chunk (ragged last chunk included).  The B200
+    # kernels compute every image the same way whatever the batch, so with
+    # bf16 transforms payload and reconstruction are those of compress /
+    # decompress on the device bit for bit; cuDNN (fp32) may pick another
+    # algorithm for a smaller batch, so there they agree within rounding.
+    torch.manual_seed(0)
+    model = FactorizedPrior(128, 192).to(cuda_device).eval()
+    model.update(force=True)
+    x = _smooth_images(5, 64, 96, "cpu", seed=7).pin_memory()
+    fast = accelerate(model, P=4, device="cuda:0", transforms=transforms)
+    exact = transforms == "bf16"
+    with torch.inference_mode():
+        ref = fast.compress(x.to(cuda_device))
+        x_ref = fast.decompress(ref["strings"], ref["shape"])["x_hat"]
+        out = fast.compress_host(x, chunk_images=2)
+        assert out["shape"] == ref["shape"]
+        if exact:
+            assert torch.equal(out["strings"][0].packed, ref["strings"][0].packed)
+        x_dev = fast.decompress(out["strings"], out["shape"])["x_hat"]
+        host = torch.empty(x_ref.shape, dtype=x_ref.dtype).pin_memory()
+        res = fast.decompress_host(out["strings"], out["shape"], host, chunk_images=2)
+        torch.cuda.synchronize()
+        assert res["x_hat"] is host
+        fresh = fast.decompress_host(out["strings"], out["shape"], chunk_images=3)["x_hat"]
+        torch.cuda.synchronize()
+        assert fresh.device.type == "cpu"
+        for got in (host, fresh):
+            if exact:
+                assert torch.equal(got, x_dev.cpu()) and torch.equal(got, x_ref.cpu())
+            else:
+                torch.testing.assert_close(got, x_dev.cpu(), atol=1e-4, rtol=0)
+    with pytest.raises(CoderInputError):
+        fast.compress_host(x.to(cuda_device))
