@@ -50,7 +50,8 @@ using namespace tcx;
 
 constexpr int kBM = 128;          // output pixels per tile (MMA M)
 constexpr int kBK = 64;           // bf16 per K block: one 128-byte row
-constexpr int kStages = 4;
+constexpr int kSmemBudget = 227 * 1024;  // dynamic shared memory per CTA
+constexpr int kMaxStages = 8;
 constexpr int kEpiWarps = 8;      // warps 0-7: two per TMEM lane quarter, one per column half
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kProducerWarp = 8;
@@ -61,6 +62,11 @@ constexpr int kGatherThreads = 128;
 // produces a 12 x 28 output block; cout = 3 (25 taps x 3 = 75 -> npad 80)
 constexpr int kScatterTY = 8, kScatterTX = 16, kScatterCoreH = 6, kScatterCoreW = 14, kScatterCout = 3;
 constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
+// First layer, patch path: the tile's fp32 input window (3 channels x
+// (2 TY + 3) rows x (2 TX + 8) columns, TX <= 64) arrives by one TMA load
+// into one of two patch buffers.
+constexpr int kPatchBuf = 11520;     // >= (2 TX + 8) * (2 TY + 3) * 3 * 4 for TX in {8, 16, 32, 64}, 128-aligned
+constexpr int kPatchMaxTX = 64;
 constexpr uint64_t kWaitNs = 1000000000ull;
 
 enum Epi : int { kEpiBf16 = 0, kEpiGdn = 1, kEpiIgdn = 2, kEpiF32 = 3, kEpiF32Clamp = 4, kEpiScatter = 5 };
@@ -88,6 +94,9 @@ struct ConvParams {
     const float *beta;
     const float *x_in;   // first layer: fp32 NCHW [B, 3, Hin, Win]
     const void *wgather; // first layer: packed weight image
+    int patch_tma;       // first layer: 1 = input windows by TMA (tmA maps x_in), 0 = direct loads
+    int patch_w, patch_h;  // patch box: columns (2 TX + 8), rows (2 TY + 3)
+    uint32_t patch_bytes;
     void *out;
     int *err;
 };
@@ -103,14 +112,24 @@ struct Layout {
     static constexpr int kX2 = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
     static constexpr int kS = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
+    // operand ring: as many stages as the shared memory left over holds
+    // (more bytes in flight hide more of the TMA round trip)
+    static constexpr int kFixedBytes = kNpad * kGatherK * 2 * (kGather ? 1 : 0) + (kNorm ? 2 * kNpad * kNpad * 2 : 0) +
+                                       (kEpi == kEpiScatter ? kBM * (kNpad + 1) * 4 : 0) + (kGather ? 2 * kPatchBuf : 0) +
+                                       2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
+    static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
+    static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
     static constexpr int offW = kStages * kStage;
     static constexpr int offG = offW + kW;
     static constexpr int offX2 = offG + kG;
     static constexpr int offS = offX2 + kX2;
-    static constexpr int offBias = offS + kS;
+    static constexpr int kP = kGather ? 2 * kPatchBuf : 0;
+    static constexpr int offPatch = offS + kS;
+    static constexpr int offBias = offPatch + kP;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
-    static constexpr int kBars = 2 * kStages + 7;
+    static constexpr int kBars = 2 * kStages + 7 + (kGather ? 4 : 0);
+    static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
     static constexpr int kBytes = offSlot + 32;
     static constexpr int kAlloc = kBytes + 1024;  // base alignment slack
@@ -119,6 +138,7 @@ struct Layout {
     static constexpr int kSplit = kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
     static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
+    static_assert(offPatch % 128 == 0 && kPatchBuf % 128 == 0, "patch buffer alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
@@ -160,12 +180,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Lay::offBar);
     uint64_t *full = bars;
+    constexpr int kStages = Lay::kStages;
     uint64_t *empty = bars + kStages;
     uint64_t *accf = bars + 2 * kStages;
     uint64_t *acce = accf + 2;
     uint64_t *g2bar = acce + 2;
     uint64_t *cbar = g2bar + 1;
     uint64_t *dbar = cbar + 1;  // abort path: drains this CTA's MMAs
+    uint64_t *pfull = dbar + 1;   // first layer: patch buffer loaded (2)
+    uint64_t *pempty = pfull + 2; // first layer: patch buffer read by all gather threads (2)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::offSlot);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 4);
     volatile int *epi_ok = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 8);
@@ -187,6 +210,12 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         mbar_init(g2bar, 1);
         mbar_init(cbar, 1);
         mbar_init(dbar, 2);
+        if (kGather) {
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&pfull[b], 1);
+                mbar_init(&pempty[b], kGatherThreads);
+            }
+        }
         *abort = 0;
         fence_barrier_init();
     }
@@ -209,6 +238,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
             if (!kGather) {
                 tma_prefetch_desc(&tmA);
                 tma_prefetch_desc(&tmW);
+            } else if (p.patch_tma) {
+                tma_prefetch_desc(&tmA);
             }
             // one-time operands: gamma (GDN) and the first layer's weights
             uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
@@ -250,6 +281,33 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                     // let this CTA's loads in flight land before the CTA exits
                     for (int s = 0; s < kStages; ++s)
                         if (last_round[s] >= 0) mbar_wait(&full[s], (uint32_t)last_round[s] & 1, nullptr, kWaitNs / 10);
+                }
+            }
+            if (kGather && p.patch_tma) {
+                // input windows: patch buffer it % 2 for the CTA's it-th tile
+                uint32_t it = 0;
+                int last_round[2] = {-1, -1};
+                for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
+                    int b, ph, gy0, gx0;
+                    tile_coords(p, tile, b, ph, gy0, gx0);
+                    const int pb = it & 1;
+                    const uint32_t r = it >> 1;
+                    if (!mbar_wait(&pempty[pb], (r & 1) ^ 1, abort, kWaitNs)) {
+                        fail(p, abort, kErrProducer);
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&pfull[pb], p.patch_bytes);
+                    // x starts 4 columns left of the window's first input column
+                    // (2 gx0 - 2): a multiple of 4 floats, as TMA requires; the
+                    // rows above / columns left of the image read as zeros
+                    tma_load_4d(smem + Lay::offPatch + pb * kPatchBuf, &tmA, &pfull[pb], 2 * gx0 - 4, 2 * gy0 - 2, 0,
+                                b);
+                    last_round[pb] = (int)r;
+                }
+                if (*abort) {
+                    for (int pb = 0; pb < 2; ++pb)
+                        if (last_round[pb] >= 0)
+                            mbar_wait(&pfull[pb], (uint32_t)last_round[pb] & 1, nullptr, kWaitNs / 10);
                 }
             }
             if (cbytes && *abort) mbar_wait(cbar, 0, nullptr, kWaitNs / 10);
@@ -532,10 +590,47 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 fail(p, abort, kErrGather);
                 break;
             }
+            const uint32_t a0 = smem_u32(smem + s * Lay::kStage) + row_off;
+            if (p.patch_tma) {
+                const int pb = it & 1;
+                if (!mbar_wait(&pfull[pb], (it >> 1) & 1, abort, kWaitNs)) {
+                    fail(p, abort, kErrGather);
+                    break;
+                }
+                // pixel (ty, tx) of the tile reads patch rows 2 ty + ky and
+                // columns 2 tx + 2 + kx (the patch starts 2 rows above and 4
+                // columns left of the tile's first output pixel's centre)
+                const int ty = m / p.TX, tx = m - (m / p.TX) * p.TX;
+                const float *pt = reinterpret_cast<const float *>(smem + Lay::offPatch + pb * kPatchBuf) +
+                                  (2 * ty) * p.patch_w + 2 * tx + 2;
+                float f[kGatherK];
+#pragma unroll
+                for (int ci = 0; ci < 3; ++ci) {
+#pragma unroll
+                    for (int ky = 0; ky < 5; ++ky) {
+                        const float *q = pt + (ci * p.patch_h + ky) * p.patch_w;
+                        const float2 v01 = *reinterpret_cast<const float2 *>(q);
+                        const float2 v23 = *reinterpret_cast<const float2 *>(q + 2);
+                        const int k = ci * 25 + ky * 5;
+                        f[k] = v01.x;
+                        f[k + 1] = v01.y;
+                        f[k + 2] = v23.x;
+                        f[k + 3] = v23.y;
+                        f[k + 4] = q[4];
+                    }
+                }
+#pragma unroll
+                for (int k = 75; k < kGatherK; ++k) f[k] = 0.f;
+#pragma unroll
+                for (int kc = 0; kc < kGatherK / 8; ++kc)
+                    st_shared_v4(a0 + kc * 128, pack_bf16x2(f[kc * 8], f[kc * 8 + 1]),
+                                 pack_bf16x2(f[kc * 8 + 2], f[kc * 8 + 3]), pack_bf16x2(f[kc * 8 + 4], f[kc * 8 + 5]),
+                                 pack_bf16x2(f[kc * 8 + 6], f[kc * 8 + 7]));
+                mbar_arrive(&pempty[pb]);  // this thread has read the window
+            } else {
             const int gy = gy0 + m / p.TX, gx = gx0 + m % p.TX;
             const bool valid = gy < p.GH && gx < p.GW;
             const float *img = p.x_in + (int64_t)b * 3 * p.Hin * p.Win;
-            const uint32_t a0 = smem_u32(smem + s * Lay::kStage) + row_off;
 #pragma unroll
             for (int kc = 0; kc < kGatherK / 8; ++kc) {
                 float f[8];
@@ -552,6 +647,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 }
                 st_shared_v4(a0 + kc * 128, pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
                              pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+            }
             }
             fence_proxy_async_smem();
             mbar_arrive(&full[s]);
@@ -591,21 +687,24 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// bf16 operand tiles, 128-byte swizzled; fp32 = the first layer's unswizzled
+// input windows.  Out-of-bounds elements read as zero.
 static int make_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
-                    const cuuint32_t *box, const cuuint32_t *estrides) {
+                    const cuuint32_t *box, const cuuint32_t *estrides, bool fp32 = false) {
     auto fn = encode_fn();
     if (!fn) return fcai::fail(FCAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(base), dims, strides, box, estrides,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+                    const_cast<void *>(base), dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    fp32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fcai::fail(FCAI_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return FCAI_OK;
 }
 
-// Largest power-of-two tile width (<= 128) that wastes the fewest columns.
-static int pick_tx(int gw) {
+// Largest power-of-two tile width (<= max_tx) that wastes the fewest columns.
+static int pick_tx(int gw, int max_tx = 128) {
     int best = 8, waste_best = 1 << 30;
-    for (int tx = 8; tx <= 128; tx <<= 1) {
+    for (int tx = 8; tx <= max_tx; tx <<= 1) {
         int waste = ((gw + tx - 1) / tx) * tx - gw;
         if (waste < waste_best || (waste == waste_best && tx > best)) {
             best = tx;
@@ -619,6 +718,7 @@ template <int kNpad, int kEpi, bool kGather>
 static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const ConvParams &p,
                   cudaStream_t stream) {
     using Lay = Layout<kNpad, kEpi, kGather>;
+    static_assert(Lay::kAlloc <= kSmemBudget, "shared memory");
     auto kernel = conv_tc_kernel<kNpad, kEpi, kGather>;
     static int configured[64] = {0};
     int dev = 0;
@@ -747,10 +847,21 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         p.step_x = kScatterCoreW;
         p.step_y = kScatterCoreH;
     } else {
-        p.TX = pick_tx(p.GW);
+        // the first layer's input windows come by TMA when the fp32 image
+        // allows it: rows a multiple of 16 bytes, base 16-byte aligned
+        const bool patch = gather && w_in % 4 == 0 && (reinterpret_cast<uintptr_t>(input) & 15) == 0;
+        p.TX = pick_tx(p.GW, patch ? kPatchMaxTX : 128);
         p.TY = kBM / p.TX;
         p.step_x = p.TX;
         p.step_y = p.TY;
+        if (patch) {
+            p.patch_tma = 1;
+            p.patch_w = 2 * p.TX + 8;
+            p.patch_h = 2 * p.TY + 3;
+            p.patch_bytes = (uint32_t)(p.patch_w * p.patch_h * 3 * 4);
+            if (p.patch_bytes > (uint32_t)kPatchBuf || p.patch_w > 256 || p.patch_h > 256)
+                return fcai::fail(FCAI_ERR_INVALID, "first-layer input window exceeds its buffer");
+        }
     }
     p.clamp = L->clamp01 ? 1 : 0;
     p.tiles_x = (p.GW + p.step_x - 1) / p.step_x;
@@ -810,6 +921,14 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.err = err;
 
     CUtensorMap ma{}, mw{}, mg{};
+    if (gather && p.patch_tma) {
+        // fp32 NCHW image as [B][3][Hin][Win]; one box = one tile's window
+        cuuint64_t dims[4] = {(cuuint64_t)w_in, (cuuint64_t)h_in, 3, (cuuint64_t)batch};
+        cuuint64_t strides[3] = {(cuuint64_t)w_in * 4, (cuuint64_t)h_in * w_in * 4, (cuuint64_t)3 * h_in * w_in * 4};
+        cuuint32_t box[4] = {(cuuint32_t)p.patch_w, (cuuint32_t)p.patch_h, 3, 1};
+        cuuint32_t es[4] = {1, 1, 1, 1};
+        if ((rc = make_map(&ma, input, 4, dims, strides, box, es, true))) return rc;
+    }
     if (!gather) {
         const int s = p.stride;
         cuuint64_t dims[4] = {(cuuint64_t)L->cin, (cuuint64_t)w_in, (cuuint64_t)h_in, (cuuint64_t)batch};

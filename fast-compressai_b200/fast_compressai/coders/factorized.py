@@ -21,15 +21,18 @@ import torch
 from .errors import CoderInputError
 from .warp_div import WarpDivBackend, WarpDivPayload
 
-# One copy stream per device for the host-batch entry points.
-_COPY_STREAMS: dict[int, torch.cuda.Stream] = {}
+# One copy stream per compute stream for the host-batch entry points, so that
+# callers on different streams (several batches in flight) do not serialise
+# their uploads and downloads on one copy queue.
+_COPY_STREAMS: dict[tuple[int, int], torch.cuda.Stream] = {}
 
 
-def _copy_stream(device: torch.device) -> torch.cuda.Stream:
+def _copy_stream(device: torch.device, compute: torch.cuda.Stream) -> torch.cuda.Stream:
     index = device.index if device.index is not None else torch.cuda.current_device()
-    stream = _COPY_STREAMS.get(index)
+    key = (index, compute.cuda_stream)
+    stream = _COPY_STREAMS.get(key)
     if stream is None:
-        stream = _COPY_STREAMS[index] = torch.cuda.Stream(device=index)
+        stream = _COPY_STREAMS.setdefault(key, torch.cuda.Stream(device=index))
     return stream
 
 
@@ -110,7 +113,7 @@ class FactorizedWarpDivCodec:
         dev = self._device()
         with torch.no_grad(), torch.cuda.device(dev):
             compute = torch.cuda.current_stream(dev)
-            copy = _copy_stream(dev)
+            copy = _copy_stream(dev, compute)
             x = x.float().contiguous()
             x_dev = torch.empty(x.shape, dtype=torch.float32, device=dev)
             copy.wait_stream(compute)  # x_dev's memory is free for the copies
@@ -146,7 +149,7 @@ class FactorizedWarpDivCodec:
         dev = y_hat.device
         with torch.no_grad(), torch.cuda.device(dev):
             compute = torch.cuda.current_stream(dev)
-            copy = _copy_stream(dev)
+            copy = _copy_stream(dev, compute)
             g_s = self.model.g_s
             fused = getattr(g_s, "fuses_clamp", False)
             for i0, i1 in _chunks(y_hat.shape[0], chunk_images):

@@ -61,7 +61,10 @@ def _nhwc(x):
     return x.permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("H,W", [(64, 96), (40, 72), (33, 47)])
+# widths divisible by 4 take the TMA input-window path (tiles of up to 64
+# columns; 260 -> 130 output columns is ragged, 16 -> tiles 8 wide and 16
+# high), the others the direct-load path
+@pytest.mark.parametrize("H,W", [(64, 96), (40, 72), (36, 260), (16, 16), (33, 47)])
 def test_first_layer_gather_gdn(cuda_device, H, W):
     torch.manual_seed(1)
     conv = torch.nn.Conv2d(3, 128, 5, 2, 2).to(cuda_device)
