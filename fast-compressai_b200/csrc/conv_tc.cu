@@ -52,8 +52,7 @@ constexpr int kBM = 128;          // output pixels per tile (MMA M)
 constexpr int kBK = 64;           // bf16 per K block: one 128-byte row
 constexpr int kSmemBudget = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
-constexpr int kEpiWarps = 8;      // warps 0-7: two per TMEM lane quarter, one per column half
-constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kEpiWarpsMax = 8;   // warps 0-7 may hold epilogue roles (Layout::kEpiWarps of them do)
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kGatherThread0 = 320;  // warps 10-13
@@ -101,20 +100,25 @@ struct ConvParams {
     int *err;
 };
 
-template <int kNpad, int kEpi, bool kGather>
+// kPair: CTA pairs (cluster of 2) share each MMA (cta_group::2, M = 256):
+// each CTA holds its 128 pixel rows of A and half of the N rows of B (and of
+// gamma), so a CTA's operand ring carries a quarter less per MMA and fits more
+// stages.
+template <int kNpad, int kEpi, bool kGather, bool kPair = false>
 struct Layout {
     static constexpr bool kNorm = kEpi == kEpiGdn || kEpi == kEpiIgdn;
+    static constexpr int kNB = kPair ? kNpad / 2 : kNpad;  // B / gamma rows this CTA holds
     static constexpr int kA = kGather ? kBM * kGatherK * 2 : kBM * kBK * 2;
-    static constexpr int kB = kGather ? 0 : kNpad * kBK * 2;
+    static constexpr int kB = kGather ? 0 : kNB * kBK * 2;
     static constexpr int kStage = kA + kB;
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
-    static constexpr int kG = kNorm ? kNpad * kNpad * 2 : 0;
+    static constexpr int kG = kNorm ? kNB * kNpad * 2 : 0;
     static constexpr int kX2 = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
     static constexpr int kS = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
     // operand ring: as many stages as the shared memory left over holds
     // (more bytes in flight hide more of the TMA round trip)
-    static constexpr int kFixedBytes = kNpad * kGatherK * 2 * (kGather ? 1 : 0) + (kNorm ? 2 * kNpad * kNpad * 2 : 0) +
+    static constexpr int kFixedBytes = kW + kG + kX2 +
                                        (kEpi == kEpiScatter ? kBM * (kNpad + 1) * 4 : 0) + (kGather ? 2 * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
     static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
@@ -128,19 +132,26 @@ struct Layout {
     static constexpr int offBias = offPatch + kP;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
-    static constexpr int kBars = 2 * kStages + 7 + (kGather ? 4 : 0);
+    static constexpr int kBars = 2 * kStages + 7 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
     static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
     static constexpr int kBytes = offSlot + 32;
     static constexpr int kAlloc = kBytes + 1024;  // base alignment slack
     static constexpr int kThreads = kGather ? 448 : 320;
+    // Epilogue warps: one per TMEM lane quarter where the mainloop bounds the
+    // layer (fewer warps competing with the MMA warp for issue slots), two
+    // (column halves) where the epilogue is the heavy part: the first layer
+    // (K = 80) and the scatter layer.
+    static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter) ? 8 : 4;
+    static constexpr int kEpiThreads = kEpiWarps * 32;
     // column split between the two epilogue warps of a lane quarter
-    static constexpr int kSplit = kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
+    static constexpr int kSplit = kEpiWarps == 8 && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
     static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
     static_assert(offPatch % 128 == 0 && kPatchBuf % 128 == 0, "patch buffer alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
+    static_assert(!kPair || (!kGather && kEpi != kEpiScatter && kNB % 8 == 0), "pair instances: TMA operands");
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
 };
 
@@ -169,11 +180,11 @@ __device__ __forceinline__ void fail(const ConvParams &p, volatile int *abort, i
     if (p.err) atomicOr(p.err, code);
 }
 
-template <int kNpad, int kEpi, bool kGather>
-__global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
+template <int kNpad, int kEpi, bool kGather, bool kPair>
+__global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmG, const ConvParams p) {
-    using Lay = Layout<kNpad, kEpi, kGather>;
+    using Lay = Layout<kNpad, kEpi, kGather, kPair>;
     constexpr bool kNorm = Lay::kNorm;
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem =
@@ -189,6 +200,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
     uint64_t *dbar = cbar + 1;  // abort path: drains this CTA's MMAs
     uint64_t *pfull = dbar + 1;   // first layer: patch buffer loaded (2)
     uint64_t *pempty = pfull + 2; // first layer: patch buffer read by all gather threads (2)
+    uint64_t *x2full = dbar + 1;  // pairs (rank 0): both CTAs wrote their x^2 tile
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Lay::offSlot);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 4);
     volatile int *epi_ok = reinterpret_cast<volatile int *>(smem + Lay::offSlot + 8);
@@ -197,6 +209,13 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Pairs: CTA `rank` of the cluster takes pixel sub-tile `rank` of each
+    // pair tile; rank 0 (the leader) issues all MMAs of the pair.
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int unit0 = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // first tile (pair tile) of this CTA
+    const int unit_step = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int sub_x = kPair ? (int)rank * p.TX : 0;                      // sub-tile origin within a pair tile
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -205,8 +224,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], kEpiThreads);
+            mbar_init(&acce[b], kPair ? 2 : Lay::kEpiThreads);  // pairs: one arrival per CTA's epilogue
         }
+        if (kPair) mbar_init(x2full, 2);
         mbar_init(g2bar, 1);
         mbar_init(cbar, 1);
         mbar_init(dbar, 2);
@@ -224,11 +244,18 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         if (kNorm) s_beta[i] = i < p.cout ? p.beta[i] : 1.f;
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(tmem_slot, p.tmem_cols);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(tmem_slot, p.tmem_cols);  // same warp and slot in both CTAs
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, p.tmem_cols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // pairs: both CTAs' barriers exist before any remote arrive or load names them
+    if (kPair) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -245,9 +272,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
             uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
             if (cbytes) {
                 mbar_arrive_expect_tx(cbar, cbytes);
-                if (kNorm) {
-                    tma_load_3d(smem + Lay::offG, &tmG, cbar, 0, 0, 0);
-                    tma_load_3d(smem + Lay::offG + Lay::kG / 2, &tmG, cbar, kBK, 0, 0);
+                if (kNorm) {  // pairs: this CTA's half of the gamma rows
+                    tma_load_3d(smem + Lay::offG, &tmG, cbar, 0, (int)rank * Lay::kNB, 0);
+                    tma_load_3d(smem + Lay::offG + Lay::kG / 2, &tmG, cbar, kBK, (int)rank * Lay::kNB, 0);
                 }
                 if (kGather) bulk_load(smem + Lay::offW, p.wgather, Lay::kW, cbar);
             }
@@ -255,9 +282,10 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 uint32_t it = 0;
                 int last_round[kStages];
                 for (int s = 0; s < kStages; ++s) last_round[s] = -1;
-                for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x) {
+                for (int tile = unit0; tile < p.tiles_total && !*abort; tile += unit_step) {
                     int b, ph, gy0, gx0;
                     tile_coords(p, tile, b, ph, gy0, gx0);
+                    gx0 += sub_x;
                     const Taps &tp = p.taps[ph];
                     for (int t = 0; t < tp.n && !*abort; ++t) {
                         const int ix = gx0 * p.stride + tp.dx[t];
@@ -270,15 +298,24 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                                 break;
                             }
                             unsigned char *st = smem + s * Lay::kStage;
-                            mbar_arrive_expect_tx(&full[s], Lay::kStage);
-                            tma_load_4d(st, &tmA, &full[s], cb * kBK, ix, iy, b);
-                            tma_load_3d(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
+                            if (kPair) {
+                                // both CTAs' bytes count on the leader's full[s]
+                                const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                                if (leader) mbar_arrive_expect_tx(&full[s], 2 * Lay::kStage);
+                                tma_load_4d_pair(st, &tmA, fb, cb * kBK, ix, iy, b);
+                                tma_load_3d_pair(st + Lay::kA, &tmW, fb, cb * kBK, (int)rank * Lay::kNB, tp.w[t]);
+                            } else {
+                                mbar_arrive_expect_tx(&full[s], Lay::kStage);
+                                tma_load_4d(st, &tmA, &full[s], cb * kBK, ix, iy, b);
+                                tma_load_3d(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
+                            }
                             last_round[s] = (int)r;
                         }
                     }
                 }
-                if (*abort) {
-                    // let this CTA's loads in flight land before the CTA exits
+                if (*abort && leader) {
+                    // let the loads in flight land before the CTA exits (pairs:
+                    // the leader's full[s] also counts the peer's loads)
                     for (int s = 0; s < kStages; ++s)
                         if (last_round[s] >= 0) mbar_wait(&full[s], (uint32_t)last_round[s] & 1, nullptr, kWaitNs / 10);
                 }
@@ -314,12 +351,13 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_bf16(kBM, kNpad);
+        // (pairs: the leader alone; its commits arrive in both CTAs)
+        if (lane == 0 && leader) {
+            const uint32_t idesc = idesc_bf16(kPair ? 2 * kBM : kBM, kNpad);
             bool consts = !kGather;
             uint32_t it = 0;
             int j = 0;
-            for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++j) {
+            for (int tile = unit0; tile < p.tiles_total && !*abort; tile += unit_step, ++j) {
                 if (!consts) {
                     if (!mbar_wait(cbar, 0, abort, kWaitNs)) {
                         fail(p, abort, kErrMma);
@@ -331,7 +369,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 tile_coords(p, tile, b, ph, gy0, gx0);
                 const int buf = j & 1;
                 const uint32_t use = j >> 1;
-                if (!mbar_wait(&acce[buf], (use & 1) ^ 1, abort, kWaitNs)) {
+                if (!mbar_wait(&acce[buf], (use & 1) ^ 1, abort, kWaitNs, kPair)) {
                     fail(p, abort, kErrMma);
                     break;
                 }
@@ -355,6 +393,12 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                         for (int kk = 0; kk < kGatherK / 16; ++kk)
                             mma_bf16(d, smem_desc(a0 + kk * 256, 128, 1280, 0), smem_desc(w0 + kk * 256, 128, 1280, 0),
                                      idesc, kk != 0);
+                    } else if (kPair) {
+                        const uint32_t b0 = a0 + Lay::kA;
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk)
+                            mma_bf16_pair(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
+                                          idesc, (ks | kk) != 0);
                     } else {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
@@ -362,13 +406,16 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                             mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
                                      idesc, (ks | kk) != 0);
                     }
-                    mma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    // frees the stage (pairs: in both CTAs) once these MMAs have read it
+                    if (kPair) mma_commit_pair_both(&empty[s], 3);
+                    else mma_commit(&empty[s]);
                 }
                 if (!ok) break;
-                mma_commit(&accf[buf]);
+                if (kPair) mma_commit_pair_both(&accf[buf], 3);
+                else mma_commit(&accf[buf]);
             }
         }
-    } else if (warp < kEpiWarps) {
+    } else if (warp < Lay::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
         // Warp w reads TMEM lanes 32*(w%4).. (tile rows) and column half w/4.
         // Thread 0 alone waits on the mbarriers and publishes the outcome in
@@ -381,9 +428,10 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         bool consts = !kNorm;
         int j = 0;
-        for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++j) {
+        for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
             int b, ph, gy0, gx0;
             tile_coords(p, tile, b, ph, gy0, gx0);
+            gx0 += sub_x;
             const int buf = j & 1;
             const uint32_t use = j >> 1;
             if (threadIdx.x == 0) {
@@ -393,7 +441,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 if (!ok) fail(p, abort, kErrEpilogue);
                 *epi_ok = ok ? 1 : 0;
             }
-            named_barrier_sync(1, kEpiThreads);
+            named_barrier_sync(1, Lay::kEpiThreads);
             if (!*epi_ok) break;
             consts = true;
             tc_fence_after();
@@ -417,11 +465,11 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + c + e] = __uint_as_float(v[e]);
                 }
-                named_barrier_sync(1, kEpiThreads);
+                named_barrier_sync(1, Lay::kEpiThreads);
                 float *out = reinterpret_cast<float *>(p.out);
                 const int64_t plane = (int64_t)p.Hout * p.Wout;
                 const float b0 = s_bias[0], b1 = s_bias[1], b2 = s_bias[2];
-                for (int item = threadIdx.x; item < kScatterCoreH * kScatterCoreW * 4; item += kEpiThreads) {
+                for (int item = threadIdx.x; item < kScatterCoreH * kScatterCoreW * 4; item += Lay::kEpiThreads) {
                     const int core = item >> 2, py = (item >> 1) & 1, px = item & 1;
                     const int ci = core / kScatterCoreW, cj = core - ci * kScatterCoreW;
                     const int oyv = 2 * (gy0 + ci) + py, oxv = 2 * (gx0 + cj) + px;
@@ -456,7 +504,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                     o[plane] = a1;
                     o[2 * plane] = a2;
                 }
-                named_barrier_sync(1, kEpiThreads);  // S is rewritten by the next tile
+                named_barrier_sync(1, Lay::kEpiThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
                 // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile
                 const uint32_t x2 = smem_u32(smem + Lay::offX2);
@@ -482,25 +530,47 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                     }
                 }
                 fence_proxy_async_smem();
-                named_barrier_sync(1, kEpiThreads);
+                named_barrier_sync(1, Lay::kEpiThreads);
                 if (threadIdx.x == 0) {
-                    tc_fence_after();
                     const uint32_t g0 = smem_u32(smem + Lay::offG);
                     const uint32_t d2 = tmem_base + buf * p.buf_stride + kNpad;
-                    const uint32_t idesc = idesc_bf16(kBM, kNpad);
+                    bool ok = true;
+                    if (kPair) {
+                        // norm = x^2 (each CTA its 128 rows) x gamma^T (each CTA half
+                        // the rows): the leader issues it once both tiles are written
+                        mbar_arrive_cluster(mapa_shared(smem_u32(x2full), 0));
+                        if (leader) {
+                            ok = mbar_wait(x2full, j & 1, abort, kWaitNs, true);
+                            if (ok) {
+                                tc_fence_after();
+                                const uint32_t idesc = idesc_bf16(2 * kBM, kNpad);
 #pragma unroll
-                    for (int kk = 0; kk < kNpad / 16; ++kk) {
-                        const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
-                        const uint32_t goff = (kk / 4) * (kNpad * 128) + (kk % 4) * 32;
-                        mma_bf16(d2, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc,
-                                 kk != 0);
+                                for (int kk = 0; kk < kNpad / 16; ++kk) {
+                                    const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
+                                    const uint32_t goff = (kk / 4) * (Lay::kNB * 128) + (kk % 4) * 32;
+                                    mma_bf16_pair(d2, smem_desc(x2 + koff, 16, 1024, 2),
+                                                  smem_desc(g0 + goff, 16, 1024, 2), idesc, kk != 0);
+                                }
+                                mma_commit_pair_both(g2bar, 3);
+                            }
+                        }
+                    } else {
+                        tc_fence_after();
+                        const uint32_t idesc = idesc_bf16(kBM, kNpad);
+#pragma unroll
+                        for (int kk = 0; kk < kNpad / 16; ++kk) {
+                            const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
+                            const uint32_t goff = (kk / 4) * (kNpad * 128) + (kk % 4) * 32;
+                            mma_bf16(d2, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc,
+                                     kk != 0);
+                        }
+                        mma_commit(g2bar);
                     }
-                    mma_commit(g2bar);
-                    const bool ok = mbar_wait(g2bar, j & 1, abort, kWaitNs);
+                    if (ok) ok = mbar_wait(g2bar, j & 1, abort, kWaitNs);
                     if (!ok) fail(p, abort, kErrEpilogue);
                     *epi_ok = ok ? 1 : 0;
                 }
-                named_barrier_sync(1, kEpiThreads);
+                named_barrier_sync(1, Lay::kEpiThreads);
                 if (!*epi_ok) break;
                 tc_fence_after();
                 // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm))
@@ -572,9 +642,16 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acce[buf]);
+            if (kPair) {
+                // every epilogue thread of this CTA is done with the buffer; one
+                // arrival per CTA on the leader's acce
+                named_barrier_sync(1, Lay::kEpiThreads);
+                if (threadIdx.x == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[buf]), 0));
+            } else {
+                mbar_arrive(&acce[buf]);
+            }
             // the next tile's epi_ok must not be written before every thread read this one
-            named_barrier_sync(1, kEpiThreads);
+            named_barrier_sync(1, Lay::kEpiThreads);
         }
     } else if (kGather) {
         // ------------------------------------------------------------ gather (first layer)
@@ -656,17 +733,23 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather>::kThreads, 1)
 
     // ---------------------------------------------------------------- teardown
     __syncthreads();
-    if (*abort) {
+    if (*abort && leader) {
         // the two threads that issue MMAs (MMA lane, epilogue thread 0) commit
         // to dbar; TMEM is freed only once everything they issued completed
-        if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0) mma_commit(dbar);
+        if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0) {
+            if (kPair) mma_commit_pair(dbar);
+            else mma_commit(dbar);
+        }
         if (warp == kMmaWarp && lane == 0) mbar_wait(dbar, 0, nullptr, kWaitNs / 10);
         __syncthreads();
     }
+    // pairs: no remote arrive, load or MMA reaches a CTA that has left
+    if (kPair) cluster_sync_all();
     if (warp == kMmaWarp) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, p.tmem_cols);
+        if (kPair) tmem_dealloc_pair(tmem_base, p.tmem_cols);
+        else tmem_dealloc(tmem_base, p.tmem_cols);
     }
 }
 
@@ -714,27 +797,69 @@ static int pick_tx(int gw, int max_tx = 128) {
     return best;
 }
 
-template <int kNpad, int kEpi, bool kGather>
+template <int kNpad, int kEpi, bool kGather, bool kPair = false>
 static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const ConvParams &p,
                   cudaStream_t stream) {
-    using Lay = Layout<kNpad, kEpi, kGather>;
+    using Lay = Layout<kNpad, kEpi, kGather, kPair>;
     static_assert(Lay::kAlloc <= kSmemBudget, "shared memory");
-    auto kernel = conv_tc_kernel<kNpad, kEpi, kGather>;
+    auto kernel = conv_tc_kernel<kNpad, kEpi, kGather, kPair>;
     static int configured[64] = {0};
+    static int max_clusters[64] = {0};
     int dev = 0;
     FCAI_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (dev < 0 || dev >= 64) return fcai::fail(FCAI_ERR_CUDA, "device ordinal %d unsupported", dev);
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(Lay::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Lay::kAlloc;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (!configured[dev]) {
         FCAI_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kAlloc));
+        if (kPair) {
+            // pairs that can be resident at once (one CTA per SM)
+            cfg.gridDim = dim3(2, 1, 1);
+            int n = 0;
+            FCAI_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+            if (n < 1) return fcai::fail(FCAI_ERR_CUDA, "no CTA pair of this layer fits on the device");
+            max_clusters[dev] = n;
+        }
         configured[dev] = 1;
     }
-    int grid = p.tiles_total < fcai::sm_count() ? p.tiles_total : fcai::sm_count();
-    kernel<<<grid, Lay::kThreads, Lay::kAlloc, stream>>>(a, w, g, p);
+    if (kPair) {
+        const int clusters = p.tiles_total < max_clusters[dev] ? p.tiles_total : max_clusters[dev];
+        cfg.gridDim = dim3(2 * clusters, 1, 1);
+        FCAI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, a, w, g, p));
+    } else {
+        int grid = p.tiles_total < fcai::sm_count() ? p.tiles_total : fcai::sm_count();
+        kernel<<<grid, Lay::kThreads, Lay::kAlloc, stream>>>(a, w, g, p);
+    }
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
 
-static int dispatch(int npad, int epi, bool gather, const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g,
-                    const ConvParams &p, cudaStream_t stream) {
+static int dispatch(int npad, int epi, bool gather, bool pair, const CUtensorMap &a, const CUtensorMap &w,
+                    const CUtensorMap &g, const ConvParams &p, cudaStream_t stream) {
+    if (pair) {
+        if (npad == 128) {
+            switch (epi) {
+                case kEpiBf16: return launch<128, kEpiBf16, false, true>(a, w, g, p, stream);
+                case kEpiGdn: return launch<128, kEpiGdn, false, true>(a, w, g, p, stream);
+                case kEpiIgdn: return launch<128, kEpiIgdn, false, true>(a, w, g, p, stream);
+                case kEpiF32: return launch<128, kEpiF32, false, true>(a, w, g, p, stream);
+                default: break;
+            }
+        } else if (npad == 192) {
+            if (epi == kEpiF32) return launch<192, kEpiF32, false, true>(a, w, g, p, stream);
+            if (epi == kEpiBf16) return launch<192, kEpiBf16, false, true>(a, w, g, p, stream);
+        }
+        return fcai::fail(FCAI_ERR_INVALID, "no CTA-pair kernel for npad=%d epilogue=%d", npad, epi);
+    }
     if (gather) {
         if (npad == 128 && epi == kEpiGdn) return launch<128, kEpiGdn, true>(a, w, g, p, stream);
         return fcai::fail(FCAI_ERR_INVALID, "first-layer kernel is built for 128 channels with GDN");
@@ -822,6 +947,12 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     if (norm && (!L->gdn_beta || !L->gdn_gamma || L->out_format != FCAI_FMT_NHWC_BF16))
         return fcai::fail(FCAI_ERR_INVALID, "GDN epilogue needs beta, gamma and a bf16 NHWC output");
     const bool scatter = L->algorithm == FCAI_ALGO_SCATTER;
+    if (L->algorithm != FCAI_ALGO_IMPLICIT_GEMM && L->algorithm != FCAI_ALGO_SCATTER &&
+        L->algorithm != FCAI_ALGO_IMPLICIT_GEMM_PAIR)
+        return fcai::fail(FCAI_ERR_INVALID, "unknown layer algorithm %d", (int)L->algorithm);
+    const bool pair = L->algorithm == FCAI_ALGO_IMPLICIT_GEMM_PAIR;
+    if (pair && (gather || npad != L->cout || (npad != 128 && npad != 192)))
+        return fcai::fail(FCAI_ERR_INVALID, "CTA-pair layers take bf16 NHWC input and 128 or 192 output channels");
     if (scatter && (!deconv || L->cout > 10 || npad != (25 * L->cout + 15) / 16 * 16 || norm ||
                     L->out_format != FCAI_FMT_NCHW_F32))
         return fcai::fail(FCAI_ERR_INVALID,
@@ -850,9 +981,15 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         // the first layer's input windows come by TMA when the fp32 image
         // allows it: rows a multiple of 16 bytes, base 16-byte aligned
         const bool patch = gather && w_in % 4 == 0 && (reinterpret_cast<uintptr_t>(input) & 15) == 0;
-        p.TX = pick_tx(p.GW, patch ? kPatchMaxTX : 128);
+        if (pair) {
+            // a pair tile is two TX x TY sub-tiles side by side
+            p.TX = pick_tx((p.GW + 1) / 2, 128);
+            while (p.TX > 8 && ((p.GW + 2 * p.TX - 1) / (2 * p.TX)) * 2 * p.TX - p.GW >= p.TX) p.TX >>= 1;
+        } else {
+            p.TX = pick_tx(p.GW, patch ? kPatchMaxTX : 128);
+        }
         p.TY = kBM / p.TX;
-        p.step_x = p.TX;
+        p.step_x = pair ? 2 * p.TX : p.TX;
         p.step_y = p.TY;
         if (patch) {
             p.patch_tma = 1;
@@ -939,18 +1076,18 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         if ((rc = make_map(&ma, input, 4, dims, strides, box, es))) return rc;
         cuuint64_t wd[3] = {(cuuint64_t)L->cin, (cuuint64_t)npad, (cuuint64_t)(scatter ? 1 : 25)};
         cuuint64_t ws[2] = {(cuuint64_t)L->cin * 2, (cuuint64_t)npad * L->cin * 2};
-        cuuint32_t wb[3] = {(cuuint32_t)kBK, (cuuint32_t)npad, 1};
+        cuuint32_t wb[3] = {(cuuint32_t)kBK, (cuuint32_t)(pair ? npad / 2 : npad), 1};  // pairs: half the rows each
         cuuint32_t we[3] = {1, 1, 1};
         if ((rc = make_map(&mw, L->weight, 3, wd, ws, wb, we))) return rc;
     }
     if (norm) {
         cuuint64_t gd[3] = {(cuuint64_t)npad, (cuuint64_t)npad, 1};
         cuuint64_t gs[2] = {(cuuint64_t)npad * 2, (cuuint64_t)npad * npad * 2};
-        cuuint32_t gb[3] = {(cuuint32_t)kBK, (cuuint32_t)npad, 1};
+        cuuint32_t gb[3] = {(cuuint32_t)kBK, (cuuint32_t)(pair ? npad / 2 : npad), 1};
         cuuint32_t ge[3] = {1, 1, 1};
         if ((rc = make_map(&mg, L->gdn_gamma, 3, gd, gs, gb, ge))) return rc;
     }
-    return dispatch(npad, epi, gather, ma, mw, mg, p, stream);
+    return dispatch(npad, epi, gather, pair, ma, mw, mg, p, stream);
 }
 
 int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h, int32_t w,

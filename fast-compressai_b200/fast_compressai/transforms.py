@@ -34,7 +34,7 @@ FCAI_LAYER_CONV5S2 = 0
 FCAI_LAYER_DECONV5S2 = 1
 FCAI_EPI_NONE, FCAI_EPI_GDN, FCAI_EPI_IGDN = 0, 1, 2
 FCAI_FMT_NHWC_BF16, FCAI_FMT_NCHW_F32 = 0, 1
-FCAI_ALGO_IMPLICIT_GEMM, FCAI_ALGO_SCATTER = 0, 1
+FCAI_ALGO_IMPLICIT_GEMM, FCAI_ALGO_SCATTER, FCAI_ALGO_IMPLICIT_GEMM_PAIR = 0, 1, 2
 
 
 class FcaiLayer(ctypes.Structure):
@@ -140,7 +140,8 @@ def _gdn_params(gdn: nn.Module):
     return beta.detach().float().contiguous(), gamma.detach().float().reshape(c, c)
 
 
-def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool) -> _Layer:
+def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool,
+                pair: bool = False) -> _Layer:
     transposed = isinstance(conv, nn.ConvTranspose2d)
     if tuple(conv.kernel_size) != (5, 5) or tuple(conv.stride) != (2, 2) or tuple(conv.padding) != (2, 2):
         raise ConfigurationError("B200 transforms support 5x5 stride-2 padding-2 layers only")
@@ -186,7 +187,7 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         in_format=FCAI_FMT_NCHW_F32 if first else FCAI_FMT_NHWC_BF16,
         out_format=out_format,
         clamp01=1 if clamp else 0,
-        algorithm=FCAI_ALGO_SCATTER if scatter else FCAI_ALGO_IMPLICIT_GEMM,
+        algorithm=FCAI_ALGO_SCATTER if scatter else (FCAI_ALGO_IMPLICIT_GEMM_PAIR if pair else FCAI_ALGO_IMPLICIT_GEMM),
         reserved=0,
         weight=weight.data_ptr(),
         bias=bias.data_ptr(),

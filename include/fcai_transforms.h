@@ -50,12 +50,17 @@ extern "C" {
 enum { FCAI_LAYER_CONV5S2 = 0, FCAI_LAYER_DECONV5S2 = 1 };
 enum { FCAI_EPI_NONE = 0, FCAI_EPI_GDN = 1, FCAI_EPI_IGDN = 2 };
 enum { FCAI_FMT_NHWC_BF16 = 0, FCAI_FMT_NCHW_F32 = 1 };
-/* FCAI_ALGO_IMPLICIT_GEMM: GEMM over output pixels x output channels.
+/* FCAI_ALGO_IMPLICIT_GEMM: GEMM over output pixels x output channels, one CTA
+ *   per tile of 128 output pixels.
+ * FCAI_ALGO_IMPLICIT_GEMM_PAIR: the same GEMM on CTA pairs (clusters of 2):
+ *   2-SM tensor-core MMAs over 256 output pixels, each SM staging half of the
+ *   weight rows.  Layers with bf16 NHWC input and 128 or 192 output channels;
+ *   results are identical to FCAI_ALGO_IMPLICIT_GEMM.
  * FCAI_ALGO_SCATTER: transposed convolutions with cout <= 10 (the last
  *   synthesis layer): GEMM over input pixels x (25 taps * cout) columns on
  *   halo tiles, each output pixel summing its taps in the epilogue, so the
  *   input is read about 1.5x instead of once per tap. */
-enum { FCAI_ALGO_IMPLICIT_GEMM = 0, FCAI_ALGO_SCATTER = 1 };
+enum { FCAI_ALGO_IMPLICIT_GEMM = 0, FCAI_ALGO_SCATTER = 1, FCAI_ALGO_IMPLICIT_GEMM_PAIR = 2 };
 
 typedef struct {
     int32_t kind;       /* FCAI_LAYER_CONV5S2 or FCAI_LAYER_DECONV5S2 */

@@ -79,26 +79,31 @@ def test_first_layer_gather_gdn(cuda_device, H, W):
         _check(mine, _ref_layer(x, conv, gdn))
 
 
+# pair=True: CTA pairs (2-SM MMAs), the algorithm for 128 / 192 output
+# channels that callers can ask for; pair=False: one CTA per 128-pixel tile
+@pytest.mark.parametrize("pair", [False, True])
 @pytest.mark.parametrize("cin,cout,use_gdn,H,W", [(128, 128, True, 64, 96), (128, 128, True, 37, 50),
-                                                 (128, 192, False, 32, 48), (192, 128, False, 16, 24)])
-def test_conv_layers(cuda_device, cin, cout, use_gdn, H, W):
+                                                 (128, 192, False, 32, 48), (192, 128, False, 16, 24),
+                                                 (128, 128, False, 9, 70), (128, 128, True, 2, 3)])
+def test_conv_layers(cuda_device, cin, cout, use_gdn, H, W, pair):
     torch.manual_seed(2)
     conv = torch.nn.Conv2d(cin, cout, 5, 2, 2).to(cuda_device)
     gdn = GDN(cout).to(cuda_device) if use_gdn else None
     with torch.no_grad():
         x = torch.randn(2, cin, H, W, device=cuda_device)
         out_f32 = not use_gdn and cout == 192
-        layer = _make_layer(conv, gdn, first=False, out_f32=out_f32, clamp=False)
+        layer = _make_layer(conv, gdn, first=False, out_f32=out_f32, clamp=False, pair=pair)
         out = _run([layer], _nhwc(x), first_is_nchw=False)
         torch.cuda.synchronize()
         mine = out if out_f32 else out.float().permute(0, 3, 1, 2)
         _check(mine, _ref_layer(x, conv, gdn, out_bf16=not out_f32))
 
 
+@pytest.mark.parametrize("pair", [False, True])
 @pytest.mark.parametrize("cin,cout,use_gdn,H,W", [(192, 128, True, 8, 12), (128, 128, True, 16, 24),
                                                  (128, 128, True, 9, 13), (128, 3, False, 16, 24),
                                                  (128, 3, False, 9, 13), (128, 3, False, 31, 47)])
-def test_deconv_layers(cuda_device, cin, cout, use_gdn, H, W):
+def test_deconv_layers(cuda_device, cin, cout, use_gdn, H, W, pair):
     torch.manual_seed(3)
     deconv = torch.nn.ConvTranspose2d(cin, cout, 5, 2, 2, output_padding=1).to(cuda_device)
     gdn = GDN(cout, inverse=True).to(cuda_device) if use_gdn else None
@@ -106,7 +111,7 @@ def test_deconv_layers(cuda_device, cin, cout, use_gdn, H, W):
         x = torch.randn(2, cin, H, W, device=cuda_device) * 0.5
         out_f32 = cout == 3
         for clamp in ((False, True) if out_f32 else (False,)):
-            layer = _make_layer(deconv, gdn, first=False, out_f32=out_f32, clamp=clamp)
+            layer = _make_layer(deconv, gdn, first=False, out_f32=out_f32, clamp=clamp, pair=pair and cout > 10)
             out = _run([layer], _nhwc(x), first_is_nchw=False)
             torch.cuda.synchronize()
             mine = out if out_f32 else out.float().permute(0, 3, 1, 2)
@@ -220,3 +225,25 @@ def test_host_batch_entry_points_match_device_ones(cuda_device, transforms):
                 torch.testing.assert_close(got, x_dev.cpu(), atol=1e-4, rtol=0)
     with pytest.raises(CoderInputError):
         fast.compress_host(x.to(cuda_device))
+
+
+@pytest.mark.parametrize("kind", ["conv_gdn", "deconv_igdn", "conv_latent"])
+def test_pair_tiles_match_single_tiles_bitwise(cuda_device, kind):
+    # FCAI_ALGO_IMPLICIT_GEMM_PAIR accumulates the same products in the same
+    # order as the one-CTA algorithm, so the outputs are identical
+    torch.manual_seed(5)
+    if kind == "conv_gdn":
+        mod, gdn, shape, f32 = torch.nn.Conv2d(128, 128, 5, 2, 2), GDN(128), (3, 45, 71, 128), False
+    elif kind == "deconv_igdn":
+        mod, gdn = torch.nn.ConvTranspose2d(128, 128, 5, 2, 2, output_padding=1), GDN(128, inverse=True)
+        shape, f32 = (3, 19, 27, 128), False
+    else:
+        mod, gdn, shape, f32 = torch.nn.Conv2d(128, 192, 5, 2, 2), None, (2, 30, 50, 128), True
+    mod = mod.to(cuda_device)
+    gdn = gdn.to(cuda_device) if gdn is not None else None
+    with torch.no_grad():
+        x = torch.randn(*shape, device=cuda_device).to(torch.bfloat16)
+        outs = [_run([_make_layer(mod, gdn, first=False, out_f32=f32, clamp=False, pair=pr)], x, first_is_nchw=False)
+                for pr in (False, True)]
+        torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
