@@ -52,7 +52,6 @@ constexpr int kBM = 128;          // output pixels per tile (MMA M)
 constexpr int kBK = 64;           // bf16 per K block: one 128-byte row
 constexpr int kSmemBudget = 227 * 1024;  // dynamic shared memory per CTA
 constexpr int kMaxStages = 8;
-constexpr int kEpiWarpsMax = 8;   // warps 0-7 may hold epilogue roles (Layout::kEpiWarps of them do)
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kGatherThread0 = 320;  // warps 10-13
@@ -96,6 +95,7 @@ struct ConvParams {
     int patch_tma;       // first layer: 1 = input windows by TMA (tmA maps x_in), 0 = direct loads
     int patch_w, patch_h;  // patch box: columns (2 TX + 8), rows (2 TY + 3)
     uint32_t patch_bytes;
+    int tma_store;       // GDN conv layers: the output tile leaves through TMA stores (tmO)
     void *out;
     int *err;
 };
@@ -183,7 +183,8 @@ __device__ __forceinline__ void fail(const ConvParams &p, volatile int *abort, i
 template <int kNpad, int kEpi, bool kGather, bool kPair>
 __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmG, const ConvParams p) {
+                   const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmO,
+                   const ConvParams p) {
     using Lay = Layout<kNpad, kEpi, kGather, kPair>;
     constexpr bool kNorm = Lay::kNorm;
     extern __shared__ unsigned char smem_raw[];
@@ -425,6 +426,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         const int m = threadIdx.x & 127;  // TMEM lane = tile row = output pixel
         const int half = threadIdx.x >> 7;
         const int c_lo = half ? Lay::kSplit : 0, c_hi = half ? kNpad : Lay::kSplit;
+        // GDN passes: columns per thread, equal for both halves, in 16-column chunks
+        constexpr int kEpiChunks = (Lay::kEpiWarps == 8 ? Lay::kSplit : kNpad) / 16;
+        static_assert(!kNorm || Lay::kEpiWarps != 8 || 2 * Lay::kSplit == kNpad, "equal column halves");
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         bool consts = !kNorm;
         int j = 0;
@@ -435,6 +439,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             const int buf = j & 1;
             const uint32_t use = j >> 1;
             if (threadIdx.x == 0) {
+                // the x^2 tile doubles as the previous tile's output staging
+                if (kNorm && p.tma_store) bulk_wait_read_all();
                 bool ok = !*abort;
                 if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
                 if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
@@ -506,27 +512,33 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 }
                 named_barrier_sync(1, Lay::kEpiThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
-                // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile
+                // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile.
+                // 16-column chunks, the next chunk's TMEM load in flight while
+                // this one is converted and stored.
                 const uint32_t x2 = smem_u32(smem + Lay::offX2);
-#pragma unroll 1
-                for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
-                    uint32_t v[32];
-                    tmem_ld32(d1 + c0, v);
-                    tmem_wait_ld();
+                {
+                    uint32_t v[2][16];
+                    tmem_ld16(d1 + c_lo, v[0]);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint32_t w[4];
+                    for (int k = 0; k < kEpiChunks; ++k) {
+                        tmem_wait_ld();
+                        tmem_regs_ready(v[k & 1]);
+                        if (k + 1 < kEpiChunks) tmem_ld16(d1 + c_lo + (k + 1) * 16, v[(k + 1) & 1]);
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int c = c0 + q * 8 + e * 2;
-                            const float a = __uint_as_float(v[q * 8 + e * 2]) + s_bias[c];
-                            const float bb = __uint_as_float(v[q * 8 + e * 2 + 1]) + s_bias[c + 1];
-                            w[e] = pack_bf16x2(a * a, bb * bb);
+                        for (int q = 0; q < 2; ++q) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int c = c_lo + k * 16 + q * 8 + e * 2;
+                                const float a = __uint_as_float(v[k & 1][q * 8 + e * 2]) + s_bias[c];
+                                const float bb = __uint_as_float(v[k & 1][q * 8 + e * 2 + 1]) + s_bias[c + 1];
+                                w[e] = pack_bf16x2(a * a, bb * bb);
+                            }
+                            const int k0 = c_lo + k * 16 + q * 8;
+                            const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                            st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
+                                         w[3]);
                         }
-                        const int k0 = c0 + q * 8;
-                        const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
-                        st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
-                                     w[3]);
                     }
                 }
                 fence_proxy_async_smem();
@@ -573,34 +585,65 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 named_barrier_sync(1, Lay::kEpiThreads);
                 if (!*epi_ok) break;
                 tc_fence_after();
-                // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm))
+                // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm)),
+                // pipelined like pass 1
                 __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
                                       (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
-#pragma unroll 1
-                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
-                    uint32_t v[16], nv[16];
-                    tmem_ld16(d1 + c0, v);
-                    tmem_ld16(d1 + kNpad + c0, nv);
-                    tmem_wait_ld();
-                    uint32_t o[8];
+                {
+                    uint32_t v[2][16], nv[2][16];
+                    tmem_ld16(d1 + c_lo, v[0]);
+                    tmem_ld16(d1 + kNpad + c_lo, nv[0]);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int c = c0 + 2 * e;
-                        const float n0 = __uint_as_float(nv[2 * e]) + s_beta[c];
-                        const float n1 = __uint_as_float(nv[2 * e + 1]) + s_beta[c + 1];
-                        float r0 = rsqrtf(n0), r1 = rsqrtf(n1);
-                        if (kEpi == kEpiIgdn) {
-                            r0 *= n0;  // sqrt(n) = n * rsqrt(n)
-                            r1 *= n1;
+                    for (int k = 0; k < kEpiChunks; ++k) {
+                        tmem_wait_ld();
+                        tmem_regs_ready(v[k & 1]);
+                        tmem_regs_ready(nv[k & 1]);
+                        if (k + 1 < kEpiChunks) {
+                            tmem_ld16(d1 + c_lo + (k + 1) * 16, v[(k + 1) & 1]);
+                            tmem_ld16(d1 + kNpad + c_lo + (k + 1) * 16, nv[(k + 1) & 1]);
                         }
-                        const float x0 = __uint_as_float(v[2 * e]) + s_bias[c];
-                        const float x1 = __uint_as_float(v[2 * e + 1]) + s_bias[c + 1];
-                        o[e] = pack_bf16x2(x0 * r0, x1 * r1);
+                        const int c0 = c_lo + k * 16;
+                        uint32_t o[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const int c = c0 + 2 * e;
+                            const float n0 = __uint_as_float(nv[k & 1][2 * e]) + s_beta[c];
+                            const float n1 = __uint_as_float(nv[k & 1][2 * e + 1]) + s_beta[c + 1];
+                            float r0 = rsqrtf(n0), r1 = rsqrtf(n1);
+                            if (kEpi == kEpiIgdn) {
+                                r0 *= n0;  // sqrt(n) = n * rsqrt(n)
+                                r1 *= n1;
+                            }
+                            const float x0 = __uint_as_float(v[k & 1][2 * e]) + s_bias[c];
+                            const float x1 = __uint_as_float(v[k & 1][2 * e + 1]) + s_bias[c + 1];
+                            o[e] = pack_bf16x2(x0 * r0, x1 * r1);
+                        }
+                        if (p.tma_store) {
+                            // into the staging tile (the x^2 tile's layout: 128-byte
+                            // rows per 64 channels, 16-byte chunks swizzled by row)
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                const int k0 = c0 + q * 8;
+                                const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                                st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), o[q * 4],
+                                             o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+                            }
+                        } else if (valid) {
+                            uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+                            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                        }
                     }
-                    if (valid) {
-                        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
-                        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+                if (p.tma_store) {
+                    // the whole tile, 64 channels per box; TMA leaves out the
+                    // pixels beyond the image
+                    fence_proxy_async_smem();
+                    named_barrier_sync(1, Lay::kEpiThreads);
+                    if (threadIdx.x == 0) {
+                        tma_store_4d(&tmO, smem + Lay::offX2, 0, gx0, gy0, b);
+                        tma_store_4d(&tmO, smem + Lay::offX2 + kBM * 128, kBK, gx0, gy0, b);
+                        bulk_commit_group();
                     }
                 }
             } else if (kEpi == kEpiBf16) {
@@ -653,6 +696,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             // the next tile's epi_ok must not be written before every thread read this one
             named_barrier_sync(1, Lay::kEpiThreads);
         }
+        if (kNorm && p.tma_store && threadIdx.x == 0) bulk_wait_all();  // stores complete before the CTA exits
     } else if (kGather) {
         // ------------------------------------------------------------ gather (first layer)
         const int m = threadIdx.x - kGatherThread0;
@@ -798,8 +842,8 @@ static int pick_tx(int gw, int max_tx = 128) {
 }
 
 template <int kNpad, int kEpi, bool kGather, bool kPair = false>
-static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const ConvParams &p,
-                  cudaStream_t stream) {
+static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const CUtensorMap &o,
+                  const ConvParams &p, cudaStream_t stream) {
     using Lay = Layout<kNpad, kEpi, kGather, kPair>;
     static_assert(Lay::kAlloc <= kSmemBudget, "shared memory");
     auto kernel = conv_tc_kernel<kNpad, kEpi, kGather, kPair>;
@@ -834,56 +878,56 @@ static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap 
     if (kPair) {
         const int clusters = p.tiles_total < max_clusters[dev] ? p.tiles_total : max_clusters[dev];
         cfg.gridDim = dim3(2 * clusters, 1, 1);
-        FCAI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, a, w, g, p));
+        FCAI_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, a, w, g, o, p));
     } else {
         int grid = p.tiles_total < fcai::sm_count() ? p.tiles_total : fcai::sm_count();
-        kernel<<<grid, Lay::kThreads, Lay::kAlloc, stream>>>(a, w, g, p);
+        kernel<<<grid, Lay::kThreads, Lay::kAlloc, stream>>>(a, w, g, o, p);
     }
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
 
 static int dispatch(int npad, int epi, bool gather, bool pair, const CUtensorMap &a, const CUtensorMap &w,
-                    const CUtensorMap &g, const ConvParams &p, cudaStream_t stream) {
+                    const CUtensorMap &g, const CUtensorMap &o, const ConvParams &p, cudaStream_t stream) {
     if (pair) {
         if (npad == 128) {
             switch (epi) {
-                case kEpiBf16: return launch<128, kEpiBf16, false, true>(a, w, g, p, stream);
-                case kEpiGdn: return launch<128, kEpiGdn, false, true>(a, w, g, p, stream);
-                case kEpiIgdn: return launch<128, kEpiIgdn, false, true>(a, w, g, p, stream);
-                case kEpiF32: return launch<128, kEpiF32, false, true>(a, w, g, p, stream);
+                case kEpiBf16: return launch<128, kEpiBf16, false, true>(a, w, g, o, p, stream);
+                case kEpiGdn: return launch<128, kEpiGdn, false, true>(a, w, g, o, p, stream);
+                case kEpiIgdn: return launch<128, kEpiIgdn, false, true>(a, w, g, o, p, stream);
+                case kEpiF32: return launch<128, kEpiF32, false, true>(a, w, g, o, p, stream);
                 default: break;
             }
         } else if (npad == 192) {
-            if (epi == kEpiF32) return launch<192, kEpiF32, false, true>(a, w, g, p, stream);
-            if (epi == kEpiBf16) return launch<192, kEpiBf16, false, true>(a, w, g, p, stream);
+            if (epi == kEpiF32) return launch<192, kEpiF32, false, true>(a, w, g, o, p, stream);
+            if (epi == kEpiBf16) return launch<192, kEpiBf16, false, true>(a, w, g, o, p, stream);
         }
         return fcai::fail(FCAI_ERR_INVALID, "no CTA-pair kernel for npad=%d epilogue=%d", npad, epi);
     }
     if (gather) {
-        if (npad == 128 && epi == kEpiGdn) return launch<128, kEpiGdn, true>(a, w, g, p, stream);
+        if (npad == 128 && epi == kEpiGdn) return launch<128, kEpiGdn, true>(a, w, g, o, p, stream);
         return fcai::fail(FCAI_ERR_INVALID, "first-layer kernel is built for 128 channels with GDN");
     }
     switch (npad) {
         case 128:
             switch (epi) {
-                case kEpiBf16: return launch<128, kEpiBf16, false>(a, w, g, p, stream);
-                case kEpiGdn: return launch<128, kEpiGdn, false>(a, w, g, p, stream);
-                case kEpiIgdn: return launch<128, kEpiIgdn, false>(a, w, g, p, stream);
-                case kEpiF32: return launch<128, kEpiF32, false>(a, w, g, p, stream);
+                case kEpiBf16: return launch<128, kEpiBf16, false>(a, w, g, o, p, stream);
+                case kEpiGdn: return launch<128, kEpiGdn, false>(a, w, g, o, p, stream);
+                case kEpiIgdn: return launch<128, kEpiIgdn, false>(a, w, g, o, p, stream);
+                case kEpiF32: return launch<128, kEpiF32, false>(a, w, g, o, p, stream);
                 default: break;
             }
             break;
         case 192:
-            if (epi == kEpiF32) return launch<192, kEpiF32, false>(a, w, g, p, stream);
-            if (epi == kEpiBf16) return launch<192, kEpiBf16, false>(a, w, g, p, stream);
+            if (epi == kEpiF32) return launch<192, kEpiF32, false>(a, w, g, o, p, stream);
+            if (epi == kEpiBf16) return launch<192, kEpiBf16, false>(a, w, g, o, p, stream);
             break;
         case 16:
-            if (epi == kEpiF32Clamp) return launch<16, kEpiF32Clamp, false>(a, w, g, p, stream);
-            if (epi == kEpiF32) return launch<16, kEpiF32, false>(a, w, g, p, stream);
+            if (epi == kEpiF32Clamp) return launch<16, kEpiF32Clamp, false>(a, w, g, o, p, stream);
+            if (epi == kEpiF32) return launch<16, kEpiF32, false>(a, w, g, o, p, stream);
             break;
         case 80:
-            if (epi == kEpiScatter) return launch<80, kEpiScatter, false>(a, w, g, p, stream);
+            if (epi == kEpiScatter) return launch<80, kEpiScatter, false>(a, w, g, o, p, stream);
             break;
         default:
             break;
@@ -1057,7 +1101,18 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.out = output;
     p.err = err;
 
-    CUtensorMap ma{}, mw{}, mg{};
+    CUtensorMap ma{}, mw{}, mg{}, mo{};
+    // GDN conv layers (one phase: output pixels of a tile are a dense box)
+    // write through TMA stores; the output base must be 16-byte aligned
+    p.tma_store = norm && !deconv && L->out_format == FCAI_FMT_NHWC_BF16 &&
+                  (reinterpret_cast<uintptr_t>(output) & 15) == 0 ? 1 : 0;
+    if (p.tma_store) {
+        cuuint64_t od[4] = {(cuuint64_t)npad, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)batch};
+        cuuint64_t os[3] = {(cuuint64_t)npad * 2, (cuuint64_t)wo * npad * 2, (cuuint64_t)ho * wo * npad * 2};
+        cuuint32_t ob[4] = {(cuuint32_t)kBK, (cuuint32_t)p.TX, (cuuint32_t)p.TY, 1};
+        cuuint32_t oe[4] = {1, 1, 1, 1};
+        if ((rc = make_map(&mo, output, 4, od, os, ob, oe))) return rc;
+    }
     if (gather && p.patch_tma) {
         // fp32 NCHW image as [B][3][Hin][Win]; one box = one tile's window
         cuuint64_t dims[4] = {(cuuint64_t)w_in, (cuuint64_t)h_in, 3, (cuuint64_t)batch};
@@ -1087,7 +1142,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         cuuint32_t ge[3] = {1, 1, 1};
         if ((rc = make_map(&mg, L->gdn_gamma, 3, gd, gs, gb, ge))) return rc;
     }
-    return dispatch(npad, epi, gather, pair, ma, mw, mg, p, stream);
+    return dispatch(npad, epi, gather, pair, ma, mw, mg, mo, p, stream);
 }
 
 int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h, int32_t w,
