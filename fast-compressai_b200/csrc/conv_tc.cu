@@ -113,7 +113,13 @@ struct Layout {
     static constexpr int kStage = kA + kB;
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
     static constexpr int kG = kNorm ? kNB * kNpad * 2 : 0;
-    static constexpr int kX2 = kNorm ? kBM * kNpad * 2 : 0;
+    // Ping-pong epilogue (the first layer, whose epilogue outweighs its K = 80
+    // mainloop): two groups of 4 warps take alternate tiles, each with its own
+    // accumulator buffer, x^2 / staging tile and GDN barrier, so one tile's
+    // GDN GEMM and stores overlap the other's passes.
+    static constexpr bool kPingPong = kGather && kNorm;
+    static constexpr int kX2One = kNorm ? kBM * kNpad * 2 : 0;
+    static constexpr int kX2 = kPingPong ? 2 * kX2One : kX2One;
     static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
     static constexpr int kS = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
     // operand ring: as many stages as the shared memory left over holds
@@ -132,7 +138,7 @@ struct Layout {
     static constexpr int offBias = offPatch + kP;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
-    static constexpr int kBars = 2 * kStages + 7 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
+    static constexpr int kBars = 2 * kStages + 8 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
     static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
     static constexpr int kBytes = offSlot + 32;
@@ -145,7 +151,9 @@ struct Layout {
     static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter) ? 8 : 4;
     static constexpr int kEpiThreads = kEpiWarps * 32;
     // column split between the two epilogue warps of a lane quarter
-    static constexpr int kSplit = kEpiWarps == 8 && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
+    static constexpr int kSplit = kEpiWarps == 8 && !kPingPong && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
+    static constexpr int kGroups = kPingPong ? 2 : 1;
+    static constexpr int kGroupThreads = kEpiThreads / kGroups;
     static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
     static_assert(offPatch % 128 == 0 && kPatchBuf % 128 == 0, "patch buffer alignment");
@@ -196,8 +204,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
     uint64_t *empty = bars + kStages;
     uint64_t *accf = bars + 2 * kStages;
     uint64_t *acce = accf + 2;
-    uint64_t *g2bar = acce + 2;
-    uint64_t *cbar = g2bar + 1;
+    uint64_t *g2bar = acce + 2;   // GDN GEMM done (one per epilogue group)
+    uint64_t *cbar = g2bar + 2;
     uint64_t *dbar = cbar + 1;  // abort path: drains this CTA's MMAs
     uint64_t *pfull = dbar + 1;   // first layer: patch buffer loaded (2)
     uint64_t *pempty = pfull + 2; // first layer: patch buffer read by all gather threads (2)
@@ -225,12 +233,13 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], kPair ? 2 : Lay::kEpiThreads);  // pairs: one arrival per CTA's epilogue
+            mbar_init(&acce[b], kPair ? 2 : Lay::kGroupThreads);  // pairs: one arrival per CTA's epilogue
         }
         if (kPair) mbar_init(x2full, 2);
-        mbar_init(g2bar, 1);
+        mbar_init(&g2bar[0], 1);
+        mbar_init(&g2bar[1], 1);
         mbar_init(cbar, 1);
-        mbar_init(dbar, 2);
+        mbar_init(dbar, 1 + Lay::kGroups);  // the MMA thread and each epilogue group's leader
         if (kGather) {
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&pfull[b], 1);
@@ -418,37 +427,47 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         }
     } else if (warp < Lay::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
-        // Warp w reads TMEM lanes 32*(w%4).. (tile rows) and column half w/4.
-        // Thread 0 alone waits on the mbarriers and publishes the outcome in
-        // epi_ok; all epilogue threads then meet at named barrier 1, so the
-        // group always takes the same branch and no thread waits at a barrier
-        // the others have left.
+        // Warp w reads TMEM lanes 32*(w%4).. (tile rows); with 8 warps either
+        // column half w/4 of every tile, or (ping-pong) all columns of the
+        // tiles of group w/4.  A group's first thread alone waits on the
+        // mbarriers and publishes the outcome in its epi_ok slot; the group
+        // then meets at its named barrier, so it always takes the same branch
+        // and no thread waits at a barrier the others have left.
         const int m = threadIdx.x & 127;  // TMEM lane = tile row = output pixel
-        const int half = threadIdx.x >> 7;
+        const int grp = Lay::kPingPong ? (warp >> 2) : 0;           // ping-pong group
+        const bool gleader = (threadIdx.x & (Lay::kGroupThreads - 1)) == 0;
+        const uint32_t gbar = 1 + grp;                               // the group's named barrier
+        const int half = Lay::kPingPong ? 0 : (threadIdx.x >> 7);
         const int c_lo = half ? Lay::kSplit : 0, c_hi = half ? kNpad : Lay::kSplit;
         // GDN passes: columns per thread, equal for both halves, in 16-column chunks
         constexpr int kEpiChunks = (Lay::kEpiWarps == 8 ? Lay::kSplit : kNpad) / 16;
-        static_assert(!kNorm || Lay::kEpiWarps != 8 || 2 * Lay::kSplit == kNpad, "equal column halves");
+        static_assert(!kNorm || Lay::kEpiWarps != 8 || Lay::kPingPong || 2 * Lay::kSplit == kNpad,
+                      "equal column halves");
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         bool consts = !kNorm;
-        int j = 0;
-        for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
+        volatile int *g_ok = epi_ok + grp;
+        uint64_t *g2 = &g2bar[grp];
+        const uint32_t x2 = smem_u32(smem + Lay::offX2 + grp * Lay::kX2One);
+        int j = grp;   // this CTA's tile index (groups take alternate tiles)
+        int gj = 0;    // the group's own tile count (phase of its GDN barrier)
+        for (int tile = unit0 + grp * unit_step; tile < p.tiles_total;
+             tile += Lay::kGroups * unit_step, j += Lay::kGroups, ++gj) {
             int b, ph, gy0, gx0;
             tile_coords(p, tile, b, ph, gy0, gx0);
             gx0 += sub_x;
             const int buf = j & 1;
             const uint32_t use = j >> 1;
-            if (threadIdx.x == 0) {
+            if (gleader) {
                 // the x^2 tile doubles as the previous tile's output staging
                 if (kNorm && p.tma_store) bulk_wait_read_all();
                 bool ok = !*abort;
                 if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
                 if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
                 if (!ok) fail(p, abort, kErrEpilogue);
-                *epi_ok = ok ? 1 : 0;
+                *g_ok = ok ? 1 : 0;
             }
-            named_barrier_sync(1, Lay::kEpiThreads);
-            if (!*epi_ok) break;
+            named_barrier_sync(gbar, Lay::kGroupThreads);
+            if (!*g_ok) break;
             consts = true;
             tc_fence_after();
             const int gy = gy0 + m / p.TX, gx = gx0 + m % p.TX;
@@ -471,7 +490,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
 #pragma unroll
                     for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + c + e] = __uint_as_float(v[e]);
                 }
-                named_barrier_sync(1, Lay::kEpiThreads);
+                named_barrier_sync(gbar, Lay::kGroupThreads);
                 float *out = reinterpret_cast<float *>(p.out);
                 const int64_t plane = (int64_t)p.Hout * p.Wout;
                 const float b0 = s_bias[0], b1 = s_bias[1], b2 = s_bias[2];
@@ -510,12 +529,11 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     o[plane] = a1;
                     o[2 * plane] = a2;
                 }
-                named_barrier_sync(1, Lay::kEpiThreads);  // S is rewritten by the next tile
+                named_barrier_sync(gbar, Lay::kGroupThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
                 // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile.
                 // 16-column chunks, the next chunk's TMEM load in flight while
                 // this one is converted and stored.
-                const uint32_t x2 = smem_u32(smem + Lay::offX2);
                 {
                     uint32_t v[2][16];
                     tmem_ld16(d1 + c_lo, v[0]);
@@ -542,8 +560,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     }
                 }
                 fence_proxy_async_smem();
-                named_barrier_sync(1, Lay::kEpiThreads);
-                if (threadIdx.x == 0) {
+                named_barrier_sync(gbar, Lay::kGroupThreads);
+                if (gleader) {
                     const uint32_t g0 = smem_u32(smem + Lay::offG);
                     const uint32_t d2 = tmem_base + buf * p.buf_stride + kNpad;
                     bool ok = true;
@@ -563,7 +581,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                                     mma_bf16_pair(d2, smem_desc(x2 + koff, 16, 1024, 2),
                                                   smem_desc(g0 + goff, 16, 1024, 2), idesc, kk != 0);
                                 }
-                                mma_commit_pair_both(g2bar, 3);
+                                mma_commit_pair_both(g2, 3);
                             }
                         }
                     } else {
@@ -576,14 +594,14 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                             mma_bf16(d2, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc,
                                      kk != 0);
                         }
-                        mma_commit(g2bar);
+                        mma_commit(g2);
                     }
-                    if (ok) ok = mbar_wait(g2bar, j & 1, abort, kWaitNs);
+                    if (ok) ok = mbar_wait(g2, gj & 1, abort, kWaitNs);
                     if (!ok) fail(p, abort, kErrEpilogue);
-                    *epi_ok = ok ? 1 : 0;
+                    *g_ok = ok ? 1 : 0;
                 }
-                named_barrier_sync(1, Lay::kEpiThreads);
-                if (!*epi_ok) break;
+                named_barrier_sync(gbar, Lay::kGroupThreads);
+                if (!*g_ok) break;
                 tc_fence_after();
                 // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm)),
                 // pipelined like pass 1
@@ -639,10 +657,11 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     // the whole tile, 64 channels per box; TMA leaves out the
                     // pixels beyond the image
                     fence_proxy_async_smem();
-                    named_barrier_sync(1, Lay::kEpiThreads);
-                    if (threadIdx.x == 0) {
-                        tma_store_4d(&tmO, smem + Lay::offX2, 0, gx0, gy0, b);
-                        tma_store_4d(&tmO, smem + Lay::offX2 + kBM * 128, kBK, gx0, gy0, b);
+                    named_barrier_sync(gbar, Lay::kGroupThreads);
+                    if (gleader) {
+                        const unsigned char *stg = smem + Lay::offX2 + grp * Lay::kX2One;
+                        tma_store_4d(&tmO, stg, 0, gx0, gy0, b);
+                        tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, gy0, b);
                         bulk_commit_group();
                     }
                 }
@@ -688,15 +707,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             if (kPair) {
                 // every epilogue thread of this CTA is done with the buffer; one
                 // arrival per CTA on the leader's acce
-                named_barrier_sync(1, Lay::kEpiThreads);
-                if (threadIdx.x == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[buf]), 0));
+                named_barrier_sync(gbar, Lay::kGroupThreads);
+                if (gleader) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[buf]), 0));
             } else {
                 mbar_arrive(&acce[buf]);
             }
             // the next tile's epi_ok must not be written before every thread read this one
-            named_barrier_sync(1, Lay::kEpiThreads);
+            named_barrier_sync(gbar, Lay::kGroupThreads);
         }
-        if (kNorm && p.tma_store && threadIdx.x == 0) bulk_wait_all();  // stores complete before the CTA exits
+        if (kNorm && p.tma_store && gleader) bulk_wait_all();  // stores complete before the CTA exits
     } else if (kGather) {
         // ------------------------------------------------------------ gather (first layer)
         const int m = threadIdx.x - kGatherThread0;
@@ -780,7 +799,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
     if (*abort && leader) {
         // the two threads that issue MMAs (MMA lane, epilogue thread 0) commit
         // to dbar; TMEM is freed only once everything they issued completed
-        if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0) {
+        if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0 ||
+            (Lay::kPingPong && threadIdx.x == Lay::kGroupThreads)) {
             if (kPair) mma_commit_pair(dbar);
             else mma_commit(dbar);
         }
