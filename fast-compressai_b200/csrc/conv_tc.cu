@@ -113,19 +113,20 @@ struct Layout {
     static constexpr int kStage = kA + kB;
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
     static constexpr int kG = kNorm ? kNB * kNpad * 2 : 0;
-    // Ping-pong epilogue (the first layer, whose epilogue outweighs its K = 80
-    // mainloop): two groups of 4 warps take alternate tiles, each with its own
+    // Ping-pong epilogue (the first layer and the scatter layer, whose
+    // epilogues outweigh their short mainloops): two groups of 4 warps take alternate tiles, each with its own
     // accumulator buffer, x^2 / staging tile and GDN barrier, so one tile's
     // GDN GEMM and stores overlap the other's passes.
-    static constexpr bool kPingPong = kGather && kNorm;
+    static constexpr bool kPingPong = (kGather && kNorm) || kEpi == kEpiScatter;
     static constexpr int kX2One = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kX2 = kPingPong ? 2 * kX2One : kX2One;
     static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
-    static constexpr int kS = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
+    static constexpr int kSOne = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
+    static constexpr int kS = kPingPong ? 2 * kSOne : kSOne;
     // operand ring: as many stages as the shared memory left over holds
     // (more bytes in flight hide more of the TMA round trip)
     static constexpr int kFixedBytes = kW + kG + kX2 +
-                                       (kEpi == kEpiScatter ? kBM * (kNpad + 1) * 4 : 0) + (kGather ? 2 * kPatchBuf : 0) +
+                                       kS + (kGather ? 2 * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
     static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
     static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
@@ -481,7 +482,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 // contribution to all 25 taps x 3 outputs.  Each output pixel
                 // of the 12 x 28 core block sums the 4-9 contributions that
                 // land on it; one work item = one output pixel.
-                float *S = reinterpret_cast<float *>(smem + Lay::offS);
+                float *S = reinterpret_cast<float *>(smem + Lay::offS + grp * Lay::kSOne);
 #pragma unroll 1
                 for (int c = c_lo; c < c_hi; c += 16) {
                     uint32_t v[16];
@@ -494,7 +495,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 float *out = reinterpret_cast<float *>(p.out);
                 const int64_t plane = (int64_t)p.Hout * p.Wout;
                 const float b0 = s_bias[0], b1 = s_bias[1], b2 = s_bias[2];
-                for (int item = threadIdx.x; item < kScatterCoreH * kScatterCoreW * 4; item += Lay::kEpiThreads) {
+                for (int item = threadIdx.x & (Lay::kGroupThreads - 1); item < kScatterCoreH * kScatterCoreW * 4;
+                     item += Lay::kGroupThreads) {
                     const int core = item >> 2, py = (item >> 1) & 1, px = item & 1;
                     const int ci = core / kScatterCoreW, cj = core - ci * kScatterCoreW;
                     const int oyv = 2 * (gy0 + ci) + py, oxv = 2 * (gx0 + cj) + px;
