@@ -167,8 +167,13 @@ def encode_latent(y: torch.Tensor, medians: torch.Tensor, cdfs: torch.Tensor, cd
 
 def decode_latent(packed: torch.Tensor, max_rounds: torch.Tensor, header_bytes: int, chunk_len: int,
                   cdfs: torch.Tensor, cdf_sizes: torch.Tensor, offsets: torch.Tensor, medians: torch.Tensor,
-                  out: torch.Tensor) -> torch.Tensor:
-    """Decode into the dequantised fp32 latent ``out`` [B, C, ...] (``symbol + median``)."""
+                  out: torch.Tensor, check: bool = True) -> torch.Tensor:
+    """Decode into the dequantised fp32 latent ``out`` [B, C, ...] (``symbol + median``).
+
+    check=True waits for the GPU and raises on an inconsistent payload;
+    check=False returns at once (for payloads whose header is known to agree
+    with ``max_rounds``; a damaged body then decodes to unspecified values,
+    every read staying in bounds)."""
     if not (out.is_cuda and out.dtype == torch.float32 and out.is_contiguous()):
         raise RuntimeError("output latent must be a contiguous CUDA float32 tensor")
     _check_latent(out, medians, cdfs, cdf_sizes, offsets)
@@ -187,7 +192,7 @@ def decode_latent(packed: torch.Tensor, max_rounds: torch.Tensor, header_bytes: 
         ws = workspace("decode", dev, stream, nbytes)
         rc = _native.lib().fcai_warp_div_decode_latent(
             _ptr(packed), packed.numel(), _ptr(max_rounds), K, int(header_bytes), int(chunk_len), B, N, _ptr(cdfs),
-            C, L, _ptr(cdf_sizes), _ptr(offsets), _ptr(medians), _ptr(out), _ptr(ws), ws.numel(), 1,
+            C, L, _ptr(cdf_sizes), _ptr(offsets), _ptr(medians), _ptr(out), _ptr(ws), ws.numel(), 1 if check else 0,
             ctypes.c_void_p(stream))
         _native.count_launches(2)
         _native.check(rc)

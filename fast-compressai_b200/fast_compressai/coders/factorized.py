@@ -64,9 +64,15 @@ class FactorizedWarpDivCodec:
             raise CoderInputError("entropy tables are not initialized; call model.update() before accelerate()")
         return cdfs.contiguous(), lengths.contiguous(), offsets.contiguous()
 
-    @staticmethod
-    def _medians(entropy) -> torch.Tensor:
-        return entropy._get_medians().detach().reshape(-1).float().contiguous()
+    def _medians(self, entropy) -> torch.Tensor:
+        """Per-channel medians, cached until the entropy model's quantiles change."""
+        q = entropy.quantiles
+        key = (id(q), q._version if not q.is_inference() else -1, q.data_ptr())
+        hit = self.__dict__.get("_median_cache")
+        if hit is None or hit[0] != key:
+            hit = (key, entropy._get_medians().detach().reshape(-1).float().contiguous())
+            self._median_cache = hit
+        return hit[1]
 
     def compress(self, x: torch.Tensor, timing: dict[str, float] | None = None):
         if not isinstance(x, torch.Tensor) or x.device.type != "cuda" or x.ndim != 4:

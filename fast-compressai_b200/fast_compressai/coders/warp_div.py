@@ -57,6 +57,25 @@ def _remember_rounds(max_rounds: torch.Tensor, total_rounds: int, all_ok: bool =
                 del _ROUND_STATS[key]
 
 
+def _mark_consistent(payload: "WarpDivPayload") -> "WarpDivPayload":
+    """Record that ``payload.packed``'s header agrees with ``max_rounds`` and
+    the metadata: the payload was written by this library's encoder, or its
+    round table was read from that header and the other header words were
+    compared on the host.  Such a payload is decoded without the GPU header
+    check and its host synchronisation; an in-place change of either tensor
+    (seen through the version counter; inference tensors have none) drops
+    the mark."""
+    object.__setattr__(payload, "_consistent", (_version(payload.packed), payload.packed.data_ptr(),
+                                                _version(payload.max_rounds), payload.max_rounds.data_ptr()))
+    return payload
+
+
+def _is_consistent(payload: "WarpDivPayload") -> bool:
+    tag = getattr(payload, "_consistent", None)
+    return tag is not None and tag == (_version(payload.packed), payload.packed.data_ptr(),
+                                       _version(payload.max_rounds), payload.max_rounds.data_ptr())
+
+
 def _round_stats(max_rounds: torch.Tensor) -> tuple[bool, int]:
     """(all rounds >= 2, sum of rounds)."""
     with _STATS_LOCK:
@@ -181,10 +200,19 @@ class WarpDivPayload:
         dev = torch.device(device)
         max_rounds = rounds.to(torch.uint32).to(dev, non_blocking=False)
         packed = packed_host.to(dev)
-        _remember_rounds(max_rounds, int(rounds.to(torch.int64).sum()), all_ok=bool((rounds >= 2).all()))
-        return cls(packed=packed, max_rounds=max_rounds, header_bytes=header_bytes, chunk_len=chunk_len, p_ch=p_ch,
-                   batch=batch, symbols_per_batch=symbols_per_batch, cdf_count=cdf_count,
-                   coding_fingerprint=coding_fingerprint, format_version=format_version)
+        total = int(rounds.to(torch.int64).sum())
+        _remember_rounds(max_rounds, total, all_ok=bool((rounds >= 2).all()))
+        payload = cls(packed=packed, max_rounds=max_rounds, header_bytes=header_bytes, chunk_len=chunk_len,
+                      p_ch=p_ch, batch=batch, symbols_per_batch=symbols_per_batch, cdf_count=cdf_count,
+                      coding_fingerprint=coding_fingerprint, format_version=format_version)
+        # the round table came from the header; when the other header words
+        # and the length agree with the metadata too, the GPU need not check
+        h = packed_host[:32].view(torch.int32).tolist()
+        if (batch < 32768 and h[0] == symbols_per_batch and h[1] == chunk_len and h[2] == (K | (batch << 16))
+                and h[3] == (2 | (32 << 16)) and header_bytes == (32 + 4 * n + 15) // 16 * 16
+                and packed_host.numel() == header_bytes + 128 * total):
+            _mark_consistent(payload)
+        return payload
 
 
 # ---------------------------------------------------------------------------
@@ -328,7 +356,7 @@ class WarpDivBackend:
         _remember_rounds(r.max_rounds, (r.packed.numel() - r.header_bytes) // 128)
         fingerprint = _coding_fingerprint(indexes, cdfs, cdf_sizes, offsets, channel_layout=r.index_layout_is_channel,
                                           batch=B, symbols_per_batch=N)
-        return WarpDivPayload(
+        return _mark_consistent(WarpDivPayload(
             packed=r.packed,
             max_rounds=r.max_rounds,
             header_bytes=r.header_bytes,
@@ -338,7 +366,7 @@ class WarpDivBackend:
             symbols_per_batch=N,
             cdf_count=int(cdfs.shape[0]),
             coding_fingerprint=fingerprint,
-        )
+        ))
 
     def _encode_latent(self, y: torch.Tensor, medians: torch.Tensor, cdfs, cdf_sizes, offsets,
                        p_ch: int) -> WarpDivPayload:
@@ -351,7 +379,7 @@ class WarpDivBackend:
         B = int(y.shape[0])
         N = int(y.numel() // B)
         _remember_rounds(r.max_rounds, (r.packed.numel() - r.header_bytes) // 128)
-        return WarpDivPayload(
+        return _mark_consistent(WarpDivPayload(
             packed=r.packed,
             max_rounds=r.max_rounds,
             header_bytes=r.header_bytes,
@@ -361,7 +389,7 @@ class WarpDivBackend:
             symbols_per_batch=N,
             cdf_count=int(cdfs.shape[0]),
             coding_fingerprint=_coding_fingerprint(None, cdfs, cdf_sizes, offsets, batch=B, symbols_per_batch=N),
-        )
+        ))
 
     def _decode_latent(self, payload: WarpDivPayload, cdfs, cdf_sizes, offsets, medians: torch.Tensor,
                        out: torch.Tensor) -> torch.Tensor:
@@ -376,8 +404,11 @@ class WarpDivBackend:
         if payload.batch >= 32768:
             raise CoderInputError("warp_div packed header is inconsistent with payload metadata")
         try:
+            # payloads known to be consistent decode asynchronously (no header
+            # check on the GPU, so no host synchronisation)
             return self._extension.decode_latent(payload.packed, payload.max_rounds, payload.header_bytes,
-                                                 payload.chunk_len, cdfs, cdf_sizes, offsets, medians, out)
+                                                 payload.chunk_len, cdfs, cdf_sizes, offsets, medians, out,
+                                                 check=not _is_consistent(payload))
         except (_native.NativeCallError, RuntimeError) as exc:
             _raise_coder_error(exc, "decode")
 
