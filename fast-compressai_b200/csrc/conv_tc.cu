@@ -18,12 +18,16 @@
 //
 // CTA organisation (persistent, one CTA per SM):
 //   warps 0-3   epilogue: TMEM -> registers, bias, GDN/IGDN, store
-//   warp 4      TMA producer (one lane)
-//   warp 5      MMA issuer (one lane); owns the TMEM allocation
-//   warps 6-9   gather producers (first analysis layer only)
-// A 4-stage shared-memory ring (mbarrier full/empty pairs) feeds the MMAs;
-// two TMEM accumulator buffers let the epilogue of tile j overlap the main
-// loop of tile j + 1.
+//   warps 4-7   second epilogue group (first and scatter layers: the two
+//               groups take alternate tiles)
+//   warp 8      TMA producer
+//   warp 9      MMA issuer; owns the TMEM allocation
+//   warps 10-13 gather producers (first analysis layer only)
+// The producer and MMA loops run on the whole warp, one elected lane issuing
+// each instruction (first layer: on lane 0).  A shared-memory ring of as many
+// stages as the free shared memory holds (mbarrier full/empty pairs) feeds
+// the MMAs; two TMEM accumulator buffers let the epilogue of tile j overlap
+// the main loop of tile j + 1.
 //
 // GDN fusion: the epilogue writes x^2 (bf16) of its 128 x 128 tile into
 // shared memory in the MMA operand layout and issues a second GEMM
@@ -154,6 +158,11 @@ struct Layout {
     // column split between the two epilogue warps of a lane quarter
     static constexpr int kSplit = kEpiWarps == 8 && !kPingPong && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
     static constexpr int kGroups = kPingPong ? 2 : 1;
+    // Producer and MMA loops run on the whole warp (warp-uniform operands,
+    // one elected lane issues) where TMA feeds the operand ring; the first
+    // layer, whose epilogue and gather warps bound it, keeps them on one lane
+    // so that its loops take fewer issue slots from those warps.
+    static constexpr bool kWarpIssue = !kGather;
     static constexpr int kGroupThreads = kEpiThreads / kGroups;
     static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
@@ -182,6 +191,36 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// One lane (W = false) or the whole warp (W = true) runs the calling loop.
+template <bool W>
+__device__ __forceinline__ bool wait_for(uint64_t *bar, uint32_t parity, volatile int *abort, bool cluster = false) {
+    return W ? mbar_wait_warp(bar, parity, abort, kWaitNs, cluster) : mbar_wait(bar, parity, abort, kWaitNs, cluster);
+}
+template <bool W>
+__device__ __forceinline__ bool aborted(volatile int *abort) {
+    return W ? __any_sync(0xffffffffu, *abort != 0) : *abort != 0;
+}
+template <bool W>
+__device__ __forceinline__ void mma_issue(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (W) mma_bf16_w(d, a, b, idesc, acc);
+    else mma_bf16(d, a, b, idesc, acc);
+}
+template <bool W>
+__device__ __forceinline__ void mma_issue_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (W) mma_bf16_pair_w(d, a, b, idesc, acc);
+    else mma_bf16_pair(d, a, b, idesc, acc);
+}
+template <bool W>
+__device__ __forceinline__ void commit_to(uint64_t *bar) {
+    if (W) mma_commit_w(bar);
+    else mma_commit(bar);
+}
+template <bool W>
+__device__ __forceinline__ void commit_pair_to(uint64_t *bar) {
+    if (W) mma_commit_pair_both_w(bar, 3);
+    else mma_commit_pair_both(bar, 3);
 }
 
 __device__ __forceinline__ void fail(const ConvParams &p, volatile int *abort, int code) {
@@ -272,6 +311,10 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
+        // one-time operands from lane 0; the operand ring from the whole warp
+        // (one elected lane issues each load); the first layer's input
+        // windows from lane 0
+        constexpr uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
         if (lane == 0) {
             if (!kGather) {
                 tma_prefetch_desc(&tmA);
@@ -279,8 +322,6 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             } else if (p.patch_tma) {
                 tma_prefetch_desc(&tmA);
             }
-            // one-time operands: gamma (GDN) and the first layer's weights
-            uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
             if (cbytes) {
                 mbar_arrive_expect_tx(cbar, cbytes);
                 if (kNorm) {  // pairs: this CTA's half of the gamma rows
@@ -289,89 +330,100 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 }
                 if (kGather) bulk_load(smem + Lay::offW, p.wgather, Lay::kW, cbar);
             }
-            if (!kGather) {
-                uint32_t it = 0;
-                int last_round[kStages];
-                for (int s = 0; s < kStages; ++s) last_round[s] = -1;
-                for (int tile = unit0; tile < p.tiles_total && !*abort; tile += unit_step) {
-                    int b, ph, gy0, gx0;
-                    tile_coords(p, tile, b, ph, gy0, gx0);
-                    gx0 += sub_x;
-                    const Taps &tp = p.taps[ph];
-                    for (int t = 0; t < tp.n && !*abort; ++t) {
-                        const int ix = gx0 * p.stride + tp.dx[t];
-                        const int iy = gy0 * p.stride + tp.dy[t];
-                        for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
-                            const int s = it % kStages;
-                            const uint32_t r = it / kStages;
-                            if (!mbar_wait(&empty[s], (r & 1) ^ 1, abort, kWaitNs)) {
-                                fail(p, abort, kErrProducer);
-                                break;
-                            }
-                            unsigned char *st = smem + s * Lay::kStage;
-                            if (kPair) {
+        }
+        __syncwarp();
+        if (!kGather) {
+            static_assert(kGather || Lay::kWarpIssue, "the operand ring is fed warp-wide");
+            uint32_t it = 0;
+            int last_round[kStages];
+            for (int s = 0; s < kStages; ++s) last_round[s] = -1;
+            bool stop = false;
+            for (int tile = unit0; tile < p.tiles_total && !stop; tile += unit_step) {
+                int b, ph, gy0, gx0;
+                tile_coords(p, tile, b, ph, gy0, gx0);
+                gx0 += sub_x;
+                const Taps &tp = p.taps[ph];
+                for (int t = 0; t < tp.n && !stop; ++t) {
+                    const int ix = gx0 * p.stride + tp.dx[t];
+                    const int iy = gy0 * p.stride + tp.dy[t];
+                    for (int cb = 0; cb < p.cin_blocks; ++cb, ++it) {
+                        const int s = it % kStages;
+                        const uint32_t r = it / kStages;
+                        if (!wait_for<true>(&empty[s], (r & 1) ^ 1, abort)) {
+                            if (lane == 0) fail(p, abort, kErrProducer);
+                            stop = true;
+                            break;
+                        }
+                        unsigned char *st = smem + s * Lay::kStage;
+                        if (kPair) {
+                            if (lane == 0) {
                                 // both CTAs' bytes count on the leader's full[s]
                                 const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
                                 if (leader) mbar_arrive_expect_tx(&full[s], 2 * Lay::kStage);
                                 tma_load_4d_pair(st, &tmA, fb, cb * kBK, ix, iy, b);
                                 tma_load_3d_pair(st + Lay::kA, &tmW, fb, cb * kBK, (int)rank * Lay::kNB, tp.w[t]);
-                            } else {
-                                mbar_arrive_expect_tx(&full[s], Lay::kStage);
-                                tma_load_4d(st, &tmA, &full[s], cb * kBK, ix, iy, b);
-                                tma_load_3d(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
                             }
-                            last_round[s] = (int)r;
+                            __syncwarp();
+                        } else {
+                            mbar_arrive_expect_tx_w(&full[s], Lay::kStage);
+                            tma_load_4d_w(st, &tmA, &full[s], cb * kBK, ix, iy, b);
+                            tma_load_3d_w(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
                         }
+                        last_round[s] = (int)r;
                     }
                 }
-                if (*abort && leader) {
-                    // let the loads in flight land before the CTA exits (pairs:
-                    // the leader's full[s] also counts the peer's loads)
-                    for (int s = 0; s < kStages; ++s)
-                        if (last_round[s] >= 0) mbar_wait(&full[s], (uint32_t)last_round[s] & 1, nullptr, kWaitNs / 10);
-                }
+                if (aborted<true>(abort)) stop = true;
             }
-            if (kGather && p.patch_tma) {
-                // input windows: patch buffer it % 2 for the CTA's it-th tile
-                uint32_t it = 0;
-                int last_round[2] = {-1, -1};
-                for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
-                    int b, ph, gy0, gx0;
-                    tile_coords(p, tile, b, ph, gy0, gx0);
-                    const int pb = it & 1;
-                    const uint32_t r = it >> 1;
-                    if (!mbar_wait(&pempty[pb], (r & 1) ^ 1, abort, kWaitNs)) {
-                        fail(p, abort, kErrProducer);
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&pfull[pb], p.patch_bytes);
-                    // x starts 4 columns left of the window's first input column
-                    // (2 gx0 - 2): a multiple of 4 floats, as TMA requires; the
-                    // rows above / columns left of the image read as zeros
-                    tma_load_4d(smem + Lay::offPatch + pb * kPatchBuf, &tmA, &pfull[pb], 2 * gx0 - 4, 2 * gy0 - 2, 0,
-                                b);
-                    last_round[pb] = (int)r;
-                }
-                if (*abort) {
-                    for (int pb = 0; pb < 2; ++pb)
-                        if (last_round[pb] >= 0)
-                            mbar_wait(&pfull[pb], (uint32_t)last_round[pb] & 1, nullptr, kWaitNs / 10);
-                }
+            if (lane == 0 && *abort && leader) {
+                // let the loads in flight land before the CTA exits (pairs:
+                // the leader's full[s] also counts the peer's loads)
+                for (int s = 0; s < kStages; ++s)
+                    if (last_round[s] >= 0) mbar_wait(&full[s], (uint32_t)last_round[s] & 1, nullptr, kWaitNs / 10);
             }
-            if (cbytes && *abort) mbar_wait(cbar, 0, nullptr, kWaitNs / 10);
         }
+        if (kGather && p.patch_tma && lane == 0) {
+            // input windows: patch buffer it % 2 for the CTA's it-th tile
+            uint32_t it = 0;
+            int last_round[2] = {-1, -1};
+            for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
+                int b, ph, gy0, gx0;
+                tile_coords(p, tile, b, ph, gy0, gx0);
+                const int pb = it & 1;
+                const uint32_t r = it >> 1;
+                if (!mbar_wait(&pempty[pb], (r & 1) ^ 1, abort, kWaitNs)) {
+                    fail(p, abort, kErrProducer);
+                    break;
+                }
+                mbar_arrive_expect_tx(&pfull[pb], p.patch_bytes);
+                // x starts 4 columns left of the window's first input column
+                // (2 gx0 - 2): a multiple of 4 floats, as TMA requires; the
+                // rows above / columns left of the image read as zeros
+                tma_load_4d(smem + Lay::offPatch + pb * kPatchBuf, &tmA, &pfull[pb], 2 * gx0 - 4, 2 * gy0 - 2, 0,
+                            b);
+                last_round[pb] = (int)r;
+            }
+            if (*abort) {
+                for (int pb = 0; pb < 2; ++pb)
+                    if (last_round[pb] >= 0)
+                        mbar_wait(&pfull[pb], (uint32_t)last_round[pb] & 1, nullptr, kWaitNs / 10);
+            }
+        }
+        if (lane == 0 && cbytes && *abort) mbar_wait(cbar, 0, nullptr, kWaitNs / 10);
+        __syncwarp();
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        // (pairs: the leader alone; its commits arrive in both CTAs)
-        if (lane == 0 && leader) {
+        // Lane 0, or the whole warp with one elected lane issuing (kWarpIssue);
+        // pairs: the leader CTA alone, whose commits arrive in both CTAs.
+        constexpr bool W = Lay::kWarpIssue;
+        if (leader && (W || lane == 0)) {
             const uint32_t idesc = idesc_bf16(kPair ? 2 * kBM : kBM, kNpad);
             bool consts = !kGather;
             uint32_t it = 0;
             int j = 0;
-            for (int tile = unit0; tile < p.tiles_total && !*abort; tile += unit_step, ++j) {
+            for (int tile = unit0; tile < p.tiles_total && !aborted<W>(abort); tile += unit_step, ++j) {
                 if (!consts) {
-                    if (!mbar_wait(cbar, 0, abort, kWaitNs)) {
-                        fail(p, abort, kErrMma);
+                    if (!wait_for<W>(cbar, 0, abort)) {
+                        if (lane == 0) fail(p, abort, kErrMma);
                         break;
                     }
                     consts = true;
@@ -380,8 +432,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 tile_coords(p, tile, b, ph, gy0, gx0);
                 const int buf = j & 1;
                 const uint32_t use = j >> 1;
-                if (!mbar_wait(&acce[buf], (use & 1) ^ 1, abort, kWaitNs, kPair)) {
-                    fail(p, abort, kErrMma);
+                if (!wait_for<W>(&acce[buf], (use & 1) ^ 1, abort, kPair)) {
+                    if (lane == 0) fail(p, abort, kErrMma);
                     break;
                 }
                 tc_fence_after();
@@ -391,8 +443,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 for (int ks = 0; ks < ksteps; ++ks, ++it) {
                     const int s = it % kStages;
                     const uint32_t r = it / kStages;
-                    if (!mbar_wait(&full[s], r & 1, abort, kWaitNs)) {
-                        fail(p, abort, kErrMma);
+                    if (!wait_for<W>(&full[s], r & 1, abort)) {
+                        if (lane == 0) fail(p, abort, kErrMma);
                         ok = false;
                         break;
                     }
@@ -402,29 +454,30 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         const uint32_t w0 = smem_u32(smem + Lay::offW);
 #pragma unroll
                         for (int kk = 0; kk < kGatherK / 16; ++kk)
-                            mma_bf16(d, smem_desc(a0 + kk * 256, 128, 1280, 0), smem_desc(w0 + kk * 256, 128, 1280, 0),
-                                     idesc, kk != 0);
+                            mma_issue<W>(d, smem_desc(a0 + kk * 256, 128, 1280, 0),
+                                         smem_desc(w0 + kk * 256, 128, 1280, 0), idesc, kk != 0);
                     } else if (kPair) {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk)
-                            mma_bf16_pair(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
-                                          idesc, (ks | kk) != 0);
+                            mma_issue_pair<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2),
+                                              smem_desc(b0 + kk * 32, 16, 1024, 2), idesc, (ks | kk) != 0);
                     } else {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk)
-                            mma_bf16(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
-                                     idesc, (ks | kk) != 0);
+                            mma_issue<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
+                                         idesc, (ks | kk) != 0);
                     }
                     // frees the stage (pairs: in both CTAs) once these MMAs have read it
-                    if (kPair) mma_commit_pair_both(&empty[s], 3);
-                    else mma_commit(&empty[s]);
+                    if (kPair) commit_pair_to<W>(&empty[s]);
+                    else commit_to<W>(&empty[s]);
                 }
                 if (!ok) break;
-                if (kPair) mma_commit_pair_both(&accf[buf], 3);
-                else mma_commit(&accf[buf]);
+                if (kPair) commit_pair_to<W>(&accf[buf]);
+                else commit_to<W>(&accf[buf]);
             }
+            if (W) __syncwarp();
         }
     } else if (warp < Lay::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
