@@ -129,7 +129,17 @@ struct Layout {
     static constexpr int kS = kPingPong ? 2 * kSOne : kSOne;
     // operand ring: as many stages as the shared memory left over holds
     // (more bytes in flight hide more of the TMA round trip)
-    static constexpr int kFixedBytes = kW + kG + kX2 +
+    // Constant operands (not the scatter layer): a 128 x 16 "ones" A tile
+    // (K columns 0 and 1 = 1.0) and B tiles holding, per output channel, the
+    // bias (and GDN beta) split into bf16 hi + lo parts in K columns 0 and 1.
+    // One K = 16 MMA of ones x bias starts each accumulation, and ones x beta
+    // starts each GDN norm, so the epilogue adds neither.
+    static constexpr bool kFold = kEpi != kEpiScatter;
+    static constexpr int kConstRow = 32;  // bytes per row of a K = 16 no-swizzle tile
+    static constexpr int kOnes = kFold ? kBM * kConstRow : 0;
+    static constexpr int kBiasB = kFold ? kNB * kConstRow : 0;
+    static constexpr int kBetaB = kFold && kNorm ? kNB * kConstRow : 0;
+    static constexpr int kFixedBytes = kOnes + kBiasB + kBetaB + kW + kG + kX2 +
                                        kS + (kGather ? 2 * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
     static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
@@ -140,7 +150,10 @@ struct Layout {
     static constexpr int offS = offX2 + kX2;
     static constexpr int kP = kGather ? 2 * kPatchBuf : 0;
     static constexpr int offPatch = offS + kS;
-    static constexpr int offBias = offPatch + kP;
+    static constexpr int offOnes = offPatch + kP;
+    static constexpr int offBiasB = offOnes + kOnes;
+    static constexpr int offBetaB = offBiasB + kBiasB;
+    static constexpr int offBias = offBetaB + kBetaB;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
     static constexpr int kBars = 2 * kStages + 8 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
@@ -167,6 +180,7 @@ struct Layout {
     static_assert(kEpi != kEpiScatter || kNpad == 25 * kScatterCout + 5, "scatter instance is built for cout = 3");
     static_assert(kA % 1024 == 0 || kGather, "A stage alignment");
     static_assert(offPatch % 128 == 0 && kPatchBuf % 128 == 0, "patch buffer alignment");
+    static_assert(offOnes % 128 == 0 && kOnes % 128 == 0 && kBiasB % 128 == 0, "constant tile alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
     static_assert(!kPair || (!kGather && kEpi != kEpiScatter && kNB % 8 == 0), "pair instances: TMA operands");
@@ -292,6 +306,34 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
     for (int i = threadIdx.x; i < kNpad; i += blockDim.x) {
         s_bias[i] = i < p.cout ? p.bias[i] : 0.f;
         if (kNorm) s_beta[i] = i < p.cout ? p.beta[i] : 1.f;
+    }
+    if (Lay::kFold) {
+        // no-swizzle K-major tiles: row r's K columns 0-7 at
+        // (r / 8) * 256 + (r % 8) * 16, columns 8-15 128 bytes further
+        for (int r = threadIdx.x; r < kBM + 2 * Lay::kNB; r += blockDim.x) {
+            uint32_t w0;
+            unsigned char *tile;
+            int row;
+            if (r < kBM) {
+                w0 = pack_bf16x2(1.f, 1.f);
+                tile = smem + Lay::offOnes;
+                row = r;
+            } else {
+                row = (r - kBM) % Lay::kNB;
+                const bool is_beta = r >= kBM + Lay::kNB;
+                if (is_beta && !kNorm) continue;
+                const int c = (int)rank * Lay::kNB + row;  // pairs: this CTA's half of the channels
+                const float v = is_beta ? (c < p.cout ? p.beta[c] : 1.f) : (c < p.cout ? p.bias[c] : 0.f);
+                const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+                const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+                w0 = (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
+                tile = smem + (is_beta ? Lay::offBetaB : Lay::offBiasB);
+            }
+            uint4 *q = reinterpret_cast<uint4 *>(tile + (row >> 3) * 256 + (row & 7) * 16);
+            q[0] = make_uint4(w0, 0u, 0u, 0u);
+            q[8] = make_uint4(0u, 0u, 0u, 0u);  // K columns 8-15, 128 bytes on
+        }
+        fence_proxy_async_smem();  // the tensor core reads these tiles
     }
     if (warp == kMmaWarp) {
         if (kPair) {
@@ -450,24 +492,33 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(smem + s * Lay::kStage);
+                    // the tile's accumulator starts as the bias (ones x bias)
+                    const bool first = ks == 0;
+                    if (Lay::kFold && first) {
+                        const uint64_t od = smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0);
+                        const uint64_t bd = smem_desc(smem_u32(smem + Lay::offBiasB), 128, 256, 0);
+                        if (kPair) mma_issue_pair<W>(d, od, bd, idesc, 0);
+                        else mma_issue<W>(d, od, bd, idesc, 0);
+                    }
+                    const bool fresh = first && !Lay::kFold;  // the first MMA overwrites the accumulator
                     if (kGather) {
                         const uint32_t w0 = smem_u32(smem + Lay::offW);
 #pragma unroll
                         for (int kk = 0; kk < kGatherK / 16; ++kk)
                             mma_issue<W>(d, smem_desc(a0 + kk * 256, 128, 1280, 0),
-                                         smem_desc(w0 + kk * 256, 128, 1280, 0), idesc, kk != 0);
+                                         smem_desc(w0 + kk * 256, 128, 1280, 0), idesc, !(fresh && kk == 0));
                     } else if (kPair) {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk)
                             mma_issue_pair<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2),
-                                              smem_desc(b0 + kk * 32, 16, 1024, 2), idesc, (ks | kk) != 0);
+                                              smem_desc(b0 + kk * 32, 16, 1024, 2), idesc, !(fresh && kk == 0));
                     } else {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk)
                             mma_issue<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
-                                         idesc, (ks | kk) != 0);
+                                         idesc, !(fresh && kk == 0));
                     }
                     // frees the stage (pairs: in both CTAs) once these MMAs have read it
                     if (kPair) commit_pair_to<W>(&empty[s]);
@@ -602,9 +653,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                             uint32_t w[4];
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
-                                const int c = c_lo + k * 16 + q * 8 + e * 2;
-                                const float a = __uint_as_float(v[k & 1][q * 8 + e * 2]) + s_bias[c];
-                                const float bb = __uint_as_float(v[k & 1][q * 8 + e * 2 + 1]) + s_bias[c + 1];
+                                const float a = __uint_as_float(v[k & 1][q * 8 + e * 2]);
+                                const float bb = __uint_as_float(v[k & 1][q * 8 + e * 2 + 1]);
                                 w[e] = pack_bf16x2(a * a, bb * bb);
                             }
                             const int k0 = c_lo + k * 16 + q * 8;
@@ -629,12 +679,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                             if (ok) {
                                 tc_fence_after();
                                 const uint32_t idesc = idesc_bf16(2 * kBM, kNpad);
+                                // norm = beta (ones x beta) + x^2 gamma^T
+                                mma_bf16_pair(d2, smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0),
+                                              smem_desc(smem_u32(smem + Lay::offBetaB), 128, 256, 0), idesc, 0);
 #pragma unroll
                                 for (int kk = 0; kk < kNpad / 16; ++kk) {
                                     const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
                                     const uint32_t goff = (kk / 4) * (Lay::kNB * 128) + (kk % 4) * 32;
                                     mma_bf16_pair(d2, smem_desc(x2 + koff, 16, 1024, 2),
-                                                  smem_desc(g0 + goff, 16, 1024, 2), idesc, kk != 0);
+                                                  smem_desc(g0 + goff, 16, 1024, 2), idesc, 1);
                                 }
                                 mma_commit_pair_both(g2, 3);
                             }
@@ -642,12 +695,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     } else {
                         tc_fence_after();
                         const uint32_t idesc = idesc_bf16(kBM, kNpad);
+                        // norm = beta (ones x beta) + x^2 gamma^T
+                        mma_bf16(d2, smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0),
+                                 smem_desc(smem_u32(smem + Lay::offBetaB), 128, 256, 0), idesc, 0);
 #pragma unroll
                         for (int kk = 0; kk < kNpad / 16; ++kk) {
                             const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
                             const uint32_t goff = (kk / 4) * (kNpad * 128) + (kk % 4) * 32;
                             mma_bf16(d2, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc,
-                                     kk != 0);
+                                     1);
                         }
                         mma_commit(g2);
                     }
@@ -679,16 +735,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         uint32_t o[8];
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
-                            const int c = c0 + 2 * e;
-                            const float n0 = __uint_as_float(nv[k & 1][2 * e]) + s_beta[c];
-                            const float n1 = __uint_as_float(nv[k & 1][2 * e + 1]) + s_beta[c + 1];
+                            const float n0 = __uint_as_float(nv[k & 1][2 * e]);
+                            const float n1 = __uint_as_float(nv[k & 1][2 * e + 1]);
                             float r0 = rsqrtf(n0), r1 = rsqrtf(n1);
                             if (kEpi == kEpiIgdn) {
                                 r0 *= n0;  // sqrt(n) = n * rsqrt(n)
                                 r1 *= n1;
                             }
-                            const float x0 = __uint_as_float(v[k & 1][2 * e]) + s_bias[c];
-                            const float x1 = __uint_as_float(v[k & 1][2 * e + 1]) + s_bias[c + 1];
+                            const float x0 = __uint_as_float(v[k & 1][2 * e]);
+                            const float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
                             o[e] = pack_bf16x2(x0 * r0, x1 * r1);
                         }
                         if (p.tma_store) {
@@ -731,8 +786,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     uint32_t o[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]) + s_bias[c0 + 2 * e],
-                                           __uint_as_float(v[2 * e + 1]) + s_bias[c0 + 2 * e + 1]);
+                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
                     if (valid) {
                         uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
                         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -752,7 +806,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         const int c = c0 + e;
-                        float y = __uint_as_float(v[e]) + s_bias[c];
+                        float y = __uint_as_float(v[e]);
                         if (kEpi == kEpiF32Clamp) y = fminf(fmaxf(y, 0.f), 1.f);
                         if (valid && c < p.cout) out[((int64_t)b * p.cout + c) * plane + pix] = y;
                     }
