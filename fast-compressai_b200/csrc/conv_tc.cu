@@ -99,7 +99,8 @@ struct ConvParams {
     int patch_tma;       // first layer: 1 = input windows by TMA (tmA maps x_in), 0 = direct loads
     int patch_w, patch_h;  // patch box: columns (2 TX + 8), rows (2 TY + 3)
     uint32_t patch_bytes;
-    int tma_store;       // GDN conv layers: the output tile leaves through TMA stores (tmO)
+    int tma_store;       // GDN layers: the output tile leaves through TMA stores (tmO); 1 = 4-D
+                         // NHWC box, 2 = transposed conv phase box (5-D view of the output)
     void *out;
     int *err;
 };
@@ -737,11 +738,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         for (int e = 0; e < 8; ++e) {
                             const float n0 = __uint_as_float(nv[k & 1][2 * e]);
                             const float n1 = __uint_as_float(nv[k & 1][2 * e + 1]);
-                            float r0 = rsqrtf(n0), r1 = rsqrtf(n1);
-                            if (kEpi == kEpiIgdn) {
-                                r0 *= n0;  // sqrt(n) = n * rsqrt(n)
-                                r1 *= n1;
-                            }
+                            // GDN: x / sqrt(n); IGDN: x * sqrt(n)
+                            const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
+                            const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
                             const float x0 = __uint_as_float(v[k & 1][2 * e]);
                             const float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
                             o[e] = pack_bf16x2(x0 * r0, x1 * r1);
@@ -770,8 +769,16 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     named_barrier_sync(gbar, Lay::kGroupThreads);
                     if (gleader) {
                         const unsigned char *stg = smem + Lay::offX2 + grp * Lay::kX2One;
-                        tma_store_4d(&tmO, stg, 0, gx0, gy0, b);
-                        tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, gy0, b);
+                        if (p.tma_store == 2) {
+                            // transposed conv: phase (py, px) of the output viewed as
+                            // [B * Hout / 2][py][Wout / 2][px][C]
+                            const int yrow = b * p.GH + gy0;
+                            tma_store_5d(&tmO, stg, 0, ph & 1, gx0, ph >> 1, yrow);
+                            tma_store_5d(&tmO, stg + kBM * 128, kBK, ph & 1, gx0, ph >> 1, yrow);
+                        } else {
+                            tma_store_4d(&tmO, stg, 0, gx0, gy0, b);
+                            tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, gy0, b);
+                        }
                         bulk_commit_group();
                     }
                 }
@@ -1231,16 +1238,28 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.err = err;
 
     CUtensorMap ma{}, mw{}, mg{}, mo{};
-    // GDN conv layers (one phase: output pixels of a tile are a dense box)
-    // write through TMA stores; the output base must be 16-byte aligned
-    p.tma_store = norm && !deconv && L->out_format == FCAI_FMT_NHWC_BF16 &&
-                  (reinterpret_cast<uintptr_t>(output) & 15) == 0 ? 1 : 0;
-    if (p.tma_store) {
+    // GDN layers with bf16 NHWC output write through TMA stores (the output
+    // base must be 16-byte aligned).  Conv: a tile's output pixels are a
+    // dense 4-D box.  Transposed conv: phase (py, px) of the output is the
+    // box [.., py, .., px, ..] of the 5-D view [B * Hout / 2][2][Wout / 2][2][C];
+    // its row dimension runs across images, so it is used only when no tile
+    // reaches past its image's last row (GH a multiple of TY).
+    const bool store_ok = norm && L->out_format == FCAI_FMT_NHWC_BF16 && (reinterpret_cast<uintptr_t>(output) & 15) == 0;
+    if (store_ok && !deconv) {
+        p.tma_store = 1;
         cuuint64_t od[4] = {(cuuint64_t)npad, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)batch};
         cuuint64_t os[3] = {(cuuint64_t)npad * 2, (cuuint64_t)wo * npad * 2, (cuuint64_t)ho * wo * npad * 2};
         cuuint32_t ob[4] = {(cuuint32_t)kBK, (cuuint32_t)p.TX, (cuuint32_t)p.TY, 1};
         cuuint32_t oe[4] = {1, 1, 1, 1};
         if ((rc = make_map(&mo, output, 4, od, os, ob, oe))) return rc;
+    } else if (store_ok && deconv && p.GH % p.TY == 0 && ho == 2 * p.GH && wo == 2 * p.GW) {
+        p.tma_store = 2;
+        cuuint64_t od[5] = {(cuuint64_t)npad, 2, (cuuint64_t)p.GW, 2, (cuuint64_t)batch * p.GH};
+        cuuint64_t os[4] = {(cuuint64_t)npad * 2, (cuuint64_t)2 * npad * 2, (cuuint64_t)wo * npad * 2,
+                            (cuuint64_t)2 * wo * npad * 2};
+        cuuint32_t ob[5] = {(cuuint32_t)kBK, 1, (cuuint32_t)p.TX, 1, (cuuint32_t)p.TY};
+        cuuint32_t oe[5] = {1, 1, 1, 1, 1};
+        if ((rc = make_map(&mo, output, 5, od, os, ob, oe))) return rc;
     }
     if (gather && p.patch_tma) {
         // fp32 NCHW image as [B][3][Hin][Win]; one box = one tile's window
