@@ -113,7 +113,13 @@ template <int kNpad, int kEpi, bool kGather, bool kPair = false>
 struct Layout {
     static constexpr bool kNorm = kEpi == kEpiGdn || kEpi == kEpiIgdn;
     static constexpr int kNB = kPair ? kNpad / 2 : kNpad;  // B / gamma rows this CTA holds
-    static constexpr int kA = kGather ? kBM * kGatherK * 2 : kBM * kBK * 2;
+    // Dual tiles (GDN / IGDN layers fed by TMA): a tile is 256 output
+    // pixels, one A box of 256 rows per K step, and each K step issues two
+    // M = 128 MMAs that share the B tile, so each byte of weights loaded
+    // feeds twice the MMA work.
+    static constexpr bool kDual = kNorm && !kGather && !kPair;
+    static constexpr int kRows = kDual ? 2 * kBM : kBM;  // output pixels per tile
+    static constexpr int kA = kGather ? kBM * kGatherK * 2 : kRows * kBK * 2;
     static constexpr int kB = kGather ? 0 : kNB * kBK * 2;
     static constexpr int kStage = kA + kB;
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
@@ -167,7 +173,7 @@ struct Layout {
     // layer (fewer warps competing with the MMA warp for issue slots), two
     // (column halves) where the epilogue is the heavy part: the first layer
     // (K = 80) and the scatter layer.
-    static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter) ? 8 : 4;
+    static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter || kDual) ? 8 : 4;
     static constexpr int kEpiThreads = kEpiWarps * 32;
     // column split between the two epilogue warps of a lane quarter
     static constexpr int kSplit = kEpiWarps == 8 && !kPingPong && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
@@ -294,7 +300,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         mbar_init(&g2bar[0], 1);
         mbar_init(&g2bar[1], 1);
         mbar_init(cbar, 1);
-        mbar_init(dbar, 1 + Lay::kGroups);  // the MMA thread and each epilogue group's leader
+        // the MMA thread and each epilogue thread that issues GDN GEMMs
+        mbar_init(dbar, 1 + ((Lay::kPingPong || Lay::kDual) ? 2 : 1));
         if (kGather) {
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&pfull[b], 1);
@@ -500,6 +507,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         const uint64_t bd = smem_desc(smem_u32(smem + Lay::offBiasB), 128, 256, 0);
                         if (kPair) mma_issue_pair<W>(d, od, bd, idesc, 0);
                         else mma_issue<W>(d, od, bd, idesc, 0);
+                        if (Lay::kDual) mma_issue<W>(d + kBM, od, bd, idesc, 0);  // second half's columns
                     }
                     const bool fresh = first && !Lay::kFold;  // the first MMA overwrites the accumulator
                     if (kGather) {
@@ -517,9 +525,14 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     } else {
                         const uint32_t b0 = a0 + Lay::kA;
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk)
-                            mma_issue<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2), smem_desc(b0 + kk * 32, 16, 1024, 2),
-                                         idesc, !(fresh && kk == 0));
+                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                            const uint64_t bd = smem_desc(b0 + kk * 32, 16, 1024, 2);
+                            mma_issue<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2), bd, idesc, !(fresh && kk == 0));
+                            // dual tiles: rows 128-255 of A into the second half's columns
+                            if (Lay::kDual)
+                                mma_issue<W>(d + kBM, smem_desc(a0 + kBM * 128 + kk * 32, 16, 1024, 2), bd, idesc,
+                                             !(fresh && kk == 0));
+                        }
                     }
                     // frees the stage (pairs: in both CTAs) once these MMAs have read it
                     if (kPair) commit_pair_to<W>(&empty[s]);
@@ -533,6 +546,157 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         }
     } else if (warp < Lay::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
+        if constexpr (Lay::kDual) {
+            // Dual tiles: rows 0-127 of the tile (TMEM columns [0, 128) of the
+            // buffer) belong to group 0 (warps 0-3), rows 128-255 (columns
+            // [128, 256)) to group 1 (warps 4-7).  Each thread keeps its
+            // pixel's 128 conv outputs in registers, so the GDN GEMM writes
+            // the norm over them in TMEM.  The groups use the one x^2 /
+            // staging tile in turn, group 0 first.  Named barriers: 1 + h
+            // (group h), 3 (all 256 threads, tile start), 4 (group 0 hands the
+            // tile to group 1).  No thread leaves the loop between the tile
+            // start and its end, so every barrier always meets all its threads.
+            const int h = warp >> 2;
+            const int m = threadIdx.x & 127;
+            const bool hleader = m == 0;
+            const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+            const uint32_t x2 = smem_u32(smem + Lay::offX2);
+            volatile int *t_ok = epi_ok;
+            volatile int *h_ok = epi_ok + 1 + h;
+            bool consts = false;
+            int j = 0;
+            for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
+                int b, ph, gy0, gx0;
+                tile_coords(p, tile, b, ph, gy0, gx0);
+                const int buf = j & 1;
+                const uint32_t use = j >> 1;
+                if (threadIdx.x == 0) {
+                    bool ok = !*abort;
+                    if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
+                    if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
+                    if (!ok) fail(p, abort, kErrEpilogue);
+                    *t_ok = ok ? 1 : 0;
+                }
+                // group 1's leader saw its stores read the x^2 tile before it got here
+                named_barrier_sync(3, 2 * kBM);
+                if (!*t_ok) break;
+                consts = true;
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + buf * p.buf_stride + h * kBM;  // this half's columns
+                uint32_t xv[kNpad / 16][16];
+#pragma unroll
+                for (int k = 0; k < kNpad / 16; ++k) tmem_ld16(dcol + lane_addr + k * 16, xv[k]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < kNpad / 16; ++k) tmem_regs_ready(xv[k]);
+                if (h == 1) named_barrier_sync(4, 2 * kBM);  // group 0 is done with the tile
+                // x^2 (bf16) into the 128-byte-swizzled operand tile
+#pragma unroll
+                for (int k = 0; k < kNpad / 16; ++k) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float a = __uint_as_float(xv[k][q * 8 + 2 * e]);
+                            const float c = __uint_as_float(xv[k][q * 8 + 2 * e + 1]);
+                            w[e] = pack_bf16x2(a * a, c * c);
+                        }
+                        const int k0 = k * 16 + q * 8;
+                        const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                        st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
+                                     w[3]);
+                    }
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();  // the TMEM loads above precede the GEMM that overwrites those columns
+                named_barrier_sync(1 + h, kBM);
+                if (hleader) {
+                    tc_fence_after();
+                    const uint32_t g0 = smem_u32(smem + Lay::offG);
+                    const uint32_t idesc = idesc_bf16(kBM, kNpad);
+                    // norm = beta (ones x beta) + x^2 gamma^T, over this half's conv outputs
+                    mma_bf16(dcol, smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0),
+                             smem_desc(smem_u32(smem + Lay::offBetaB), 128, 256, 0), idesc, 0);
+#pragma unroll
+                    for (int kk = 0; kk < kNpad / 16; ++kk) {
+                        const uint32_t koff = (kk / 4) * (kBM * 128) + (kk % 4) * 32;
+                        const uint32_t goff = (kk / 4) * (kNpad * 128) + (kk % 4) * 32;
+                        mma_bf16(dcol, smem_desc(x2 + koff, 16, 1024, 2), smem_desc(g0 + goff, 16, 1024, 2), idesc, 1);
+                    }
+                    mma_commit(&g2bar[h]);
+                    const bool ok = mbar_wait(&g2bar[h], j & 1, abort, kWaitNs);
+                    if (!ok) fail(p, abort, kErrEpilogue);
+                    *h_ok = ok ? 1 : 0;
+                }
+                named_barrier_sync(1 + h, kBM);
+                const bool hok = *h_ok != 0;
+                tc_fence_after();
+                if (hok) {
+                    // y = x * rsqrt(norm) (IGDN: x * sqrt(norm)) into the staging tile
+                    // (the GEMM has read x^2), or straight to global memory
+                    const int row = h * kBM + m;
+                    const int ty = row / p.TX, tx = row - ty * p.TX;
+                    const int gy = gy0 + ty, gx = gx0 + tx;
+                    const bool valid = gy < p.GH && gx < p.GW;
+                    const int oy = gy * p.out_step + (p.phases == 4 ? (ph >> 1) : 0);
+                    const int ox = gx * p.out_step + (p.phases == 4 ? (ph & 1) : 0);
+                    __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
+                                          (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
+                    uint32_t nv[2][16];
+                    tmem_ld16(dcol + lane_addr, nv[0]);
+#pragma unroll
+                    for (int k = 0; k < kNpad / 16; ++k) {
+                        tmem_wait_ld();
+                        tmem_regs_ready(nv[k & 1]);
+                        if (k + 1 < kNpad / 16) tmem_ld16(dcol + lane_addr + (k + 1) * 16, nv[(k + 1) & 1]);
+                        uint32_t o[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float n0 = __uint_as_float(nv[k & 1][2 * e]);
+                            const float n1 = __uint_as_float(nv[k & 1][2 * e + 1]);
+                            const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
+                            const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
+                            o[e] = pack_bf16x2(__uint_as_float(xv[k][2 * e]) * r0, __uint_as_float(xv[k][2 * e + 1]) * r1);
+                        }
+                        if (p.tma_store) {
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                const int k0 = k * 16 + q * 8;
+                                const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                                st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), o[q * 4],
+                                             o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+                            }
+                        } else if (valid) {
+                            uint4 *dst = reinterpret_cast<uint4 *>(orow + k * 16);
+                            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                        }
+                    }
+                }
+                fence_proxy_async_smem();
+                named_barrier_sync(1 + h, kBM);
+                if (hleader && hok && p.tma_store) {
+                    // this half: TY / 2 rows of the tile, 64 channels per box
+                    const unsigned char *stg = smem + Lay::offX2;
+                    const int hy = gy0 + h * (p.TY / 2);
+                    if (p.tma_store == 2) {
+                        const int yrow = b * p.GH + hy;
+                        tma_store_5d(&tmO, stg, 0, ph & 1, gx0, ph >> 1, yrow);
+                        tma_store_5d(&tmO, stg + kBM * 128, kBK, ph & 1, gx0, ph >> 1, yrow);
+                    } else {
+                        tma_store_4d(&tmO, stg, 0, gx0, hy, b);
+                        tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, hy, b);
+                    }
+                    bulk_commit_group();
+                }
+                tc_fence_before();
+                mbar_arrive(&acce[buf]);  // this thread is done with the accumulator
+                if (hleader && p.tma_store) bulk_wait_read_all();  // the staging tile may be rewritten
+                if (h == 0) named_barrier_arrive(4, 2 * kBM);
+            }
+            if (hleader && p.tma_store) bulk_wait_all();  // stores complete before the CTA exits
+        } else {
         // Warp w reads TMEM lanes 32*(w%4).. (tile rows); with 8 warps either
         // column half w/4 of every tile, or (ping-pong) all columns of the
         // tiles of group w/4.  A group's first thread alone waits on the
@@ -832,6 +996,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             named_barrier_sync(gbar, Lay::kGroupThreads);
         }
         if (kNorm && p.tma_store && gleader) bulk_wait_all();  // stores complete before the CTA exits
+        }
     } else if (kGather) {
         // ------------------------------------------------------------ gather (first layer)
         const int m = threadIdx.x - kGatherThread0;
@@ -916,7 +1081,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         // the two threads that issue MMAs (MMA lane, epilogue thread 0) commit
         // to dbar; TMEM is freed only once everything they issued completed
         if ((warp == kMmaWarp && lane == 0) || threadIdx.x == 0 ||
-            (Lay::kPingPong && threadIdx.x == Lay::kGroupThreads)) {
+            ((Lay::kPingPong || Lay::kDual) && threadIdx.x == kBM)) {
             if (kPair) mma_commit_pair(dbar);
             else mma_commit(dbar);
         }
@@ -1131,6 +1296,8 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         L->algorithm != FCAI_ALGO_IMPLICIT_GEMM_PAIR)
         return fcai::fail(FCAI_ERR_INVALID, "unknown layer algorithm %d", (int)L->algorithm);
     const bool pair = L->algorithm == FCAI_ALGO_IMPLICIT_GEMM_PAIR;
+    // the kernel instance takes 256-pixel dual tiles exactly when this holds
+    const bool dual = norm && !gather && !pair;
     if (pair && (gather || npad != L->cout || (npad != 128 && npad != 192)))
         return fcai::fail(FCAI_ERR_INVALID, "CTA-pair layers take bf16 NHWC input and 128 or 192 output channels");
     if (scatter && (!deconv || L->cout > 10 || npad != (25 * L->cout + 15) / 16 * 16 || norm ||
@@ -1168,7 +1335,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         } else {
             p.TX = pick_tx(p.GW, patch ? kPatchMaxTX : 128);
         }
-        p.TY = kBM / p.TX;
+        p.TY = (dual ? 2 * kBM : kBM) / p.TX;
         p.step_x = pair ? 2 * p.TX : p.TX;
         p.step_y = p.TY;
         if (patch) {
@@ -1245,11 +1412,13 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     // its row dimension runs across images, so it is used only when no tile
     // reaches past its image's last row (GH a multiple of TY).
     const bool store_ok = norm && L->out_format == FCAI_FMT_NHWC_BF16 && (reinterpret_cast<uintptr_t>(output) & 15) == 0;
+    // dual tiles store each 128-row half on its own: TY / 2 rows
+    const int box_rows = dual ? p.TY / 2 : p.TY;
     if (store_ok && !deconv) {
         p.tma_store = 1;
         cuuint64_t od[4] = {(cuuint64_t)npad, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)batch};
         cuuint64_t os[3] = {(cuuint64_t)npad * 2, (cuuint64_t)wo * npad * 2, (cuuint64_t)ho * wo * npad * 2};
-        cuuint32_t ob[4] = {(cuuint32_t)kBK, (cuuint32_t)p.TX, (cuuint32_t)p.TY, 1};
+        cuuint32_t ob[4] = {(cuuint32_t)kBK, (cuuint32_t)p.TX, (cuuint32_t)box_rows, 1};
         cuuint32_t oe[4] = {1, 1, 1, 1};
         if ((rc = make_map(&mo, output, 4, od, os, ob, oe))) return rc;
     } else if (store_ok && deconv && p.GH % p.TY == 0 && ho == 2 * p.GH && wo == 2 * p.GW) {
@@ -1257,7 +1426,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         cuuint64_t od[5] = {(cuuint64_t)npad, 2, (cuuint64_t)p.GW, 2, (cuuint64_t)batch * p.GH};
         cuuint64_t os[4] = {(cuuint64_t)npad * 2, (cuuint64_t)2 * npad * 2, (cuuint64_t)wo * npad * 2,
                             (cuuint64_t)2 * wo * npad * 2};
-        cuuint32_t ob[5] = {(cuuint32_t)kBK, 1, (cuuint32_t)p.TX, 1, (cuuint32_t)p.TY};
+        cuuint32_t ob[5] = {(cuuint32_t)kBK, 1, (cuuint32_t)p.TX, 1, (cuuint32_t)box_rows};
         cuuint32_t oe[5] = {1, 1, 1, 1, 1};
         if ((rc = make_map(&mo, output, 5, od, os, ob, oe))) return rc;
     }

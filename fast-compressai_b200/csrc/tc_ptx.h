@@ -129,6 +129,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// Arrives on the named barrier without waiting (the threads that bar.sync on
+// it wait for these arrivals too).
+__device__ __forceinline__ void named_barrier_arrive(uint32_t id, uint32_t threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // PTX approximate square root and reciprocal square root (flush-to-zero;
 // inputs here are at least the GDN beta, far above the subnormal range).
