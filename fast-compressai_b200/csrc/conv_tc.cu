@@ -63,6 +63,7 @@ constexpr int kGatherThreads = 128;
 // scatter layers: 8 x 16 input pixels per tile, of which the 6 x 14 core
 // produces a 12 x 28 output block; cout = 3 (25 taps x 3 = 75 -> npad 80)
 constexpr int kScatterTY = 8, kScatterTX = 16, kScatterCoreH = 6, kScatterCoreW = 14, kScatterCout = 3;
+constexpr int kScatterMaxCinBlocks = 4;  // scatter layers keep their weights resident: cin <= 256
 constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
 // First layer, patch path: the tile's fp32 input window (3 channels x
 // (2 TY + 3) rows x (2 TX + 8) columns, TX <= 64) arrives by one TMA load
@@ -120,7 +121,11 @@ struct Layout {
     static constexpr bool kDual = kNorm && !kGather && !kPair;
     static constexpr int kRows = kDual ? 2 * kBM : kBM;  // output pixels per tile
     static constexpr int kA = kGather ? kBM * kGatherK * 2 : kRows * kBK * 2;
-    static constexpr int kB = kGather ? 0 : kNB * kBK * 2;
+    // the scatter layer's weights (npad x cin, at most 4 K blocks) stay
+    // resident, loaded once; its ring stages carry the A tile only
+    static constexpr bool kWRes = kEpi == kEpiScatter;
+    static constexpr int kB = (kGather || kWRes) ? 0 : kNB * kBK * 2;
+    static constexpr int kWResBytes = kWRes ? kScatterMaxCinBlocks * kNpad * kBK * 2 : 0;
     static constexpr int kStage = kA + kB;
     static constexpr int kW = kGather ? kNpad * kGatherK * 2 : 0;
     static constexpr int kG = kNorm ? kNB * kNpad * 2 : 0;
@@ -146,12 +151,13 @@ struct Layout {
     static constexpr int kOnes = kFold ? kBM * kConstRow : 0;
     static constexpr int kBiasB = kFold ? kNB * kConstRow : 0;
     static constexpr int kBetaB = kFold && kNorm ? kNB * kConstRow : 0;
-    static constexpr int kFixedBytes = kOnes + kBiasB + kBetaB + kW + kG + kX2 +
+    static constexpr int kFixedBytes = kWResBytes + kOnes + kBiasB + kBetaB + kW + kG + kX2 +
                                        kS + (kGather ? 2 * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
     static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
     static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
-    static constexpr int offW = kStages * kStage;
+    static constexpr int offWRes = kStages * kStage;
+    static constexpr int offW = offWRes + kWResBytes;
     static constexpr int offG = offW + kW;
     static constexpr int offX2 = offG + kG;
     static constexpr int offS = offX2 + kX2;
@@ -189,6 +195,7 @@ struct Layout {
     static_assert(offPatch % 128 == 0 && kPatchBuf % 128 == 0, "patch buffer alignment");
     static_assert(offOnes % 128 == 0 && kOnes % 128 == 0 && kBiasB % 128 == 0, "constant tile alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
+    static_assert(kWResBytes % 1024 == 0 && (kNpad * kBK * 2) % 1024 == 0 || !kWRes, "resident weight alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
     static_assert(!kPair || (!kGather && kEpi != kEpiScatter && kNB % 8 == 0), "pair instances: TMA operands");
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
@@ -364,7 +371,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         // one-time operands from lane 0; the operand ring from the whole warp
         // (one elected lane issues each load); the first layer's input
         // windows from lane 0
-        constexpr uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0);
+        const uint32_t cbytes = (kNorm ? Lay::kG : 0) + (kGather ? Lay::kW : 0) +
+                                (Lay::kWRes ? (uint32_t)(p.cin_blocks * kNpad * kBK * 2) : 0u);
         if (lane == 0) {
             if (!kGather) {
                 tma_prefetch_desc(&tmA);
@@ -379,6 +387,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     tma_load_3d(smem + Lay::offG + Lay::kG / 2, &tmG, cbar, kBK, (int)rank * Lay::kNB, 0);
                 }
                 if (kGather) bulk_load(smem + Lay::offW, p.wgather, Lay::kW, cbar);
+                if (Lay::kWRes)
+                    for (int cb = 0; cb < p.cin_blocks; ++cb)
+                        tma_load_3d(smem + Lay::offWRes + cb * (kNpad * kBK * 2), &tmW, cbar, cb * kBK, 0, 0);
             }
         }
         __syncwarp();
@@ -417,7 +428,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         } else {
                             mbar_arrive_expect_tx_w(&full[s], Lay::kStage);
                             tma_load_4d_w(st, &tmA, &full[s], cb * kBK, ix, iy, b);
-                            tma_load_3d_w(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
+                            if (!Lay::kWRes) tma_load_3d_w(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
                         }
                         last_round[s] = (int)r;
                     }
@@ -467,7 +478,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         constexpr bool W = Lay::kWarpIssue;
         if (leader && (W || lane == 0)) {
             const uint32_t idesc = idesc_bf16(kPair ? 2 * kBM : kBM, kNpad);
-            bool consts = !kGather;
+            bool consts = !(kGather || Lay::kWRes);  // the first layer's / scatter layer's weights arrive once
             uint32_t it = 0;
             int j = 0;
             for (int tile = unit0; tile < p.tiles_total && !aborted<W>(abort); tile += unit_step, ++j) {
@@ -523,7 +534,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                             mma_issue_pair<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2),
                                               smem_desc(b0 + kk * 32, 16, 1024, 2), idesc, !(fresh && kk == 0));
                     } else {
-                        const uint32_t b0 = a0 + Lay::kA;
+                        // resident weights: K block ks (the scatter layer has one tap)
+                        const uint32_t b0 = Lay::kWRes ? smem_u32(smem + Lay::offWRes) + ks * (kNpad * kBK * 2)
+                                                       : a0 + Lay::kA;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 16; ++kk) {
                             const uint64_t bd = smem_desc(b0 + kk * 32, 16, 1024, 2);
@@ -1305,6 +1318,8 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         return fcai::fail(FCAI_ERR_INVALID,
                           "scatter layers are transposed convolutions with cout <= 10, npad = round16(25 * cout) "
                           "and an fp32 NCHW output");
+    if (scatter && L->cin > kScatterMaxCinBlocks * kBK)
+        return fcai::fail(FCAI_ERR_INVALID, "scatter layers take at most %d input channels", kScatterMaxCinBlocks * kBK);
     int epi;
     if (scatter) epi = kEpiScatter;
     else if (L->epilogue == FCAI_EPI_GDN) epi = kEpiGdn;

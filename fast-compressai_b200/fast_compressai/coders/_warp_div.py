@@ -144,7 +144,20 @@ def _check_latent(y: torch.Tensor, medians: torch.Tensor, cdfs, cdf_sizes, offse
     if not (isinstance(medians, torch.Tensor) and medians.dtype == torch.float32 and medians.is_contiguous()
             and medians.numel() == cdfs.shape[0] and medians.device == y.device):
         raise RuntimeError("medians must be a contiguous float32 [C] tensor on the latent's device")
-    _check_encode_inputs(torch.empty((1, 1), dtype=torch.int32, device=y.device), None, cdfs, cdf_sizes, offsets)
+    # the table checks of _check_encode_inputs, without a symbols tensor
+    tables = (cdfs, cdf_sizes, offsets)
+    if not all(isinstance(t, torch.Tensor) and t.is_cuda for t in tables):
+        raise RuntimeError("CUDA required")
+    if any(t.device != y.device for t in tables):
+        raise RuntimeError("all coder tensors must share a CUDA device")
+    if any(t.dtype != torch.int32 for t in tables):
+        raise RuntimeError("all coder inputs must be int32")
+    if not all(t.is_contiguous() for t in tables):
+        raise RuntimeError("all coder inputs must be contiguous")
+    if cdfs.dim() != 2 or cdf_sizes.dim() != 1 or offsets.dim() != 1:
+        raise RuntimeError("invalid coder input ranks/shapes")
+    if cdf_sizes.numel() != cdfs.shape[0] or offsets.numel() != cdfs.shape[0]:
+        raise RuntimeError("CDF metadata length mismatch")
 
 
 def encode_latent(y: torch.Tensor, medians: torch.Tensor, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,
