@@ -169,7 +169,11 @@ struct Layout {
     static constexpr int offBias = offBetaB + kBetaB;
     static constexpr int offBeta = offBias + kNpad * 4;
     static constexpr int offBar = (offBeta + kNpad * 4 + 7) & ~7;
-    static constexpr int kBars = 2 * kStages + 8 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
+    // TMEM accumulator buffers: 2, or 4 for the scatter layer (128 columns
+    // each), whose short tiles would otherwise make the MMA wait for the
+    // epilogue of the tile before last
+    static constexpr int kAccBufs = kEpi == kEpiScatter ? 4 : 2;
+    static constexpr int kBars = 2 * kStages + 2 * kAccBufs + 4 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
     static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
     static constexpr int kBytes = offSlot + 32;
@@ -271,8 +275,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
     constexpr int kStages = Lay::kStages;
     uint64_t *empty = bars + kStages;
     uint64_t *accf = bars + 2 * kStages;
-    uint64_t *acce = accf + 2;
-    uint64_t *g2bar = acce + 2;   // GDN GEMM done (one per epilogue group)
+    uint64_t *acce = accf + Lay::kAccBufs;
+    uint64_t *g2bar = acce + Lay::kAccBufs;   // GDN GEMM done (one per epilogue group)
     uint64_t *cbar = g2bar + 2;
     uint64_t *dbar = cbar + 1;  // abort path: drains this CTA's MMAs
     uint64_t *pfull = dbar + 1;   // first layer: patch buffer loaded (2)
@@ -299,7 +303,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             mbar_init(&full[s], kGather ? kGatherThreads : 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < Lay::kAccBufs; ++b) {
             mbar_init(&accf[b], 1);
             mbar_init(&acce[b], kPair ? 2 : Lay::kGroupThreads);  // pairs: one arrival per CTA's epilogue
         }
@@ -491,8 +495,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 }
                 int b, ph, gy0, gx0;
                 tile_coords(p, tile, b, ph, gy0, gx0);
-                const int buf = j & 1;
-                const uint32_t use = j >> 1;
+                const int buf = j % Lay::kAccBufs;
+                const uint32_t use = j / Lay::kAccBufs;
                 if (!wait_for<W>(&acce[buf], (use & 1) ^ 1, abort, kPair)) {
                     if (lane == 0) fail(p, abort, kErrMma);
                     break;
@@ -738,8 +742,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             int b, ph, gy0, gx0;
             tile_coords(p, tile, b, ph, gy0, gx0);
             gx0 += sub_x;
-            const int buf = j & 1;
-            const uint32_t use = j >> 1;
+            const int buf = j % Lay::kAccBufs;
+            const uint32_t use = j / Lay::kAccBufs;
             if (gleader) {
                 // the x^2 tile doubles as the previous tile's output staging
                 if (kNorm && p.tma_store) bulk_wait_read_all();
@@ -1381,7 +1385,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     uint32_t stride = 32;
     while (stride < (uint32_t)per_buf) stride <<= 1;
     p.buf_stride = stride;
-    p.tmem_cols = 2 * stride;
+    p.tmem_cols = (scatter ? 4 : 2) * stride;  // the kernel's accumulator buffer count
     if (p.tmem_cols > 512) return fcai::fail(FCAI_ERR_INVALID, "accumulators exceed tensor memory");
     if (scatter) {
         p.taps[0].n = 1;  // one K pass over the halo tile, all taps are GEMM columns
