@@ -52,11 +52,11 @@ def parse_args(argv=None):
     ap.add_argument("--transforms", choices=("bf16", "fp32"), default="bf16")
     ap.add_argument("--cpu-sample", type=int, default=1, help="images in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-inflight", type=int, default=1,
-                    help="also measure the end-to-end path with this many batches in flight (streams / host "
-                         "threads); reported as e2e.pipelined, the headline stays one batch at a time")
     ap.add_argument("--chunk-images", type=int, default=4,
-                    help="images per upload / download chunk of the end-to-end (host buffers) measurement")
+                    help="images per download chunk (and per upload chunk of the one-batch-at-a-time "
+                         "measurement) of the end-to-end (host buffers) measurement")
+    ap.add_argument("--upload-chunk-images", type=int, default=4,
+                    help="images per upload copy of the streamed end-to-end measurement")
     ap.add_argument("--ans-sweep", action="store_true",
                     help="BASELINE config 3 instead: the coder alone on 64 x 192 x 32 x 48 Laplacian symbols, "
                          "P in {1, 2, 4, 8, 16, 48, 192}")
@@ -405,68 +405,59 @@ def run_b200(args):
             if i >= args.warmup:
                 e2e_serial_ms.append(e0.elapsed_time(e1))
 
-        # (b) the same steps with `inflight` batches in flight, each on its own
-        # stream and host thread: one batch's upload overlaps another's download
-        # (PCIe is full duplex) and both overlap the GPU work.  Timed by events on
-        # the main stream around all steps; the per-step device working set
-        # (> 600 MB of activations) exceeds the L2, so no flush is added.
-        import threading
+        # (b) streamed, the headline: one host thread; each step's batch goes up
+        # on the upload stream (upload_host) while the previous step is still
+        # being synthesised and downloaded, the payload goes through host
+        # memory, and the reconstruction comes down on the download stream
+        # (decompress_host, ordered=False), overlapping the next step.  Every
+        # step's upload and download lie inside the timed region, which runs
+        # from an event recorded before the first upload to one recorded after
+        # the last download's event.  No L2 flush: each step's device working
+        # set (> 600 MB of activations) exceeds the 126 MB L2.
+        hosts = [x_host, x_host.clone().pin_memory()]
+        outs = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+        pbuf = torch.empty(packed_bytes * 2 + (1 << 20), dtype=torch.uint8).pin_memory()
 
-        inflight = max(1, args.e2e_inflight)
-        streams = [torch.cuda.Stream(device=dev) for _ in range(inflight)]
-        wbufs = [new_bufs() for _ in range(inflight)]
-        errors = []
-
-        def run_pipelined(nsteps):
+        def run_streamed(nsteps):
             main = torch.cuda.current_stream()
+            torch.cuda.synchronize()
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record(main)
-            for st in streams:
-                st.wait_stream(main)
-
-            def worker(w):
-                try:
-                    with torch.inference_mode(), torch.cuda.device(dev), torch.cuda.stream(streams[w]):
-                        for _ in range(w, nsteps, inflight):
-                            e2e_step(wbufs[w])
-                except Exception as exc:  # reported after the join
-                    errors.append(exc)
-
-            threads = [threading.Thread(target=worker, args=(w,)) for w in range(inflight)]
-            for th in threads:
-                th.start()
-            for th in threads:
-                th.join()
-            if errors:
-                raise errors[0]
-            for st in streams:
-                main.wait_stream(st)
+            nxt = fast.upload_host(hosts[0], chunk_images=args.upload_chunk_images)
+            readies = []
+            for i in range(nsteps):
+                cur = nxt
+                if i + 1 < nsteps:
+                    nxt = fast.upload_host(hosts[(i + 1) % 2], chunk_images=args.upload_chunk_images)
+                out = fast.compress(cur)
+                p = out["strings"][0]
+                host_payload = p.packed_to_host(pbuf)
+                main.synchronize()  # the payload has left the device (the main stream only)
+                q = WarpDivPayload.from_host_packed(host_payload, batch=p.batch, symbols_per_batch=p.symbols_per_batch,
+                                                    cdf_count=p.cdf_count, p_ch=p.p_ch, chunk_len=p.chunk_len,
+                                                    header_bytes=p.header_bytes,
+                                                    coding_fingerprint=p.coding_fingerprint, device=dev,
+                                                    non_blocking=True)
+                r = fast.decompress_host([q], out["shape"], outs[i % 2], chunk_images=args.chunk_images,
+                                         ordered=False)
+                readies.append(r["ready"])
+            for ev in readies:
+                main.wait_event(ev)
             t1.record(main)
             t1.synchronize()
             return t0.elapsed_time(t1)
 
-        pipelined_ms = 0.0
-        if inflight > 1:
-            # the workers' Python work is short; hand the interpreter lock over
-            # promptly so that one thread's launches do not wait out another's
-            # time slice (restored afterwards)
-            switch = sys.getswitchinterval()
-            sys.setswitchinterval(1e-4)
-            try:
-                run_pipelined(max(args.warmup, inflight))
-                pipelined_ms = run_pipelined(args.steps)
-            finally:
-                sys.setswitchinterval(switch)
-        t = torch.tensor([sum(e2e_serial_ms), pipelined_ms], dtype=torch.float64, device=dev)
+        run_streamed(max(args.warmup, 2))
+        streamed_ms = run_streamed(args.steps)
+        t = torch.tensor([sum(e2e_serial_ms), streamed_ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_step_ms = float(t[0]) / len(e2e_serial_ms)
+        serial_step_ms = float(t[0]) / len(e2e_serial_ms)
+        e2e_step_ms = float(t[1]) / args.steps
         e2e_value = world * in_bytes / (e2e_step_ms / 1e3) / 1e9
-        pipelined = None
-        if inflight > 1:
-            pipe_step_ms = float(t[1]) / args.steps
-            pipelined = {"value": world * in_bytes / (pipe_step_ms / 1e3) / 1e9, "ms_per_step": pipe_step_ms,
-                         "batches_in_flight": inflight, "note": "one stream and host thread per batch in flight"}
+        e2e_serial = {"value": world * in_bytes / (serial_step_ms / 1e3) / 1e9, "ms_per_step": serial_step_ms,
+                      "api": "FastModel.compress_host / decompress_host, one batch at a time (the upload "
+                             "overlaps g_a, the download g_s, chunk by chunk), L2 flushed before each step"}
 
         # ---- coder kernels alone on this batch's latent (ANS roofline) ------
         fc = fast._coder
@@ -566,9 +557,12 @@ def run_b200(args):
             "cpu_baseline": None,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_step_ms, "chunk_images": args.chunk_images,
-                    "api": "FastModel.compress_host / decompress_host (PCIe copies overlapped with the transforms "
-                           "chunk by chunk), payload through host memory; one batch at a time, L2 flushed before "
-                           "each step", "pipelined": pipelined},
+                    "upload_chunk_images": args.upload_chunk_images,
+                    "api": "FastModel.upload_host -> compress -> payload to pinned host memory and back "
+                           "(WarpDivPayload.from_host_packed) -> decompress_host(ordered=False), one host thread; "
+                           "step i+1's upload and step i's download run on their own copy streams during the "
+                           "neighbouring steps' GPU work",
+                    "serial": e2e_serial},
             "gpu_launches": launches,
             "clocks": clock_info,
             "compress_gbs": world * in_bytes / (comp_total / args.steps / 1e3) / 1e9,

@@ -31,9 +31,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/fcai_warp_div.h"
 #include "fcai_common.h"
@@ -1094,6 +1096,85 @@ __global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
 static std::mutex g_init_mutex;
 static bool g_magic_ready[64];
 
+// ---- status read-back without the copy engines -----------------------------
+// The encode's size / status words and the decode's check flags come back
+// through a 64-byte pinned host buffer mapped into the device's address space
+// (one per device and stream): a one-warp kernel stores them there, and the
+// host waits for the stream only.  A cudaMemcpy of those few bytes would be
+// queued on a copy engine behind whatever bulk transfers other streams have
+// issued (a batch's upload or download), and the host would wait for those.
+struct MappedStatus {
+    volatile long long *host;
+    long long *dev;
+};
+static std::mutex g_status_mutex;
+static std::unordered_map<uint64_t, MappedStatus> g_status;
+
+__global__ void status_to_host_kernel(const long long *__restrict__ src, long long *dst, int n) {
+    if ((int)threadIdx.x < n) dst[threadIdx.x] = src[threadIdx.x];
+}
+
+static int mapped_status(cudaStream_t stream, MappedStatus *out) {
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    const uint64_t key = ((uint64_t)(uint32_t)dev << 48) ^ reinterpret_cast<uint64_t>(stream);
+    std::lock_guard<std::mutex> lock(g_status_mutex);
+    auto it = g_status.find(key);
+    if (it != g_status.end()) {
+        *out = it->second;
+        return FCAI_OK;
+    }
+    void *h = nullptr;
+    void *d = nullptr;
+    FCAI_CUDA_TRY(cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess || !d) {
+        cudaFreeHost(h);
+        return fcai::fail(FCAI_ERR_CUDA, "mapped status buffer has no device address");
+    }
+    MappedStatus m{static_cast<volatile long long *>(h), static_cast<long long *>(d)};
+    g_status.emplace(key, m);
+    *out = m;
+    return FCAI_OK;
+}
+
+// Reads n (<= 8) status words of the control block after the stream's
+// queued work.
+static int read_status(const long long *src, int n, cudaStream_t stream, long long *out) {
+    MappedStatus m{};
+    if (int rc = mapped_status(stream, &m)) return rc;
+    status_to_host_kernel<<<1, 32, 0, stream>>>(src, m.dev, n);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    for (int i = 0; i < n; ++i) out[i] = m.host[i];
+    return FCAI_OK;
+}
+
+// ---- payload transfers without the copy engines -----------------------------
+// Copies between device memory and pinned host memory that is mapped into the
+// device's address space, done by SM loads and stores over PCIe, for the same
+// reason: a small payload must not wait behind a batch's bulk copies.
+__global__ void copy16_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst, int64_t n16) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+__global__ void copy1_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
+// The device address of p: device memory as is, host memory only if it is
+// pinned and mapped (nullptr otherwise, and for memory of another device).
+static void *device_address(const void *p, int dev) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return a.device == dev ? a.devicePointer : nullptr;
+    if (a.type == cudaMemoryTypeHost) return a.devicePointer;
+    return nullptr;
+}
+
 static int ensure_magic(cudaStream_t stream) {
     int dev = 0;
     FCAI_CUDA_TRY(cudaGetDevice(&dev));
@@ -1365,8 +1446,7 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     }
     if (rc) return rc;
     long long status[8];
-    FCAI_CUDA_TRY(cudaMemcpyAsync(status, p.ctrl->status, sizeof(status), cudaMemcpyDeviceToHost, stream));
-    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    if ((rc = read_status(p.ctrl->status, 8, stream, status))) return rc;
 
     const long long flags = status[kStFlags];
     info->header_bytes = d.header_bytes;
@@ -1457,8 +1537,7 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     if (rc) return rc;
     if (!check) return FCAI_OK;
     long long flags = 0;
-    FCAI_CUDA_TRY(cudaMemcpyAsync(&flags, &ctrl->status[kStFlags], sizeof(flags), cudaMemcpyDeviceToHost, stream));
-    FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    if ((rc = read_status(&ctrl->status[kStFlags], 1, stream, &flags))) return rc;
     if (index_layout_is_channel) *index_layout_is_channel = (flags & kFlagNonChannel) ? 0 : 1;
     return flags_to_status(flags, false);
 }
@@ -1597,6 +1676,36 @@ int fcai_warp_div_decode_latent(const uint8_t *packed, int64_t packed_bytes, con
     return decode_impl(kModeLatent, packed, packed_bytes, max_rounds, K, header_bytes, chunk_len, nullptr, B, N, cdfs,
                        C, L, cdf_sizes, offsets, medians, nullptr, y_hat_out, workspace, workspace_bytes, check,
                        nullptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fcai_payload_copy_async(void *dst, const void *src, int64_t bytes, fcai_stream_t stream_) {
+    fcai::clear_error();
+    if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fcai::fail(FCAI_ERR_INVALID, "invalid copy arguments");
+    if (bytes == 0) return FCAI_OK;
+    int dev = 0;
+    FCAI_CUDA_TRY(cudaGetDevice(&dev));
+    uint8_t *d = static_cast<uint8_t *>(device_address(dst, dev));
+    const uint8_t *s = static_cast<const uint8_t *>(device_address(src, dev));
+    if (!d || !s)
+        return fcai::fail(FCAI_ERR_INVALID,
+                          "copy operands must be memory of the current device or pinned host memory mapped into it");
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    const int threads = 256;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(d) | reinterpret_cast<uintptr_t>(s)) & 15) == 0;
+    const int64_t n16 = aligned ? bytes / 16 : 0;
+    if (n16 > 0) {
+        const int64_t blocks = std::min<int64_t>((n16 + threads - 1) / threads, 148 * 8);
+        copy16_kernel<<<(unsigned)blocks, threads, 0, stream>>>(reinterpret_cast<const uint4 *>(s),
+                                                                reinterpret_cast<uint4 *>(d), n16);
+        FCAI_CUDA_TRY(cudaGetLastError());
+    }
+    const int64_t rest = bytes - n16 * 16;
+    if (rest > 0) {
+        const int64_t blocks = std::min<int64_t>((rest + threads - 1) / threads, 148 * 8);
+        copy1_kernel<<<(unsigned)blocks, threads, 0, stream>>>(s + n16 * 16, d + n16 * 16, rest);
+        FCAI_CUDA_TRY(cudaGetLastError());
+    }
+    return FCAI_OK;
 }
 
 }  // extern "C"

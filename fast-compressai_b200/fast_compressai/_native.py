@@ -74,6 +74,7 @@ _I64 = ctypes.c_int64
 SIGNATURES: dict[str, tuple] = {
     "fcai_last_error": (ctypes.c_char_p, []),
     "fcai_version": (ctypes.c_char_p, []),
+    "fcai_payload_copy_async": (ctypes.c_int, [_P, _P, _I64, _P]),
     "fcai_warp_div_plan_create": (ctypes.c_int, [_I32, _I32, _I32, _I32, ctypes.POINTER(WarpDivPlan)]),
     "fcai_warp_div_encode": (
         ctypes.c_int,

@@ -227,6 +227,10 @@ class FastModel(nn.Module):
             return coder.decompress(*args, **kwargs)
         return self.model.decompress(*args, **kwargs)
 
+    def upload_host(self, x, **kwargs: Any) -> Any:
+        """Start the upload of a host batch and return a handle for compress() (warp_div coder only)."""
+        return self._host_coder("upload_host").upload_host(x, **kwargs)
+
     def compress_host(self, x, **kwargs: Any) -> Any:
         """compress() of a host batch, its upload overlapped with g_a (warp_div coder only)."""
         return self._host_coder("compress_host").compress_host(x, **kwargs)

@@ -16,24 +16,38 @@ index from the position, which is that tensor's definition.
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 from .errors import CoderInputError
 from .warp_div import WarpDivBackend, WarpDivPayload
 
-# One copy stream per compute stream for the host-batch entry points, so that
-# callers on different streams (several batches in flight) do not serialise
-# their uploads and downloads on one copy queue.
-_COPY_STREAMS: dict[tuple[int, int], torch.cuda.Stream] = {}
+# Copy streams of the host-batch entry points, one per (compute stream,
+# direction): uploads and downloads never queue behind each other (PCIe is
+# full duplex), and callers on different compute streams do not serialise
+# their copies on one queue.
+_COPY_STREAMS: dict[tuple[int, int, str], torch.cuda.Stream] = {}
 
 
-def _copy_stream(device: torch.device, compute: torch.cuda.Stream) -> torch.cuda.Stream:
+def _copy_stream(device: torch.device, compute: torch.cuda.Stream, direction: str) -> torch.cuda.Stream:
     index = device.index if device.index is not None else torch.cuda.current_device()
-    key = (index, compute.cuda_stream)
+    key = (index, compute.cuda_stream, direction)
     stream = _COPY_STREAMS.get(key)
     if stream is None:
         stream = _COPY_STREAMS.setdefault(key, torch.cuda.Stream(device=index))
     return stream
+
+
+@dataclass(frozen=True)
+class HostUpload:
+    """A host batch being copied to the device (``upload_host``).
+
+    ``tensor`` holds the batch once ``ready`` (recorded on the upload stream)
+    has completed; ``compress`` orders its work after that event."""
+
+    tensor: torch.Tensor
+    ready: torch.cuda.Event
 
 
 def _chunks(batch: int, chunk_images: int):
@@ -74,7 +88,13 @@ class FactorizedWarpDivCodec:
             self._median_cache = hit
         return hit[1]
 
-    def compress(self, x: torch.Tensor, timing: dict[str, float] | None = None):
+    def compress(self, x: torch.Tensor | HostUpload, timing: dict[str, float] | None = None):
+        if isinstance(x, HostUpload):
+            # the compute stream waits for the upload alone, not for other copies
+            compute = torch.cuda.current_stream(x.tensor.device)
+            compute.wait_event(x.ready)
+            x.tensor.record_stream(compute)
+            x = x.tensor
         if not isinstance(x, torch.Tensor) or x.device.type != "cuda" or x.ndim != 4:
             raise CoderInputError("warp_div FactorizedPrior.compress expects a CUDA NCHW tensor")
         with torch.no_grad():
@@ -104,6 +124,36 @@ class FactorizedWarpDivCodec:
     def _device(self) -> torch.device:
         return self.model.entropy_bottleneck._quantized_cdf.device
 
+    def upload_host(self, x: torch.Tensor, *, chunk_images: int = 4) -> HostUpload:
+        """Start copying a host batch to the device and return at once.
+
+        The copy runs on this compute stream's upload stream, in the order of
+        earlier uploads only, so it overlaps the current stream's work and
+        any downloads; ``compress(upload)`` then waits for it.  It is issued
+        as one copy per ``chunk_images`` images, so that small copies of other
+        streams (a payload going up) are not queued behind the whole batch.
+        With ``x`` in pinned memory the call does not wait for the copy.
+        ``x`` must stay unchanged until the upload's ``ready`` event has
+        completed.
+        """
+        if not isinstance(x, torch.Tensor) or x.device.type != "cpu" or x.ndim != 4:
+            raise CoderInputError("upload_host expects a host (CPU) NCHW tensor")
+        dev = self._device()
+        with torch.no_grad(), torch.cuda.device(dev):
+            compute = torch.cuda.current_stream(dev)
+            up = _copy_stream(dev, compute, "up")
+            x = x.float().contiguous()
+            with torch.cuda.stream(up):
+                # allocated on the upload stream: its memory is reused only
+                # after earlier work of that stream, and never waits for the
+                # compute stream
+                x_dev = torch.empty(x.shape, dtype=torch.float32, device=dev)
+                for i0, i1 in _chunks(x.shape[0], chunk_images):
+                    x_dev[i0:i1].copy_(x[i0:i1], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(up)
+            return HostUpload(x_dev, ready)
+
     def compress_host(self, x: torch.Tensor, *, chunk_images: int = 4):
         """``compress`` of a batch held in host memory.
 
@@ -119,7 +169,7 @@ class FactorizedWarpDivCodec:
         dev = self._device()
         with torch.no_grad(), torch.cuda.device(dev):
             compute = torch.cuda.current_stream(dev)
-            copy = _copy_stream(dev, compute)
+            copy = _copy_stream(dev, compute, "up")
             x = x.float().contiguous()
             x_dev = torch.empty(x.shape, dtype=torch.float32, device=dev)
             copy.wait_stream(compute)  # x_dev's memory is free for the copies
@@ -141,21 +191,25 @@ class FactorizedWarpDivCodec:
                                                   offsets, self.p_ch)
             return {"strings": [payload], "shape": tuple(y.shape[-2:])}
 
-    def decompress_host(self, strings, shape, out: torch.Tensor | None = None, *, chunk_images: int = 4):
+    def decompress_host(self, strings, shape, out: torch.Tensor | None = None, *, chunk_images: int = 4,
+                        ordered: bool = True):
         """``decompress`` into host memory.
 
         The latent is decoded at once; g_s then runs in chunks of
         ``chunk_images`` images and each chunk's reconstruction is copied to
         ``out`` (a pinned host tensor [B, 3, H, W], allocated if None) on a
-        copy stream while the next chunk is synthesised.  The copies are
-        ordered before later work on the current stream: synchronise it (or
-        the device) before reading ``out``.
+        copy stream while the next chunk is synthesised.  With ``ordered``
+        the copies are ordered before later work on the current stream:
+        synchronise it (or the device) before reading ``out``.  Without it
+        the current stream goes on at once (the next batch's work overlaps
+        these copies) and the result's ``"ready"`` event, recorded on the
+        download stream, completes when ``out`` holds the reconstruction.
         """
         y_hat = self._decode_latent(strings, shape)
         dev = y_hat.device
         with torch.no_grad(), torch.cuda.device(dev):
             compute = torch.cuda.current_stream(dev)
-            copy = _copy_stream(dev, compute)
+            copy = _copy_stream(dev, compute, "down")
             g_s = self.model.g_s
             fused = getattr(g_s, "fuses_clamp", False)
             for i0, i1 in _chunks(y_hat.shape[0], chunk_images):
@@ -170,8 +224,12 @@ class FactorizedWarpDivCodec:
                     copy.wait_event(done)
                     out[i0:i1].copy_(part, non_blocking=True)
                 part.record_stream(copy)
-            compute.wait_stream(copy)
-            return {"x_hat": out}
+            if ordered:
+                compute.wait_stream(copy)
+                return {"x_hat": out}
+            ready = torch.cuda.Event()
+            ready.record(copy)
+            return {"x_hat": out, "ready": ready}
 
     def _decode_latent(self, strings, shape) -> torch.Tensor:
         if (not isinstance(strings, (list, tuple)) or len(strings) != 1

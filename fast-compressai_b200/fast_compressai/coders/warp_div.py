@@ -19,6 +19,7 @@ Host overhead differs from the reference, not the results:
 
 from __future__ import annotations
 
+import ctypes
 import hashlib
 import importlib
 import threading
@@ -151,6 +152,23 @@ class WarpDivPayload:
     #   payload (whose header already holds max_rounds).  Little-endian.
     _MAGIC = b"FCWD"
 
+    def packed_to_host(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Copy ``packed`` to host memory on the current stream and return the
+        host tensor (``out[:n]`` when ``out``, a pinned uint8 buffer of at
+        least ``packed.numel()`` bytes, is given).  The copy is enqueued, not
+        waited for: synchronise the stream before reading.  Into pinned
+        mapped memory it is done by a kernel, so it does not wait behind bulk
+        copies that other streams have queued on the copy engines."""
+        n = self.packed.numel()
+        if out is None:
+            out = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        elif out.device.type != "cpu" or out.dtype != torch.uint8 or not out.is_contiguous() or out.numel() < n:
+            raise CoderInputError("out must be a contiguous host uint8 tensor of at least packed.numel() bytes")
+        dst = out[:n]
+        if not (dst.is_pinned() and _kernel_copy(dst, self.packed)):
+            dst.copy_(self.packed, non_blocking=True)
+        return dst
+
     def to_bytes(self) -> bytes:
         """Serialise (one device-to-host copy of ``packed``)."""
         return self.container_header() + self.packed.cpu().numpy().tobytes()
@@ -186,9 +204,16 @@ class WarpDivPayload:
     @classmethod
     def from_host_packed(cls, packed_host: torch.Tensor, *, batch: int, symbols_per_batch: int, cdf_count: int,
                          p_ch: int, chunk_len: int, header_bytes: int, coding_fingerprint: str | None,
-                         device="cuda", format_version: int = FORMAT_VERSION) -> "WarpDivPayload":
+                         device="cuda", format_version: int = FORMAT_VERSION,
+                         non_blocking: bool = False) -> "WarpDivPayload":
         """Build a payload from a host copy of ``packed``; ``max_rounds`` is
-        read from the packed header on the host, so no device sync happens."""
+        read from the packed header on the host, so no device sync happens.
+        With ``non_blocking`` the upload is only enqueued on the current
+        stream (later work there, such as the decode, runs after it), done by
+        a kernel reading pinned mapped ``packed_host`` directly so that it
+        does not wait behind bulk copies of other streams; ``max_rounds`` is
+        then a view of the uploaded header.  ``packed_host`` must stay
+        unchanged until that stream has passed the copy."""
         if packed_host.device.type != "cpu" or packed_host.dtype != torch.uint8:
             raise CoderInputError("packed_host must be a CPU uint8 tensor")
         K = (cdf_count + p_ch - 1) // p_ch if p_ch > 0 else 0
@@ -199,8 +224,14 @@ class WarpDivPayload:
         if bool((rounds < 0).any()):
             raise CoderInputError("warp_div packed header round counts are invalid")
         dev = torch.device(device)
-        max_rounds = rounds.to(torch.uint32).to(dev, non_blocking=False)
-        packed = packed_host.to(dev)
+        if non_blocking:
+            # the round table is the header's: a view of the device copy, so
+            # the only transfer is the payload's
+            packed = _to_device(packed_host, dev)
+            max_rounds = packed[32:32 + 4 * n].view(torch.uint32).reshape(batch, K)
+        else:
+            max_rounds = rounds.to(torch.uint32).to(dev, non_blocking=False)
+            packed = packed_host.to(dev)
         total = int(rounds.to(torch.int64).sum())
         _remember_rounds(max_rounds, total, all_ok=bool((rounds >= 2).all()))
         payload = cls(packed=packed, max_rounds=max_rounds, header_bytes=header_bytes, chunk_len=chunk_len,
@@ -214,6 +245,31 @@ class WarpDivPayload:
                 and packed_host.numel() == header_bytes + 128 * total):
             _mark_consistent(payload)
         return payload
+
+
+def _kernel_copy(dst: torch.Tensor, src: torch.Tensor) -> bool:
+    """fcai_payload_copy_async of src into dst (same byte size, contiguous) on
+    the current stream of the device operand; False, with nothing enqueued,
+    if the host operand is not pinned memory mapped into the device."""
+    cuda = dst if dst.is_cuda else src
+    with torch.cuda.device(cuda.device):
+        stream = torch.cuda.current_stream(cuda.device).cuda_stream
+        rc = _native.lib().fcai_payload_copy_async(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                                                   dst.numel() * dst.element_size(), ctypes.c_void_p(stream))
+    if rc == _native.FCAI_ERR_INVALID:
+        return False
+    _native.check(rc)
+    _native.count_launches(1 if (dst.data_ptr() | src.data_ptr()) % 16 == 0 and dst.numel() % 16 == 0 else 2)
+    return True
+
+
+def _to_device(host: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    """Asynchronous upload of a contiguous host uint8 tensor on the current stream."""
+    host = host.contiguous()
+    out = torch.empty(host.shape, dtype=host.dtype, device=dev)
+    if not (host.is_pinned() and _kernel_copy(out, host)):
+        out.copy_(host, non_blocking=True)
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -180,6 +180,17 @@ int fcai_warp_div_decode_latent(const uint8_t *packed, int64_t packed_bytes, con
                                 const float *medians, float *y_hat_out, void *workspace, int64_t workspace_bytes,
                                 int32_t check, fcai_stream_t stream);
 
+/* Copy `bytes` from src to dst on `stream` with SM loads and stores, where
+ * each operand is memory of the current device or pinned host memory mapped
+ * into its address space (cudaHostAlloc memory on a system with unified
+ * addressing).  For moving a payload between host and device while a batch's
+ * bulk copies occupy the copy engines: this copy does not queue behind them.
+ * FCAI_ERR_INVALID if an operand is neither (nothing is launched then).
+ * Asynchronous; the host memory must stay allocated until the stream passes
+ * the copy.  No counterpart in the reference (its payload stays a device
+ * tensor). */
+int fcai_payload_copy_async(void *dst, const void *src, int64_t bytes, fcai_stream_t stream);
+
 /* Message of the last error on the calling thread ("" if none). */
 const char *fcai_last_error(void);
 

@@ -227,6 +227,38 @@ def test_host_batch_entry_points_match_device_ones(cuda_device, transforms):
         fast.compress_host(x.to(cuda_device))
 
 
+def test_streamed_host_batches_match_device_ones(cuda_device):
+    # upload_host starts a batch's upload on the upload stream, compress waits
+    # for that upload alone, and decompress_host(ordered=False) leaves the
+    # download on the download stream with a "ready" event: with three
+    # batches in flight, every payload and reconstruction equals the device
+    # path's bit for bit
+    torch.manual_seed(0)
+    model = FactorizedPrior(128, 192).to(cuda_device).eval()
+    model.update(force=True)
+    fast = accelerate(model, P=4, device="cuda:0", transforms="bf16")
+    xs = [_smooth_images(3, 64, 96, "cpu", seed=s).pin_memory() for s in (11, 12, 13)]
+    outs = [torch.empty(x.shape, dtype=torch.float32).pin_memory() for x in xs]
+    with torch.inference_mode():
+        refs = [fast.compress(x.to(cuda_device)) for x in xs]
+        x_refs = [fast.decompress(r["strings"], r["shape"])["x_hat"].cpu() for r in refs]
+        torch.cuda.synchronize()
+        ups = [fast.upload_host(x) for x in xs]
+        readies = []
+        for up, ref, out in zip(ups, refs, outs):
+            got = fast.compress(up)
+            assert got["shape"] == ref["shape"]
+            assert torch.equal(got["strings"][0].packed, ref["strings"][0].packed)
+            res = fast.decompress_host(got["strings"], got["shape"], out, chunk_images=2, ordered=False)
+            assert res["x_hat"] is out
+            readies.append(res["ready"])
+        for ev, out, x_ref in zip(readies, outs, x_refs):
+            ev.synchronize()
+            assert torch.equal(out, x_ref)
+    with pytest.raises(CoderInputError):
+        fast.upload_host(xs[0].to(cuda_device))
+
+
 @pytest.mark.parametrize("kind", ["conv_gdn", "deconv_igdn", "conv_latent"])
 def test_pair_tiles_match_single_tiles_bitwise(cuda_device, kind):
     # FCAI_ALGO_IMPLICIT_GEMM_PAIR accumulates the same products in the same

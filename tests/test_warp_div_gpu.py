@@ -223,3 +223,51 @@ def test_corrupt_body_is_reported_not_read_out_of_bounds(cuda_device):
         else:
             assert out.shape == sym.shape
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("nbytes,offset", [(1, 0), (15, 3), (4096, 0), (100003, 5), (3 << 20, 0)])
+def test_payload_copy_kernel_round_trip(cuda_device, nbytes, offset):
+    # fcai_payload_copy_async moves bytes between device memory and pinned
+    # mapped host memory with SM loads / stores (16-byte path plus a byte
+    # tail, unaligned starts included), in both directions
+    from fast_compressai.coders.warp_div import _kernel_copy
+
+    rng = np.random.default_rng(nbytes)
+    data = torch.from_numpy(rng.integers(0, 256, size=nbytes + offset, dtype=np.uint8))
+    host_src = data.pin_memory()[offset:]
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
+    assert _kernel_copy(dev, host_src)
+    host_dst = torch.zeros(nbytes + offset, dtype=torch.uint8).pin_memory()[offset:]
+    assert _kernel_copy(host_dst, dev)
+    torch.cuda.synchronize()
+    assert torch.equal(dev.cpu(), data[offset:])
+    assert torch.equal(host_dst, data[offset:])
+    # pageable host memory is not mapped: refused, nothing launched
+    assert not _kernel_copy(dev, data[offset:].clone())
+
+
+def test_payload_through_host_memory_without_copy_engines(cuda_device):
+    # packed_to_host and from_host_packed(non_blocking=True) carry a payload
+    # down and back up with the payload kernel; max_rounds is then a view of
+    # the uploaded header, the result decodes like the original, and it is
+    # marked consistent (asynchronous decode)
+    from fast_compressai.coders.warp_div import _is_consistent
+
+    sym, idx, cdfs, sizes, offs = _backend_case(cuda_device)
+    be = WarpDivBackend()
+    payload = be.encode(sym, idx, cdfs, sizes, offs, p_ch=2)
+    buf = torch.empty(payload.packed.numel() + 64, dtype=torch.uint8).pin_memory()
+    host = payload.packed_to_host(buf)
+    torch.cuda.synchronize()
+    assert host.data_ptr() == buf.data_ptr() and torch.equal(host, payload.packed.cpu())
+    q = WarpDivPayload.from_host_packed(host, batch=payload.batch, symbols_per_batch=payload.symbols_per_batch,
+                                        cdf_count=payload.cdf_count, p_ch=payload.p_ch, chunk_len=payload.chunk_len,
+                                        header_bytes=payload.header_bytes,
+                                        coding_fingerprint=payload.coding_fingerprint, device=cuda_device,
+                                        non_blocking=True)
+    assert torch.equal(q.packed, payload.packed)
+    assert q.max_rounds.dtype == torch.uint32 and torch.equal(q.max_rounds.cpu(), payload.max_rounds.cpu())
+    assert _is_consistent(q)
+    assert torch.equal(be.decode(q, idx, cdfs, sizes, offs), sym)
+    with pytest.raises(CoderInputError):
+        payload.packed_to_host(torch.empty(4, dtype=torch.uint8))
