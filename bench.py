@@ -53,10 +53,10 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-sample", type=int, default=1, help="images in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk-images", type=int, default=4,
-                    help="images per download chunk (and per upload chunk of the one-batch-at-a-time "
-                         "measurement) of the end-to-end (host buffers) measurement")
-    ap.add_argument("--upload-chunk-images", type=int, default=4,
-                    help="images per upload copy of the streamed end-to-end measurement")
+                    help="images per upload / download chunk of the one-batch-at-a-time end-to-end measurement")
+    ap.add_argument("--stream-chunk-images", type=int, default=0,
+                    help="images per upload / download chunk of the streamed end-to-end measurement "
+                         "(0: the whole batch; its copies overlap the neighbouring batches anyway)")
     ap.add_argument("--ans-sweep", action="store_true",
                     help="BASELINE config 3 instead: the coder alone on 64 x 192 x 32 x 48 Laplacian symbols, "
                          "P in {1, 2, 4, 8, 16, 48, 192}")
@@ -414,6 +414,7 @@ def run_b200(args):
         # from an event recorded before the first upload to one recorded after
         # the last download's event.  No L2 flush: each step's device working
         # set (> 600 MB of activations) exceeds the 126 MB L2.
+        stream_chunk = args.stream_chunk_images if args.stream_chunk_images > 0 else args.batch
         hosts = [x_host, x_host.clone().pin_memory()]
         outs = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
         pbuf = torch.empty(packed_bytes * 2 + (1 << 20), dtype=torch.uint8).pin_memory()
@@ -423,12 +424,12 @@ def run_b200(args):
             torch.cuda.synchronize()
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record(main)
-            nxt = fast.upload_host(hosts[0], chunk_images=args.upload_chunk_images)
+            nxt = fast.upload_host(hosts[0], chunk_images=stream_chunk)
             readies = []
             for i in range(nsteps):
                 cur = nxt
                 if i + 1 < nsteps:
-                    nxt = fast.upload_host(hosts[(i + 1) % 2], chunk_images=args.upload_chunk_images)
+                    nxt = fast.upload_host(hosts[(i + 1) % 2], chunk_images=stream_chunk)
                 out = fast.compress(cur)
                 p = out["strings"][0]
                 host_payload = p.packed_to_host(pbuf)
@@ -438,8 +439,7 @@ def run_b200(args):
                                                     header_bytes=p.header_bytes,
                                                     coding_fingerprint=p.coding_fingerprint, device=dev,
                                                     non_blocking=True)
-                r = fast.decompress_host([q], out["shape"], outs[i % 2], chunk_images=args.chunk_images,
-                                         ordered=False)
+                r = fast.decompress_host([q], out["shape"], outs[i % 2], chunk_images=stream_chunk, ordered=False)
                 readies.append(r["ready"])
             for ev in readies:
                 main.wait_event(ev)
@@ -456,6 +456,7 @@ def run_b200(args):
         e2e_step_ms = float(t[1]) / args.steps
         e2e_value = world * in_bytes / (e2e_step_ms / 1e3) / 1e9
         e2e_serial = {"value": world * in_bytes / (serial_step_ms / 1e3) / 1e9, "ms_per_step": serial_step_ms,
+                      "chunk_images": args.chunk_images,
                       "api": "FastModel.compress_host / decompress_host, one batch at a time (the upload "
                              "overlaps g_a, the download g_s, chunk by chunk), L2 flushed before each step"}
 
@@ -556,8 +557,7 @@ def run_b200(args):
             },
             "cpu_baseline": None,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_step_ms, "chunk_images": args.chunk_images,
-                    "upload_chunk_images": args.upload_chunk_images,
+                    "ms_per_step": e2e_step_ms, "chunk_images": stream_chunk,
                     "api": "FastModel.upload_host -> compress -> payload to pinned host memory and back "
                            "(WarpDivPayload.from_host_packed) -> decompress_host(ordered=False), one host thread; "
                            "step i+1's upload and step i's download run on their own copy streams during the "
