@@ -39,10 +39,12 @@
 // stop, drains its MMAs and frees its TMEM before returning.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/fcai_transforms.h"
@@ -100,6 +102,8 @@ struct ConvParams {
     int patch_tma;       // first layer: 1 = input windows by TMA (tmA maps x_in), 0 = direct loads
     int patch_w, patch_h;  // patch box: columns (2 TX + 8), rows (2 TY + 3)
     uint32_t patch_bytes;
+    const float *act_scale;  // FP8 layers: device scale of the e4m3 input (amax / 448)
+    float w_scale;           // FP8 layers: scale of the e4m3 weights
     int tma_store;       // GDN layers: the output tile leaves through TMA stores (tmO); 1 = 4-D
                          // NHWC box, 2 = transposed conv phase box (5-D view of the output)
     void *out;
@@ -110,9 +114,13 @@ struct ConvParams {
 // each CTA holds its 128 pixel rows of A and half of the N rows of B (and of
 // gamma), so a CTA's operand ring carries a quarter less per MMA and fits more
 // stages.
-template <int kNpad, int kEpi, bool kGather, bool kPair = false>
+// kFp8: e4m3 operands (kind::f8f6f4) with per-tensor scales; a 128-byte K
+// block then holds 128 channels instead of 64, and the tiles are byte for
+// byte the bf16 ones.
+template <int kNpad, int kEpi, bool kGather, bool kPair = false, bool kFp8 = false>
 struct Layout {
     static constexpr bool kNorm = kEpi == kEpiGdn || kEpi == kEpiIgdn;
+    static constexpr int kKe = kFp8 ? 2 * kBK : kBK;  // operand elements per 128-byte K block
     static constexpr int kNB = kPair ? kNpad / 2 : kNpad;  // B / gamma rows this CTA holds
     // Dual tiles (GDN / IGDN layers fed by TMA): a tile is 256 output
     // pixels, one A box of 256 rows per K step, and each K step issues two
@@ -146,11 +154,14 @@ struct Layout {
     // bias (and GDN beta) split into bf16 hi + lo parts in K columns 0 and 1.
     // One K = 16 MMA of ones x bias starts each accumulation, and ones x beta
     // starts each GDN norm, so the epilogue adds neither.
-    static constexpr bool kFold = kEpi != kEpiScatter;
+    // FP8 layers scale the accumulator in the epilogue, so their bias is
+    // added there (after the scale) instead of folded.
+    static constexpr bool kFoldBias = kEpi != kEpiScatter && !kFp8;
+    static constexpr bool kFold = kFoldBias || kNorm;  // the ones tile exists
     static constexpr int kConstRow = 32;  // bytes per row of a K = 16 no-swizzle tile
     static constexpr int kOnes = kFold ? kBM * kConstRow : 0;
-    static constexpr int kBiasB = kFold ? kNB * kConstRow : 0;
-    static constexpr int kBetaB = kFold && kNorm ? kNB * kConstRow : 0;
+    static constexpr int kBiasB = kFoldBias ? kNB * kConstRow : 0;
+    static constexpr int kBetaB = kNorm ? kNB * kConstRow : 0;
     static constexpr int kFixedBytes = kWResBytes + kOnes + kBiasB + kBetaB + kW + kG + kX2 +
                                        kS + (kGather ? 2 * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
@@ -201,6 +212,7 @@ struct Layout {
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(kWResBytes % 1024 == 0 && (kNpad * kBK * 2) % 1024 == 0 || !kWRes, "resident weight alignment");
     static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
+    static_assert(!kFp8 || (!kGather && !kPair && kEpi != kEpiScatter), "FP8 instances: TMA-fed single-CTA layers");
     static_assert(!kPair || (!kGather && kEpi != kEpiScatter && kNB % 8 == 0), "pair instances: TMA operands");
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
 };
@@ -245,6 +257,11 @@ __device__ __forceinline__ void mma_issue_pair(uint32_t d, uint64_t a, uint64_t 
     else mma_bf16_pair(d, a, b, idesc, acc);
 }
 template <bool W>
+__device__ __forceinline__ void mma_issue_f8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    if (W) mma_e4m3_w(d, a, b, idesc, acc);
+    else mma_e4m3(d, a, b, idesc, acc);
+}
+template <bool W>
 __device__ __forceinline__ void commit_to(uint64_t *bar) {
     if (W) mma_commit_w(bar);
     else mma_commit(bar);
@@ -260,12 +277,12 @@ __device__ __forceinline__ void fail(const ConvParams &p, volatile int *abort, i
     if (p.err) atomicOr(p.err, code);
 }
 
-template <int kNpad, int kEpi, bool kGather, bool kPair>
-__global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads, 1)
+template <int kNpad, int kEpi, bool kGather, bool kPair, bool kFp8>
+__global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                    const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmO,
                    const ConvParams p) {
-    using Lay = Layout<kNpad, kEpi, kGather, kPair>;
+    using Lay = Layout<kNpad, kEpi, kGather, kPair, kFp8>;
     constexpr bool kNorm = Lay::kNorm;
     extern __shared__ unsigned char smem_raw[];
     unsigned char *smem =
@@ -341,6 +358,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 row = (r - kBM) % Lay::kNB;
                 const bool is_beta = r >= kBM + Lay::kNB;
                 if (is_beta && !kNorm) continue;
+                if (!is_beta && !Lay::kFoldBias) continue;
                 const int c = (int)rank * Lay::kNB + row;  // pairs: this CTA's half of the channels
                 const float v = is_beta ? (c < p.cout ? p.beta[c] : 1.f) : (c < p.cout ? p.bias[c] : 0.f);
                 const __nv_bfloat16 hi = __float2bfloat16_rn(v);
@@ -431,8 +449,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                             __syncwarp();
                         } else {
                             mbar_arrive_expect_tx_w(&full[s], Lay::kStage);
-                            tma_load_4d_w(st, &tmA, &full[s], cb * kBK, ix, iy, b);
-                            if (!Lay::kWRes) tma_load_3d_w(st + Lay::kA, &tmW, &full[s], cb * kBK, 0, tp.w[t]);
+                            tma_load_4d_w(st, &tmA, &full[s], cb * Lay::kKe, ix, iy, b);
+                            if (!Lay::kWRes) tma_load_3d_w(st + Lay::kA, &tmW, &full[s], cb * Lay::kKe, 0, tp.w[t]);
                         }
                         last_round[s] = (int)r;
                     }
@@ -482,6 +500,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
         constexpr bool W = Lay::kWarpIssue;
         if (leader && (W || lane == 0)) {
             const uint32_t idesc = idesc_bf16(kPair ? 2 * kBM : kBM, kNpad);
+            const uint32_t idesc_main = kFp8 ? idesc_e4m3(kBM, kNpad) : idesc;
             bool consts = !(kGather || Lay::kWRes);  // the first layer's / scatter layer's weights arrive once
             uint32_t it = 0;
             int j = 0;
@@ -517,14 +536,14 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     const uint32_t a0 = smem_u32(smem + s * Lay::kStage);
                     // the tile's accumulator starts as the bias (ones x bias)
                     const bool first = ks == 0;
-                    if (Lay::kFold && first) {
+                    if (Lay::kFoldBias && first) {
                         const uint64_t od = smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0);
                         const uint64_t bd = smem_desc(smem_u32(smem + Lay::offBiasB), 128, 256, 0);
                         if (kPair) mma_issue_pair<W>(d, od, bd, idesc, 0);
                         else mma_issue<W>(d, od, bd, idesc, 0);
                         if (Lay::kDual) mma_issue<W>(d + kBM, od, bd, idesc, 0);  // second half's columns
                     }
-                    const bool fresh = first && !Lay::kFold;  // the first MMA overwrites the accumulator
+                    const bool fresh = first && !Lay::kFoldBias;  // the first MMA overwrites the accumulator
                     if (kGather) {
                         const uint32_t w0 = smem_u32(smem + Lay::offW);
 #pragma unroll
@@ -542,13 +561,19 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                         const uint32_t b0 = Lay::kWRes ? smem_u32(smem + Lay::offWRes) + ks * (kNpad * kBK * 2)
                                                        : a0 + Lay::kA;
 #pragma unroll
-                        for (int kk = 0; kk < kBK / 16; ++kk) {
+                        // 4 MMAs per 128-byte K block: K = 16 bf16 or 32 e4m3 each
+                        for (int kk = 0; kk < 4; ++kk) {
                             const uint64_t bd = smem_desc(b0 + kk * 32, 16, 1024, 2);
-                            mma_issue<W>(d, smem_desc(a0 + kk * 32, 16, 1024, 2), bd, idesc, !(fresh && kk == 0));
+                            const uint64_t ad = smem_desc(a0 + kk * 32, 16, 1024, 2);
+                            const uint32_t acc = !(fresh && kk == 0);
+                            if (kFp8) mma_issue_f8<W>(d, ad, bd, idesc_main, acc);
+                            else mma_issue<W>(d, ad, bd, idesc, acc);
                             // dual tiles: rows 128-255 of A into the second half's columns
-                            if (Lay::kDual)
-                                mma_issue<W>(d + kBM, smem_desc(a0 + kBM * 128 + kk * 32, 16, 1024, 2), bd, idesc,
-                                             !(fresh && kk == 0));
+                            if (Lay::kDual) {
+                                const uint64_t ad1 = smem_desc(a0 + kBM * 128 + kk * 32, 16, 1024, 2);
+                                if (kFp8) mma_issue_f8<W>(d + kBM, ad1, bd, idesc_main, acc);
+                                else mma_issue<W>(d + kBM, ad1, bd, idesc, acc);
+                            }
                         }
                     }
                     // frees the stage (pairs: in both CTAs) once these MMAs have read it
@@ -606,6 +631,15 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                 tmem_wait_ld();
 #pragma unroll
                 for (int k = 0; k < kNpad / 16; ++k) tmem_regs_ready(xv[k]);
+                if (kFp8) {
+                    // x = (s_x s_w) * accumulator + bias
+                    const float sc = *p.act_scale * p.w_scale;
+#pragma unroll
+                    for (int k = 0; k < kNpad / 16; ++k)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            xv[k][e] = __float_as_uint(fmaf(__uint_as_float(xv[k][e]), sc, s_bias[k * 16 + e]));
+                }
                 if (h == 1) named_barrier_sync(4, 2 * kBM);  // group 0 is done with the tile
                 // x^2 (bf16) into the 128-byte-swizzled operand tile
 #pragma unroll
@@ -762,6 +796,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
             const int oy = gy * p.out_step + (p.phases == 4 ? (ph >> 1) : 0);
             const int ox = gx * p.out_step + (p.phases == 4 ? (ph & 1) : 0);
             const uint32_t d1 = tmem_base + buf * p.buf_stride + lane_addr;
+            const float sc = kFp8 ? *p.act_scale * p.w_scale : 1.f;  // FP8: the operand scales
             if (kEpi == kEpiScatter) {
                 // Transposed conv with few output channels: row m (an input
                 // pixel of the 8 x 16 tile incl. a 1-pixel halo) holds its
@@ -974,7 +1009,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     uint32_t o[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        o[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+                        o[e] = kFp8 ? pack_bf16x2(fmaf(__uint_as_float(v[2 * e]), sc, s_bias[c0 + 2 * e]),
+                                                  fmaf(__uint_as_float(v[2 * e + 1]), sc, s_bias[c0 + 2 * e + 1]))
+                                    : pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
                     if (valid) {
                         uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
                         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -995,6 +1032,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair>::kThreads,
                     for (int e = 0; e < 16; ++e) {
                         const int c = c0 + e;
                         float y = __uint_as_float(v[e]);
+                        if (kFp8) y = fmaf(y, sc, s_bias[c]);
                         if (kEpi == kEpiF32Clamp) y = fminf(fmaxf(y, 0.f), 1.f);
                         if (valid && c < p.cout) out[((int64_t)b * p.cout + c) * plane + pix] = y;
                     }
@@ -1134,11 +1172,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // bf16 operand tiles, 128-byte swizzled; fp32 = the first layer's unswizzled
 // input windows.  Out-of-bounds elements read as zero.
+enum class Elem { kBf16, kF32, kU8 };
 static int make_map(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
-                    const cuuint32_t *box, const cuuint32_t *estrides, bool fp32 = false) {
+                    const cuuint32_t *box, const cuuint32_t *estrides, bool fp32 = false, Elem elem = Elem::kBf16) {
     auto fn = encode_fn();
     if (!fn) return fcai::fail(FCAI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-    CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+    if (fp32) elem = Elem::kF32;
+    const CUtensorMapDataType dt = elem == Elem::kF32  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : elem == Elem::kU8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = fn(map, dt, rank,
                     const_cast<void *>(base), dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     fp32 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1159,12 +1202,12 @@ static int pick_tx(int gw, int max_tx = 128) {
     return best;
 }
 
-template <int kNpad, int kEpi, bool kGather, bool kPair = false>
+template <int kNpad, int kEpi, bool kGather, bool kPair = false, bool kFp8 = false>
 static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap &g, const CUtensorMap &o,
                   const ConvParams &p, cudaStream_t stream) {
-    using Lay = Layout<kNpad, kEpi, kGather, kPair>;
+    using Lay = Layout<kNpad, kEpi, kGather, kPair, kFp8>;
     static_assert(Lay::kAlloc <= kSmemBudget, "shared memory");
-    auto kernel = conv_tc_kernel<kNpad, kEpi, kGather, kPair>;
+    auto kernel = conv_tc_kernel<kNpad, kEpi, kGather, kPair, kFp8>;
     static int configured[64] = {0};
     static int max_clusters[64] = {0};
     int dev = 0;
@@ -1205,8 +1248,21 @@ static int launch(const CUtensorMap &a, const CUtensorMap &w, const CUtensorMap 
     return FCAI_OK;
 }
 
-static int dispatch(int npad, int epi, bool gather, bool pair, const CUtensorMap &a, const CUtensorMap &w,
+static int dispatch(int npad, int epi, bool gather, bool pair, bool fp8, const CUtensorMap &a, const CUtensorMap &w,
                     const CUtensorMap &g, const CUtensorMap &o, const ConvParams &p, cudaStream_t stream) {
+    if (fp8) {
+        if (npad == 128) {
+            switch (epi) {
+                case kEpiBf16: return launch<128, kEpiBf16, false, false, true>(a, w, g, o, p, stream);
+                case kEpiGdn: return launch<128, kEpiGdn, false, false, true>(a, w, g, o, p, stream);
+                case kEpiIgdn: return launch<128, kEpiIgdn, false, false, true>(a, w, g, o, p, stream);
+                default: break;
+            }
+        } else if (npad == 192 && epi == kEpiF32) {
+            return launch<192, kEpiF32, false, false, true>(a, w, g, o, p, stream);
+        }
+        return fcai::fail(FCAI_ERR_INVALID, "no FP8 kernel for npad=%d epilogue=%d", npad, epi);
+    }
     if (pair) {
         if (npad == 128) {
             switch (epi) {
@@ -1251,6 +1307,50 @@ static int dispatch(int npad, int epi, bool gather, bool pair, const CUtensorMap
             break;
     }
     return fcai::fail(FCAI_ERR_INVALID, "no kernel instance for npad=%d epilogue=%d", npad, epi);
+}
+
+// Per-tensor e4m3 quantisation (the reference's _symmetric_scale and
+// _quantize_fp8): amax of |x| over the tensor, scale = max(amax * fl(1/448), FLT_MIN),
+// q = e4m3(clamp(x / scale, +-448)) rounded to nearest even.  |x| >= 0, so
+// its float bits order like unsigned integers and atomicMax on them is the
+// float maximum.
+__global__ void amax_bf16_kernel(const uint4 *__restrict__ x, int64_t n8, uint32_t *amax_bits) {
+    float m = 0.f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint4 v = x[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            m = fmaxf(m, fabsf(__uint_as_float(w[j] << 16)));
+            m = fmaxf(m, fabsf(__uint_as_float(w[j] & 0xFFFF0000u)));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));
+}
+
+__global__ void quantize_e4m3_kernel(const uint4 *__restrict__ x, uint2 *__restrict__ out, int64_t n8,
+                                     const uint32_t *__restrict__ amax_bits, float *__restrict__ scale_out) {
+    // the reference divides by the Python float 448, which PyTorch's CUDA
+    // division by a host scalar computes as amax * fl(1 / 448); the elements
+    // are then divided by the scale tensor (a true division)
+    const float scale = fmaxf(__fmul_rn(__uint_as_float(*amax_bits), 1.0f / 448.0f), 1.17549435e-38f);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint4 v = x[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t q[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float2 f;
+            f.x = fminf(fmaxf(__fdiv_rn(__uint_as_float(w[j] << 16), scale), -448.f), 448.f);
+            f.y = fminf(fmaxf(__fdiv_rn(__uint_as_float(w[j] & 0xFFFF0000u), scale), -448.f), 448.f);
+            const uint32_t pair = (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+            q[j >> 1] |= pair << (16 * (j & 1));
+        }
+        out[i] = make_uint2(q[0], q[1]);
+    }
 }
 
 __global__ void nchw_to_nhwc_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out, int C, int HW,
@@ -1315,6 +1415,21 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     const bool pair = L->algorithm == FCAI_ALGO_IMPLICIT_GEMM_PAIR;
     // the kernel instance takes 256-pixel dual tiles exactly when this holds
     const bool dual = norm && !gather && !pair;
+    if (L->precision != FCAI_PREC_BF16 && L->precision != FCAI_PREC_FP8_E4M3)
+        return fcai::fail(FCAI_ERR_INVALID, "unknown layer precision %d", (int)L->precision);
+    const bool fp8 = L->precision == FCAI_PREC_FP8_E4M3;
+    if (fp8) {
+        if (gather || scatter || pair || L->cin % (2 * kBK))
+            return fcai::fail(FCAI_ERR_INVALID,
+                              "FP8 layers take e4m3 NHWC input with a multiple of 128 channels (no first-layer, "
+                              "scatter or CTA-pair algorithm)");
+        if (!((npad == 128 && (L->epilogue != FCAI_EPI_NONE || L->out_format == FCAI_FMT_NHWC_BF16)) ||
+              (npad == 192 && L->epilogue == FCAI_EPI_NONE && L->out_format == FCAI_FMT_NCHW_F32)))
+            return fcai::fail(FCAI_ERR_INVALID, "no FP8 kernel for npad=%d with this epilogue / output", npad);
+        if (!L->act_scale || !(L->weight_scale > 0.f) || !(L->weight_scale < 3.0e38f))
+            return fcai::fail(FCAI_ERR_INVALID, "FP8 layers need act_scale and a positive finite weight_scale");
+        if (!L->bias) return fcai::fail(FCAI_ERR_INVALID, "FP8 layers need a bias");
+    }
     if (pair && (gather || npad != L->cout || (npad != 128 && npad != 192)))
         return fcai::fail(FCAI_ERR_INVALID, "CTA-pair layers take bf16 NHWC input and 128 or 192 output channels");
     if (scatter && (!deconv || L->cout > 10 || npad != (25 * L->cout + 15) / 16 * 16 || norm ||
@@ -1372,7 +1487,9 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.stride = deconv ? 1 : 2;
     p.cin = L->cin;
     p.cout = L->cout;
-    p.cin_blocks = gather ? 1 : L->cin / kBK;
+    p.cin_blocks = gather ? 1 : L->cin / (fp8 ? 2 * kBK : kBK);  // 128-byte K blocks
+    p.act_scale = fp8 ? L->act_scale : nullptr;
+    p.w_scale = fp8 ? L->weight_scale : 1.f;
     p.Hout = ho;
     p.Wout = wo;
     p.out_step = deconv ? 2 : 1;
@@ -1458,18 +1575,23 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         if ((rc = make_map(&ma, input, 4, dims, strides, box, es, true))) return rc;
     }
     if (!gather) {
+        // operands: bf16 (2 bytes) or e4m3 (1 byte) elements; one box row is
+        // 128 bytes of channels either way
         const int s = p.stride;
+        const cuuint64_t eb = fp8 ? 1 : 2;
+        const cuuint32_t ke = fp8 ? 2 * kBK : kBK;
+        const Elem el = fp8 ? Elem::kU8 : Elem::kBf16;
         cuuint64_t dims[4] = {(cuuint64_t)L->cin, (cuuint64_t)w_in, (cuuint64_t)h_in, (cuuint64_t)batch};
-        cuuint64_t strides[3] = {(cuuint64_t)L->cin * 2, (cuuint64_t)w_in * L->cin * 2,
-                                 (cuuint64_t)h_in * w_in * L->cin * 2};
-        cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)(p.TX * s), (cuuint32_t)(p.TY * s), 1};
+        cuuint64_t strides[3] = {(cuuint64_t)L->cin * eb, (cuuint64_t)w_in * L->cin * eb,
+                                 (cuuint64_t)h_in * w_in * L->cin * eb};
+        cuuint32_t box[4] = {ke, (cuuint32_t)(p.TX * s), (cuuint32_t)(p.TY * s), 1};
         cuuint32_t es[4] = {1, (cuuint32_t)s, (cuuint32_t)s, 1};
-        if ((rc = make_map(&ma, input, 4, dims, strides, box, es))) return rc;
+        if ((rc = make_map(&ma, input, 4, dims, strides, box, es, false, el))) return rc;
         cuuint64_t wd[3] = {(cuuint64_t)L->cin, (cuuint64_t)npad, (cuuint64_t)(scatter ? 1 : 25)};
-        cuuint64_t ws[2] = {(cuuint64_t)L->cin * 2, (cuuint64_t)npad * L->cin * 2};
-        cuuint32_t wb[3] = {(cuuint32_t)kBK, (cuuint32_t)(pair ? npad / 2 : npad), 1};  // pairs: half the rows each
+        cuuint64_t ws[2] = {(cuuint64_t)L->cin * eb, (cuuint64_t)npad * L->cin * eb};
+        cuuint32_t wb[3] = {ke, (cuuint32_t)(pair ? npad / 2 : npad), 1};  // pairs: half the rows each
         cuuint32_t we[3] = {1, 1, 1};
-        if ((rc = make_map(&mw, L->weight, 3, wd, ws, wb, we))) return rc;
+        if ((rc = make_map(&mw, L->weight, 3, wd, ws, wb, we, false, el))) return rc;
     }
     if (norm) {
         cuuint64_t gd[3] = {(cuuint64_t)npad, (cuuint64_t)npad, 1};
@@ -1478,7 +1600,27 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         cuuint32_t ge[3] = {1, 1, 1};
         if ((rc = make_map(&mg, L->gdn_gamma, 3, gd, gs, gb, ge))) return rc;
     }
-    return dispatch(npad, epi, gather, pair, ma, mw, mg, mo, p, stream);
+    return dispatch(npad, epi, gather, pair, fp8, ma, mw, mg, mo, p, stream);
+}
+
+int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_out, uint32_t *amax_work,
+                       int64_t count, fcai_stream_t stream_) {
+    fcai::clear_error();
+    if (!input_bf16 || !output_e4m3 || !scale_out || !amax_work || count <= 0 || count % 8 ||
+        (reinterpret_cast<uintptr_t>(input_bf16) & 15) || (reinterpret_cast<uintptr_t>(output_e4m3) & 7) ||
+        (reinterpret_cast<uintptr_t>(amax_work) & 3) || (reinterpret_cast<uintptr_t>(scale_out) & 3))
+        return fcai::fail(FCAI_ERR_INVALID, "invalid e4m3 quantisation arguments");
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    const int64_t n8 = count / 8;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((n8 + threads - 1) / threads, (int64_t)fcai::sm_count() * 8);
+    FCAI_CUDA_TRY(cudaMemsetAsync(amax_work, 0, sizeof(uint32_t), stream));
+    ct::amax_bf16_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<const uint4 *>(input_bf16), n8, amax_work);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    ct::quantize_e4m3_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const uint4 *>(input_bf16), static_cast<uint2 *>(output_e4m3), n8, amax_work, scale_out);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
 }
 
 int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h, int32_t w,

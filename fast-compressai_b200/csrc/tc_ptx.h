@@ -176,6 +176,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[smem desc] * B[smem desc]; kind::f8f6f4 (e4m3 inputs per the
+// instruction descriptor, fp32 accumulate), K = 32 per instruction.
+__device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // Arrives on the mbarrier once every tcgen05 op issued so far by this thread completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -313,6 +324,15 @@ __device__ __forceinline__ void mma_bf16_pair_w(uint32_t d_tmem, uint64_t adesc,
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+__device__ __forceinline__ void mma_e4m3_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 __device__ __forceinline__ void mma_commit_w(uint64_t *bar) {
     asm volatile(
         "{\n\t.reg .pred e;\n\t"
@@ -375,6 +395,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
     return (1u << 4)                         // D format: f32
            | (1u << 7)                       // A format: bf16
            | (1u << 10)                      // B format: bf16
+           | ((uint32_t)(N >> 3) << 17)      // N / 8
+           | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+
+// Instruction descriptor of kind::f8f6f4 with e4m3 A and B (format code 0),
+// fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
+    return (1u << 4)                         // D format: f32
+           | (0u << 7)                       // A format: e4m3
+           | (0u << 10)                      // B format: e4m3
            | ((uint32_t)(N >> 3) << 17)      // N / 8
            | ((uint32_t)(M >> 4) << 24);     // M / 16
 }

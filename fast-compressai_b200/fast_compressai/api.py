@@ -12,9 +12,17 @@ Differences, all additive:
   * ``transforms="bf16"`` swaps g_a / g_s for this package's sm_100a
     tensor-core layers (default ``"fp32"`` keeps the model's own modules, as
     the reference does without a precision config);
-  * the reference's CAIEC precision search (``calibration_data``) and saved
-    precision maps (``precision_config_path``) are not part of this build
-    and raise ``ConfigurationError``.
+  * a saved precision map (``precision_config_path``, the reference's
+    schema-4 JSON) is applied to the B200 transforms: convolutions mapped to
+    "fp8" run the e4m3 tensor-core kernels where one exists, all other
+    modules run with bf16 operands, and the report's
+    ``precision_applications`` records each module's requested and applied
+    precision.  The map is checked against the model fingerprint, coder,
+    P_ch and operator inventory as the reference does; its candidate-catalog
+    fingerprint and device capability describe the reference's candidates
+    and search GPU and are not compared;
+  * the reference's CAIEC precision search (``calibration_data``) is not part
+    of this build and raises ``ConfigurationError``.
 """
 
 from __future__ import annotations
@@ -77,6 +85,9 @@ class AccelerationReport:
     p_ch_selection_status: str = "explicit"
     p_ch_selection_reason: str | None = None
     p_ch_sweep: tuple[Mapping[str, Any], ...] = ()
+    # (module_path, requested, applied, reason) per conv / GDN module when a
+    # precision map was applied (additive: not in the reference's report)
+    precision_applications: tuple[tuple[str, str, str, str | None], ...] = ()
 
     @property
     def accelerated(self) -> bool:
@@ -140,15 +151,23 @@ def accelerate(
         target = torch.device(cfg.device or "cuda")
         if target.type != "cuda":
             raise ConfigurationError("warp_div requires device='cuda'")
-        if cfg.precision_config_path is not None or calibration_data is not None:
-            raise ConfigurationError("CAIEC precision selection and saved precision configs are not part of this "
-                                     "build; use transforms='bf16' for the B200 tensor-core transforms")
+        if calibration_data is not None:
+            raise ConfigurationError("CAIEC precision selection is not part of this build; load a saved "
+                                     "precision config (precision_config_path) or use transforms='bf16'")
+        precision_config = None
+        layer_precisions = None
+        if cfg.precision_config_path is not None:
+            precision_config, layer_precisions = _load_precision_map(cfg.precision_config_path, model, cfg)
         runtime_model = copy.deepcopy(model).to(target).eval()
-        if transforms != "fp32":
+        if transforms != "fp32" or precision_config is not None:
             from .transforms import convert_factorized_prior
 
-            runtime_model = convert_factorized_prior(runtime_model, precision=transforms)
+            runtime_model = convert_factorized_prior(runtime_model, precision="bf16",
+                                                     layer_precisions=layer_precisions)
+            transforms = "bf16" if precision_config is None else "precision_map"
         p_ch = cfg.p_ch if cfg.p_ch is not None else 1
+        if precision_config is not None:
+            p_ch = precision_config.p_ch
         codec = FactorizedWarpDivCodec(runtime_model, p_ch)
     elif sample is not None:
         raise ConfigurationError("the legacy BF16 sample profiling of coder='rans' is not part of this build")
@@ -184,7 +203,48 @@ def accelerate(
         message=message,
         p_ch_selection_status="explicit" if P is not None or cfg.p_ch is not None else "default",
     )
+    if codec is not None and precision_config is not None:
+        apps = tuple(runtime_model.g_a.precision_notes) + tuple(runtime_model.g_s.precision_notes)
+        wrapped.acceleration_report = replace(
+            wrapped.acceleration_report,
+            precision_selection_status="loaded_from_config",
+            selected_candidate="precision_map",
+            rd_cost=float(precision_config.validated_rd_cost),
+            budget_met=bool(precision_config.budget_met),
+            precision_config_path=str(cfg.precision_config_path),
+            sensitivity_probe_count=len(precision_config.probe_records),
+            unavailable_probe_count=sum(1 for r in precision_config.probe_records
+                                        if r.get("unavailable_reason") is not None),
+            recovered_instance_count=len(precision_config.recovery_order),
+            p_ch_selection_status="loaded_from_config",
+            p_ch_selection_reason=(precision_config.p_ch_selection or {}).get("reason"),
+            p_ch_sweep=tuple((precision_config.p_ch_selection or {}).get("measurements", ())),
+            precision_applications=apps,
+        )
     return wrapped
+
+
+def _load_precision_map(path, model: nn.Module, cfg: AccelerationConfig):
+    """Load and check a saved precision config (the reference's api.py:193-236
+    checks, less the candidate-catalog fingerprint and device capability):
+    returns the config and its module_path -> precision map."""
+    from .configs.precision import PrecisionConfig, PrecisionConfigError, model_fingerprint
+
+    try:
+        config = PrecisionConfig.load(path)
+    except PrecisionConfigError as exc:
+        raise ConfigurationError(str(exc)) from exc
+    if config.model_fingerprint != model_fingerprint(model):
+        raise ConfigurationError("precision config model fingerprint does not match the input model")
+    if config.coder != cfg.coder or config.p_ch != (cfg.p_ch or 1):
+        raise ConfigurationError("precision config coder/P_ch does not match the request")
+    if config.device_type != "cuda":
+        raise ConfigurationError("precision config was not made for a CUDA device")
+    expected = {f"{t}.{i}" for t in ("g_a", "g_s") for i in range(7)}
+    paths = {a.module_path for a in config.assignments}
+    if paths != expected:
+        raise ConfigurationError("precision config operator inventory does not match the current model")
+    return config, config.precision_by_path()
 
 
 class FastModel(nn.Module):

@@ -24,6 +24,8 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+from typing import Mapping
+
 import torch
 from torch import nn
 
@@ -35,6 +37,11 @@ FCAI_LAYER_DECONV5S2 = 1
 FCAI_EPI_NONE, FCAI_EPI_GDN, FCAI_EPI_IGDN = 0, 1, 2
 FCAI_FMT_NHWC_BF16, FCAI_FMT_NCHW_F32 = 0, 1
 FCAI_ALGO_IMPLICIT_GEMM, FCAI_ALGO_SCATTER, FCAI_ALGO_IMPLICIT_GEMM_PAIR = 0, 1, 2
+FCAI_PREC_BF16, FCAI_PREC_FP8_E4M3 = 0, 1
+# e4m3 (float8_e4m3fn) range and the reference's per-tensor scale floor
+# (backends/pytorch/fp8_operators.py:16-17, 44-46)
+FP8_MAX = 448.0
+FP8_SCALE_MIN = float(torch.finfo(torch.float32).tiny)
 
 
 class FcaiLayer(ctypes.Structure):
@@ -48,11 +55,14 @@ class FcaiLayer(ctypes.Structure):
         ("out_format", ctypes.c_int32),
         ("clamp01", ctypes.c_int32),
         ("algorithm", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("precision", ctypes.c_int32),
         ("weight", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("gdn_beta", ctypes.c_void_p),
         ("gdn_gamma", ctypes.c_void_p),
+        ("act_scale", ctypes.c_void_p),
+        ("weight_scale", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -72,6 +82,33 @@ def pack_tma_weight(weight: torch.Tensor, transposed: bool, npad: int) -> torch.
     if npad > cout:
         packed = torch.cat([packed, packed.new_zeros(25, npad - cout, cin)], dim=1)
     return packed.to(torch.bfloat16).contiguous()
+
+
+def fp8_weight_scale(weight: torch.Tensor) -> float:
+    """Per-tensor symmetric scale of a weight as the reference computes it on
+    CUDA (backends/pytorch/fp8_operators.py:44-46): amax / 448 with the Python
+    float 448, which PyTorch evaluates as amax * fl32(1 / 448), floored at
+    FLT_MIN; written out so that it is the same on any device."""
+    amax = weight.detach().float().abs().amax().cpu()
+    inv = torch.tensor(1.0 / FP8_MAX, dtype=torch.float32)
+    return float(torch.clamp(amax * inv, min=FP8_SCALE_MIN))
+
+
+def pack_tma_weight_fp8(weight: torch.Tensor, transposed: bool, npad: int) -> tuple[torch.Tensor, float]:
+    """[25][npad][cin] e4m3 (as uint8) and its per-tensor scale: the bf16
+    packing's layout with q = e4m3(clamp(w / scale, +-448))."""
+    w = weight.detach().float()
+    scale = fp8_weight_scale(w)
+    if transposed:
+        cin, cout = w.shape[0], w.shape[1]
+        packed = w.permute(2, 3, 1, 0).reshape(25, cout, cin)
+    else:
+        cout, cin = w.shape[0], w.shape[1]
+        packed = w.permute(2, 3, 0, 1).reshape(25, cout, cin)
+    if npad > cout:
+        packed = torch.cat([packed, packed.new_zeros(25, npad - cout, cin)], dim=1)
+    q = torch.clamp(packed / torch.tensor(scale, dtype=torch.float32, device=packed.device), -FP8_MAX, FP8_MAX)
+    return q.to(torch.float8_e4m3fn).view(torch.uint8).contiguous(), scale
 
 
 def pack_gather_weight(weight: torch.Tensor, npad: int) -> torch.Tensor:
@@ -109,6 +146,7 @@ class _Layer:
     npad: int
     out_format: int
     name: str = ""
+    precision: str = "bf16"
 
     def flops(self, batch: int, h_in: int, w_in: int) -> float:
         """Algorithmic FLOPs: 2 * cin * 25 * cout per output (conv) or input
@@ -140,8 +178,26 @@ def _gdn_params(gdn: nn.Module):
     return beta.detach().float().contiguous(), gamma.detach().float().reshape(c, c)
 
 
+def fp8_supported(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool) -> str | None:
+    """None if the B200 FP8 kernels take this layer, else the reason they do
+    not (the layer then runs with bf16 operands)."""
+    if first:
+        return "the first analysis layer (cin = 3) has no FP8 kernel"
+    if conv.in_channels % 128:
+        return "FP8 layers need a multiple of 128 input channels"
+    npad = _round16(conv.out_channels)
+    transposed = isinstance(conv, nn.ConvTranspose2d)
+    if transposed and out_f32 and gdn is None and conv.out_channels <= 10:
+        return "the scatter algorithm of the last synthesis layer has no FP8 kernel"
+    if npad == 128 and not out_f32:
+        return None
+    if npad == 192 and out_f32 and gdn is None:
+        return None
+    return f"no FP8 kernel for {conv.out_channels} output channels with this epilogue"
+
+
 def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool,
-                pair: bool = False) -> _Layer:
+                pair: bool = False, precision: str = "bf16") -> _Layer:
     transposed = isinstance(conv, nn.ConvTranspose2d)
     if tuple(conv.kernel_size) != (5, 5) or tuple(conv.stride) != (2, 2) or tuple(conv.padding) != (2, 2):
         raise ConfigurationError("B200 transforms support 5x5 stride-2 padding-2 layers only")
@@ -165,6 +221,14 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         if cin % 64:
             raise ConfigurationError("B200 transforms need input channels divisible by 64")
         weight = pack_scatter_weight(conv.weight, npad) if scatter else pack_tma_weight(conv.weight, transposed, npad)
+    if precision not in ("bf16", "fp8"):
+        raise ConfigurationError(f"unknown B200 layer precision {precision!r}")
+    w_scale = 1.0
+    if precision == "fp8":
+        reason = fp8_supported(conv, gdn, first=first, out_f32=out_f32)
+        if reason is not None or pair:
+            raise ConfigurationError(reason or "FP8 layers do not use CTA pairs")
+        weight, w_scale = pack_tma_weight_fp8(conv.weight, transposed, npad)
     if npad > 256:
         raise ConfigurationError("B200 transforms support up to 256 output channels per layer")
     bias = conv.bias.detach().float().contiguous()
@@ -188,13 +252,16 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         out_format=out_format,
         clamp01=1 if clamp else 0,
         algorithm=FCAI_ALGO_SCATTER if scatter else (FCAI_ALGO_IMPLICIT_GEMM_PAIR if pair else FCAI_ALGO_IMPLICIT_GEMM),
+        precision=FCAI_PREC_FP8_E4M3 if precision == "fp8" else FCAI_PREC_BF16,
+        act_scale=None,
+        weight_scale=w_scale,
         reserved=0,
         weight=weight.data_ptr(),
         bias=bias.data_ptr(),
         gdn_beta=beta_ptr,
         gdn_gamma=gamma_ptr,
     )
-    return _Layer(desc, tuple(keep), desc.kind, cout, npad, out_format)
+    return _Layer(desc, tuple(keep), desc.kind, cout, npad, out_format, precision=precision)
 
 
 def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
@@ -216,7 +283,18 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
         if timing is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-        _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(cur.data_ptr()),
+        src = cur
+        if layer.precision == "fp8":
+            # the input's per-tensor e4m3 copy and its scale (amax / 448)
+            src = torch.empty(cur.shape, dtype=torch.uint8, device=x.device)
+            scal = torch.empty(2, dtype=torch.float32, device=x.device)  # [scale, amax bits]
+            _native.check(lib.fcai_quantize_e4m3(ctypes.c_void_p(cur.data_ptr()), ctypes.c_void_p(src.data_ptr()),
+                                                 ctypes.c_void_p(scal.data_ptr()),
+                                                 ctypes.c_void_p(scal.data_ptr() + 4), cur.numel(),
+                                                 ctypes.c_void_p(stream)))
+            _native.count_launches(2)
+            layer.desc.act_scale = scal.data_ptr()
+        _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
                                              ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
         _native.count_launches(1)
         if timing is not None:
@@ -241,23 +319,63 @@ class _Packed(nn.Sequential):
             self._sig = self._signature()
 
 
-class B200Analysis(_Packed):
-    """g_a on the tensor cores: fp32 NCHW image -> fp32 NCHW latent."""
+def resolve_precisions(prefix: str, modules: list, requested: Mapping[str, str] | None, *, first_conv: int | None,
+                       last_f32: bool) -> tuple[list[str], list[tuple[str, str, str, str | None]]]:
+    """Per fused layer of a 7-module g_a / g_s: the operand precision the B200
+    kernels use ("bf16" or "fp8"), and per module (path, requested, applied,
+    reason).  Convolutions requested in "fp8" get the e4m3 kernels where one
+    exists; every other request runs with bf16 operands (a 16-bit format:
+    "fp16" requests keep 16-bit operands, in bf16).  GDN / IGDN modules run
+    inside the convolution kernel, whose norm GEMM is bf16."""
+    requested = dict(requested or {})
+    layer_prec, notes = [], []
+    for i in range(0, 7, 2):
+        conv = modules[i]
+        gdn = modules[i + 1] if i + 1 < 7 else None
+        path = f"{prefix}.{i}"
+        want = requested.get(path, "bf16")
+        applied, reason = "bf16", None
+        if want == "fp8":
+            reason = fp8_supported(conv, gdn, first=(i == first_conv), out_f32=(i == 6 and last_f32))
+            if reason is None:
+                applied = "fp8"
+        elif want not in ("bf16", "fp16", "fp32"):
+            raise ConfigurationError(f"unknown precision {want!r} for {path}")
+        elif want != "bf16":
+            reason = f"{want} runs with bf16 operands on the B200 kernels"
+        layer_prec.append(applied)
+        notes.append((path, want, applied, reason))
+        if gdn is not None:
+            gpath = f"{prefix}.{i + 1}"
+            gwant = requested.get(gpath, "bf16")
+            notes.append((gpath, gwant, "bf16",
+                          None if gwant == "bf16" else "the fused GDN norm GEMM runs with bf16 operands"))
+    return layer_prec, notes
 
-    def __init__(self, g_a: nn.Sequential):
+
+class B200Analysis(_Packed):
+    """g_a on the tensor cores: fp32 NCHW image -> fp32 NCHW latent.
+
+    ``precisions`` maps module paths ("g_a.0" ... "g_a.6") to requested
+    precisions (a saved precision map); see ``resolve_precisions``."""
+
+    def __init__(self, g_a: nn.Sequential, precisions: Mapping[str, str] | None = None):
         super().__init__(*list(g_a))
         if len(self) != 7:
             raise ConfigurationError("g_a must be conv, GDN, conv, GDN, conv, GDN, conv")
+        self._layer_prec, self.precision_notes = resolve_precisions("g_a", list(self), precisions, first_conv=0,
+                                                                     last_f32=True)
         self._build()
         self._sig = self._signature()
 
     def _build(self) -> None:
         m = list(self)
+        lp = self._layer_prec
         self._layers = [
-            _make_layer(m[0], m[1], first=True, out_f32=False, clamp=False),
-            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False),
-            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False),
-            _make_layer(m[6], None, first=False, out_f32=True, clamp=False),
+            _make_layer(m[0], m[1], first=True, out_f32=False, clamp=False, precision=lp[0]),
+            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False, precision=lp[1]),
+            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False, precision=lp[2]),
+            _make_layer(m[6], None, first=False, out_f32=True, clamp=False, precision=lp[3]),
         ]
         for i, layer in enumerate(self._layers):
             layer.name = f"g_a.{2 * i}" + ("+gdn" if i < 3 else "")
@@ -279,23 +397,26 @@ class B200Synthesis(_Packed):
 
     fuses_clamp = True
 
-    def __init__(self, g_s: nn.Sequential):
+    def __init__(self, g_s: nn.Sequential, precisions: Mapping[str, str] | None = None):
         super().__init__(*list(g_s))
         if len(self) != 7:
             raise ConfigurationError("g_s must be deconv, IGDN, deconv, IGDN, deconv, IGDN, deconv")
         self.channels = self[0].in_channels
+        self._layer_prec, self.precision_notes = resolve_precisions("g_s", list(self), precisions, first_conv=None,
+                                                                     last_f32=True)
         self._build()
         self._sig = self._signature()
 
     def _build(self) -> None:
         m = list(self)
+        lp = self._layer_prec
         self._layers = [
-            _make_layer(m[0], m[1], first=False, out_f32=False, clamp=False),
-            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False),
-            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False),
+            _make_layer(m[0], m[1], first=False, out_f32=False, clamp=False, precision=lp[0]),
+            _make_layer(m[2], m[3], first=False, out_f32=False, clamp=False, precision=lp[1]),
+            _make_layer(m[4], m[5], first=False, out_f32=False, clamp=False, precision=lp[2]),
         ]
-        self._last = _make_layer(m[6], None, first=False, out_f32=True, clamp=False)
-        self._last_clamped = _make_layer(m[6], None, first=False, out_f32=True, clamp=True)
+        self._last = _make_layer(m[6], None, first=False, out_f32=True, clamp=False, precision=lp[3])
+        self._last_clamped = _make_layer(m[6], None, first=False, out_f32=True, clamp=True, precision=lp[3])
         for i, layer in enumerate(self._layers):
             layer.name = f"g_s.{2 * i}+igdn"
         self._last.name = self._last_clamped.name = "g_s.6"
@@ -315,8 +436,13 @@ class B200Synthesis(_Packed):
             return _run(self._layers + [self._last_clamped if clamp else self._last], nhwc, first_is_nchw=False)
 
 
-def convert_factorized_prior(model: nn.Module, precision: str = "bf16") -> nn.Module:
-    """Swap g_a / g_s for the B200 tensor-core modules (in place; returns the model)."""
+def convert_factorized_prior(model: nn.Module, precision: str = "bf16",
+                             layer_precisions: Mapping[str, str] | None = None) -> nn.Module:
+    """Swap g_a / g_s for the B200 tensor-core modules (in place; returns the model).
+
+    ``layer_precisions`` (module path -> "fp8" / "fp16" / "bf16" / "fp32",
+    e.g. a loaded precision map) selects the e4m3 kernels per convolution
+    where they exist; the modules' ``precision_notes`` record what ran."""
     if precision != "bf16":
         raise ConfigurationError(f"unsupported transform precision {precision!r}")
     if not torch.cuda.is_available():
@@ -325,8 +451,8 @@ def convert_factorized_prior(model: nn.Module, precision: str = "bf16") -> nn.Mo
     if dev.type != "cuda":
         raise ConfigurationError("convert the model after moving it to the CUDA device")
     with torch.no_grad(), torch.cuda.device(dev):
-        g_a = B200Analysis(model.g_a)
-        g_s = B200Synthesis(model.g_s)
+        g_a = B200Analysis(model.g_a, layer_precisions)
+        g_s = B200Synthesis(model.g_s, layer_precisions)
     # the new modules hold the same FP32 children, so state_dict keys are unchanged
     model.g_a = g_a
     model.g_s = g_s

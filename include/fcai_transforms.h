@@ -61,6 +61,16 @@ enum { FCAI_FMT_NHWC_BF16 = 0, FCAI_FMT_NCHW_F32 = 1 };
  *   halo tiles, each output pixel summing its taps in the epilogue, so the
  *   input is read about 1.5x instead of once per tap. */
 enum { FCAI_ALGO_IMPLICIT_GEMM = 0, FCAI_ALGO_SCATTER = 1, FCAI_ALGO_IMPLICIT_GEMM_PAIR = 2 };
+/* Operand precision of the convolution.  FCAI_PREC_FP8_E4M3 follows the
+ * reference's FP8 candidates (backends/pytorch/fp8_operators.py: per-tensor
+ * symmetric scales amax / 448, e4m3 operands, scaled GEMM, then bias): the
+ * input is e4m3 NHWC (fcai_quantize_e4m3) with its scale at act_scale, the
+ * weights are e4m3 packed like the bf16 TMA layers with scale weight_scale,
+ * the accumulator is multiplied by act_scale * weight_scale before the bias
+ * and epilogue.  TMA algorithm only, cin a multiple of 128; npad 128 (bf16
+ * NHWC output, optionally GDN / IGDN, whose norm GEMM stays bf16) or npad
+ * 192 without epilogue to fp32 NCHW (the latent layer). */
+enum { FCAI_PREC_BF16 = 0, FCAI_PREC_FP8_E4M3 = 1 };
 
 typedef struct {
     int32_t kind;       /* FCAI_LAYER_CONV5S2 or FCAI_LAYER_DECONV5S2 */
@@ -72,11 +82,14 @@ typedef struct {
     int32_t out_format; /* FCAI_FMT_*: NHWC_BF16 stores npad channels; NCHW_F32 stores cout */
     int32_t clamp01;    /* clamp outputs to [0, 1] (NCHW_F32 output only) */
     int32_t algorithm;  /* FCAI_ALGO_* */
-    int32_t reserved;
+    int32_t precision;  /* FCAI_PREC_* */
     const void *weight; /* packed, see above */
     const float *bias;
     const float *gdn_beta;
     const void *gdn_gamma;
+    const float *act_scale; /* FP8: device float, the input's scale (written by fcai_quantize_e4m3) */
+    float weight_scale;     /* FP8: the weights' scale */
+    int32_t reserved;
 } fcai_layer;
 
 /* Output spatial size of a layer for an input of h_in x w_in. */
@@ -85,6 +98,16 @@ int fcai_layer_out_size(const fcai_layer *layer, int32_t h_in, int32_t w_in, int
 /* One layer: output = epilogue(conv(input) + bias). */
 int fcai_layer_forward(const fcai_layer *layer, int32_t batch, int32_t h_in, int32_t w_in, const void *input,
                        void *output, int32_t *err, fcai_stream_t stream);
+
+/* Per-tensor symmetric e4m3 quantisation of a bf16 tensor of `count`
+ * elements (count % 8 == 0, 16-byte aligned buffers), as the reference's
+ * _symmetric_scale / _quantize_fp8 (backends/pytorch/fp8_operators.py:44-51):
+ * scale = max(amax(|x|) * fl(1 / 448), FLT_MIN) (the reference's amax / 448.0,
+ * which PyTorch's CUDA division by a host scalar evaluates this way),
+ * out = e4m3(clamp(x / scale, +-448)) rounded to nearest even.  Writes the scale to *scale_out (device) and the
+ * amax bits to *amax_work (device, 4 bytes, cleared by the call). */
+int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_out, uint32_t *amax_work,
+                       int64_t count, fcai_stream_t stream);
 
 /* fp32 NCHW [B, C, H, W] -> bf16 NHWC [B, H, W, C] (C % 8 == 0). */
 int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h,
