@@ -102,6 +102,7 @@ struct ConvParams {
     int patch_tma;       // first layer: 1 = input windows by TMA (tmA maps x_in), 0 = direct loads
     int patch_w, patch_h;  // patch box: columns (2 TX + 8), rows (2 TY + 3)
     uint32_t patch_bytes;
+    uint32_t *amax_out;      // optional: running max of |output| (float bits), for an FP8 consumer
     const float *act_scale;  // FP8 layers: device scale of the e4m3 input (amax / 448)
     float w_scale;           // FP8 layers: scale of the e4m3 weights
     int tma_store;       // GDN layers: the output tile leaves through TMA stores (tmO); 1 = 4-D
@@ -231,6 +232,19 @@ __device__ __forceinline__ void tile_coords(const ConvParams &p, int tile, int &
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
     __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// |x| of bf16 values orders like its bits without the sign, so the running
+// max of a thread's outputs is kept as two 16-bit lanes (vmaxu2) and folded
+// into one float at the end.
+__device__ __forceinline__ uint32_t amax_bf16x2(uint32_t am2, uint32_t packed) {
+    return __vmaxu2(am2, packed & 0x7FFF7FFFu);
+}
+// The warp's max |output| into *dst (float bits; all 32 lanes call it).
+__device__ __forceinline__ void amax_flush(uint32_t *dst, uint32_t am2) {
+    uint32_t am = max(am2 & 0xFFFFu, am2 >> 16) << 16;
+    am = __reduce_max_sync(0xffffffffu, am);
+    if (dst && (threadIdx.x & 31) == 0) atomicMax(dst, am);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -605,6 +619,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             const uint32_t x2 = smem_u32(smem + Lay::offX2);
             volatile int *t_ok = epi_ok;
             volatile int *h_ok = epi_ok + 1 + h;
+            uint32_t am2 = 0;  // max |output| of this thread's valid pixels (amax_out)
             bool consts = false;
             int j = 0;
             for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
@@ -709,6 +724,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
                             const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
                             o[e] = pack_bf16x2(__uint_as_float(xv[k][2 * e]) * r0, __uint_as_float(xv[k][2 * e + 1]) * r1);
+                            if (valid) am2 = amax_bf16x2(am2, o[e]);
                         }
                         if (p.tma_store) {
 #pragma unroll
@@ -747,6 +763,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 if (h == 0) named_barrier_arrive(4, 2 * kBM);
             }
             if (hleader && p.tma_store) bulk_wait_all();  // stores complete before the CTA exits
+            if (p.amax_out) amax_flush(p.amax_out, am2);
         } else {
         // Warp w reads TMEM lanes 32*(w%4).. (tile rows); with 8 warps either
         // column half w/4 of every tile, or (ping-pong) all columns of the
@@ -767,6 +784,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
         const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
         bool consts = !kNorm;
         volatile int *g_ok = epi_ok + grp;
+        uint32_t am2 = 0;  // max |output| of this thread's valid pixels (amax_out)
         uint64_t *g2 = &g2bar[grp];
         const uint32_t x2 = smem_u32(smem + Lay::offX2 + grp * Lay::kX2One);
         int j = grp;   // this CTA's tile index (groups take alternate tiles)
@@ -960,6 +978,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             const float x0 = __uint_as_float(v[k & 1][2 * e]);
                             const float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
                             o[e] = pack_bf16x2(x0 * r0, x1 * r1);
+                            if (valid) am2 = amax_bf16x2(am2, o[e]);
                         }
                         if (p.tma_store) {
                             // into the staging tile (the x^2 tile's layout: 128-byte
@@ -1012,6 +1031,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                         o[e] = kFp8 ? pack_bf16x2(fmaf(__uint_as_float(v[2 * e]), sc, s_bias[c0 + 2 * e]),
                                                   fmaf(__uint_as_float(v[2 * e + 1]), sc, s_bias[c0 + 2 * e + 1]))
                                     : pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+                    if (valid)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) am2 = amax_bf16x2(am2, o[e]);
                     if (valid) {
                         uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
                         dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -1051,6 +1073,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             named_barrier_sync(gbar, Lay::kGroupThreads);
         }
         if (kNorm && p.tma_store && gleader) bulk_wait_all();  // stores complete before the CTA exits
+        if (p.amax_out) amax_flush(p.amax_out, am2);
         }
     } else if (kGather) {
         // ------------------------------------------------------------ gather (first layer)
@@ -1489,6 +1512,10 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.cout = L->cout;
     p.cin_blocks = gather ? 1 : L->cin / (fp8 ? 2 * kBK : kBK);  // 128-byte K blocks
     p.act_scale = fp8 ? L->act_scale : nullptr;
+    if (L->amax_out && L->out_format != FCAI_FMT_NHWC_BF16)
+        return fcai::fail(FCAI_ERR_INVALID, "amax_out is for layers with a bf16 NHWC output");
+    if (L->amax_out && scatter) return fcai::fail(FCAI_ERR_INVALID, "amax_out is not produced by scatter layers");
+    p.amax_out = L->amax_out;
     p.w_scale = fp8 ? L->weight_scale : 1.f;
     p.Hout = ho;
     p.Wout = wo;
@@ -1604,7 +1631,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
 }
 
 int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_out, uint32_t *amax_work,
-                       int64_t count, fcai_stream_t stream_) {
+                       int32_t amax_ready, int64_t count, fcai_stream_t stream_) {
     fcai::clear_error();
     if (!input_bf16 || !output_e4m3 || !scale_out || !amax_work || count <= 0 || count % 8 ||
         (reinterpret_cast<uintptr_t>(input_bf16) & 15) || (reinterpret_cast<uintptr_t>(output_e4m3) & 7) ||
@@ -1614,9 +1641,12 @@ int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_o
     const int64_t n8 = count / 8;
     const int threads = 256;
     const int64_t blocks = std::min<int64_t>((n8 + threads - 1) / threads, (int64_t)fcai::sm_count() * 8);
-    FCAI_CUDA_TRY(cudaMemsetAsync(amax_work, 0, sizeof(uint32_t), stream));
-    ct::amax_bf16_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<const uint4 *>(input_bf16), n8, amax_work);
-    FCAI_CUDA_TRY(cudaGetLastError());
+    if (!amax_ready) {
+        FCAI_CUDA_TRY(cudaMemsetAsync(amax_work, 0, sizeof(uint32_t), stream));
+        ct::amax_bf16_kernel<<<(unsigned)blocks, threads, 0, stream>>>(static_cast<const uint4 *>(input_bf16), n8,
+                                                                        amax_work);
+        FCAI_CUDA_TRY(cudaGetLastError());
+    }
     ct::quantize_e4m3_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
         static_cast<const uint4 *>(input_bf16), static_cast<uint2 *>(output_e4m3), n8, amax_work, scale_out);
     FCAI_CUDA_TRY(cudaGetLastError());

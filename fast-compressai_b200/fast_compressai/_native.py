@@ -75,7 +75,7 @@ SIGNATURES: dict[str, tuple] = {
     "fcai_last_error": (ctypes.c_char_p, []),
     "fcai_version": (ctypes.c_char_p, []),
     "fcai_payload_copy_async": (ctypes.c_int, [_P, _P, _I64, _P]),
-    "fcai_quantize_e4m3": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P]),
+    "fcai_quantize_e4m3": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I64, _P]),
     "fcai_warp_div_plan_create": (ctypes.c_int, [_I32, _I32, _I32, _I32, ctypes.POINTER(WarpDivPlan)]),
     "fcai_warp_div_encode": (
         ctypes.c_int,

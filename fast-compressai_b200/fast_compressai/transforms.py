@@ -63,6 +63,7 @@ class FcaiLayer(ctypes.Structure):
         ("act_scale", ctypes.c_void_p),
         ("weight_scale", ctypes.c_float),
         ("reserved", ctypes.c_int32),
+        ("amax_out", ctypes.c_void_p),
     ]
 
 
@@ -273,8 +274,13 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
     else:
         h, w = x.shape[1], x.shape[2]
     cur = x
-    for layer in layers:
+    scal = None  # [scale, amax bits] of the current input when the producing layer computed its amax
+    for i, layer in enumerate(layers):
         ho, wo = (2 * h, 2 * w) if layer.kind == FCAI_LAYER_DECONV5S2 else ((h - 1) // 2 + 1, (w - 1) // 2 + 1)
+        # an FP8 next layer takes its input's amax from this layer's epilogue
+        nxt = layers[i + 1] if i + 1 < len(layers) else None
+        feeds_fp8 = (nxt is not None and nxt.precision == "fp8" and layer.out_format == FCAI_FMT_NHWC_BF16
+                     and layer.desc.algorithm != FCAI_ALGO_SCATTER)
         if layer.out_format == FCAI_FMT_NHWC_BF16:
             out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=x.device)
         else:
@@ -285,18 +291,29 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
             ev0.record()
         src = cur
         if layer.precision == "fp8":
-            # the input's per-tensor e4m3 copy and its scale (amax / 448)
+            # the input's per-tensor e4m3 copy and its scale (amax / 448); the
+            # amax came with the input when the previous layer produced it
             src = torch.empty(cur.shape, dtype=torch.uint8, device=x.device)
-            scal = torch.empty(2, dtype=torch.float32, device=x.device)  # [scale, amax bits]
+            ready = scal is not None
+            if not ready:
+                scal = torch.zeros(2, dtype=torch.float32, device=x.device)
             _native.check(lib.fcai_quantize_e4m3(ctypes.c_void_p(cur.data_ptr()), ctypes.c_void_p(src.data_ptr()),
                                                  ctypes.c_void_p(scal.data_ptr()),
-                                                 ctypes.c_void_p(scal.data_ptr() + 4), cur.numel(),
-                                                 ctypes.c_void_p(stream)))
-            _native.count_launches(2)
+                                                 ctypes.c_void_p(scal.data_ptr() + 4), 1 if ready else 0,
+                                                 cur.numel(), ctypes.c_void_p(stream)))
+            _native.count_launches(1 if ready else 2)
             layer.desc.act_scale = scal.data_ptr()
-        _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
-                                             ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
+        next_scal = None
+        if feeds_fp8:
+            next_scal = torch.zeros(2, dtype=torch.float32, device=x.device)
+            layer.desc.amax_out = next_scal.data_ptr() + 4
+        try:
+            _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
+                                                 ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
+        finally:
+            layer.desc.amax_out = None  # the buffer is this call's
         _native.count_launches(1)
+        scal = next_scal
         if timing is not None:
             ev1.record()
             timing.append((layer.name, layer.flops(B, h, w), ev0, ev1))

@@ -90,6 +90,8 @@ typedef struct {
     const float *act_scale; /* FP8: device float, the input's scale (written by fcai_quantize_e4m3) */
     float weight_scale;     /* FP8: the weights' scale */
     int32_t reserved;
+    uint32_t *amax_out;     /* optional (bf16 NHWC outputs): device word the layer raises to the float bits of
+                               max |output| over the tensor (caller zeroes it), for an FP8 consumer's scale */
 } fcai_layer;
 
 /* Output spatial size of a layer for an input of h_in x w_in. */
@@ -104,10 +106,13 @@ int fcai_layer_forward(const fcai_layer *layer, int32_t batch, int32_t h_in, int
  * _symmetric_scale / _quantize_fp8 (backends/pytorch/fp8_operators.py:44-51):
  * scale = max(amax(|x|) * fl(1 / 448), FLT_MIN) (the reference's amax / 448.0,
  * which PyTorch's CUDA division by a host scalar evaluates this way),
- * out = e4m3(clamp(x / scale, +-448)) rounded to nearest even.  Writes the scale to *scale_out (device) and the
- * amax bits to *amax_work (device, 4 bytes, cleared by the call). */
+ * out = e4m3(clamp(x / scale, +-448)) rounded to nearest even.  Writes the
+ * scale to *scale_out (device).  With amax_ready = 0 the call computes the
+ * amax into *amax_work (device, 4 bytes, cleared first); with amax_ready != 0,
+ * *amax_work already holds it (the producing layer's amax_out) and the call
+ * only quantises. */
 int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_out, uint32_t *amax_work,
-                       int64_t count, fcai_stream_t stream);
+                       int32_t amax_ready, int64_t count, fcai_stream_t stream);
 
 /* fp32 NCHW [B, C, H, W] -> bf16 NHWC [B, H, W, C] (C % 8 == 0). */
 int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, int32_t channels, int32_t h,

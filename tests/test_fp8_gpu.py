@@ -42,7 +42,7 @@ def _quantize(x_bf16):
     stream = torch.cuda.current_stream().cuda_stream
     _native.check(_native.lib().fcai_quantize_e4m3(ctypes.c_void_p(x_bf16.data_ptr()), ctypes.c_void_p(q.data_ptr()),
                                                    ctypes.c_void_p(scal.data_ptr()),
-                                                   ctypes.c_void_p(scal.data_ptr() + 4), x_bf16.numel(),
+                                                   ctypes.c_void_p(scal.data_ptr() + 4), 0, x_bf16.numel(),
                                                    ctypes.c_void_p(stream)))
     return q, scal[0]
 
@@ -103,6 +103,38 @@ def test_fp8_layers_match_the_scaled_gemm(cuda_device, kind, cout, use_gdn, H, W
         torch.cuda.synchronize()
         mine = out if out_f32 else out.float().permute(0, 3, 1, 2)
         _check(mine, _ref_fp8_layer(x, conv, gdn, out_bf16=not out_f32))
+
+
+@pytest.mark.parametrize("kind", ["conv_gdn", "deconv_igdn", "first_layer"])
+def test_producer_amax_equals_the_tensor_amax(cuda_device, kind):
+    # a layer whose output feeds an FP8 layer reports max |output| over its
+    # valid pixels (ragged tiles included) through amax_out; the quantiser
+    # then skips its own pass.  Bit-exact with the amax of the output tensor.
+    torch.manual_seed(5)
+    first = kind == "first_layer"
+    if kind == "deconv_igdn":
+        conv = torch.nn.ConvTranspose2d(128, 128, 5, 2, 2, output_padding=1).to(cuda_device)
+        gdn = GDN(128, inverse=True).to(cuda_device)
+        x = torch.randn(2, 128, 9, 13, device=cuda_device)
+    elif first:
+        conv = torch.nn.Conv2d(3, 128, 5, 2, 2).to(cuda_device)
+        gdn = GDN(128).to(cuda_device)
+        x = torch.rand(2, 3, 36, 52, device=cuda_device)
+    else:
+        conv = torch.nn.Conv2d(128, 128, 5, 2, 2).to(cuda_device)
+        gdn = GDN(128).to(cuda_device)
+        x = torch.randn(2, 128, 37, 50, device=cuda_device)
+    nxt = torch.nn.Conv2d(128, 128, 5, 2, 2).to(cuda_device)
+    with torch.no_grad():
+        a = _make_layer(conv, gdn, first=first, out_f32=False, clamp=False)
+        b = _make_layer(nxt, GDN(128).to(cuda_device), first=False, out_f32=False, clamp=False, precision="fp8")
+        inp = x if first else x.permute(0, 2, 3, 1).contiguous().to(torch.bfloat16)
+        mid = _run([a], inp, first_is_nchw=first)
+        both = _run([a, b], inp, first_is_nchw=first)  # amax from a's epilogue
+        alone = _run([b], mid, first_is_nchw=False)      # amax pass of the quantiser
+        torch.cuda.synchronize()
+        assert torch.equal(both, alone)
+        assert a.desc.amax_out is None
 
 
 def _map_for(model, p_ch, tmp_path):
