@@ -52,6 +52,8 @@ def parse_args(argv=None):
     ap.add_argument("--transforms", choices=("bf16", "fp32"), default="bf16")
     ap.add_argument("--cpu-sample", type=int, default=1, help="images in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-precision-map", action="store_true",
+                    help="skip the extra measurement with the reference's example precision map (FP8 layers)")
     ap.add_argument("--chunk-images", type=int, default=4,
                     help="images per upload / download chunk of the one-batch-at-a-time end-to-end measurement")
     ap.add_argument("--stream-chunk-images", type=int, default=0,
@@ -495,6 +497,50 @@ def run_b200(args):
         x_ref = ref.g_s(torch.round(ref.g_a(xs) - medr) + medr).clamp(0, 1)
         psnr_drop = psnr(x_ref, xs) - psnr(x_hat[:nq], xs)
 
+        # ---- the reference's example precision map ------------------------
+        # (examples/precision_configs/FactorizedPrior of the reference, kept as
+        # a test fixture): convolutions it maps to fp8 run the e4m3 kernels
+        # where one exists, everything else bf16.  The fixture's model
+        # fingerprint is rewritten for this random-init model.  Same step,
+        # timing and L2 flush as the headline.
+        pmap = None
+        fixture = ROOT / "tests" / "golden" / "precision_map_factorized.json"
+        if not args.no_precision_map and fixture.exists():
+            import tempfile
+
+            from fast_compressai.configs import model_fingerprint
+
+            data = json.loads(fixture.read_text())
+            data["model_fingerprint"] = model_fingerprint(model)
+            data["p_ch"] = args.p_ch
+            with tempfile.TemporaryDirectory() as td, torch.inference_mode(False):
+                mp = Path(td) / "map.json"
+                mp.write_text(json.dumps(data))
+                fast_pm = fast_compressai.accelerate(model, P=args.p_ch, device=str(dev), precision_config_path=str(mp))
+            for _ in range(max(args.warmup, 1)):
+                out_pm = fast_pm.compress(x)
+                x_hat_pm = fast_pm.decompress(out_pm["strings"], out_pm["shape"])["x_hat"]
+            pm_ev = []
+            for _ in range(args.steps):
+                flush.fill_(1.0)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                out_pm = fast_pm.compress(x)
+                x_hat_pm = fast_pm.decompress(out_pm["strings"], out_pm["shape"])["x_hat"]
+                b.record()
+                pm_ev.append((a, b))
+            torch.cuda.synchronize()
+            pm_ms = sum(a.elapsed_time(b) for a, b in pm_ev) / len(pm_ev)
+            rep_pm = fast_pm.acceleration_report
+            pmap = {
+                "value": in_bytes / (pm_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": pm_ms,
+                "psnr_drop_db_vs_fp32": psnr(x_ref, xs) - psnr(x_hat_pm[:nq], xs),
+                "payload_bytes_ratio_vs_headline": out_pm["strings"][0].packed.numel() / packed_bytes,
+                "fp8_modules": [m for m, _, got, _ in rep_pm.precision_applications if got == "fp8"],
+                "note": "per rank, not gathered; the reference's example map with its fingerprint rewritten",
+            }
+            del fast_pm
+
     # ---- payload-size gather (the only collective of the path) --------------
     gathered = sharding.gather_payload_stats(sharding.payload_stats(payload), device=dev)
     total_payload = gathered["packed_bytes"]
@@ -570,6 +616,7 @@ def run_b200(args):
             "bpp_per_input_value": total_payload * 8 / (world * x.numel()),
             "bpp_per_pixel": total_payload * 8 / (world * x.numel() / 3),
             "psnr_drop_db_vs_fp32": psnr_drop,
+            "precision_map": pmap,
             "ans": {
                 "encode_ms": enc_ms,
                 "decode_ms": dec_ms,

@@ -327,7 +327,8 @@ class _Packed(nn.Sequential):
     from them; the packs are rebuilt if a parameter is modified in place."""
 
     def _signature(self):
-        return tuple((id(t), t._version) for t in self.parameters())
+        # inference tensors have no version counter (and cannot change in place)
+        return tuple((id(t), -1 if t.is_inference() else t._version) for t in self.parameters())
 
     def _refresh_if_stale(self) -> None:
         if self._sig != self._signature():
