@@ -90,6 +90,7 @@ struct ConvParams {
     int clamp;                                        // scatter epilogue: clamp to [0, 1]
     int stride;                                       // input step per GEMM pixel (2 conv, 1 deconv)
     int cin, cout, cin_blocks;
+    int out_c0, cout_total;                           // fp32 NCHW output: first channel written, channels per image
     int Hout, Wout, out_step;                         // output tensor size, output step per GEMM pixel
     int Hin, Win;
     int tiles_total;
@@ -127,7 +128,10 @@ struct Layout {
     // pixels, one A box of 256 rows per K step, and each K step issues two
     // M = 128 MMAs that share the B tile, so each byte of weights loaded
     // feeds twice the MMA work.
-    static constexpr bool kDual = kNorm && !kGather && !kPair;
+    // GDN over 192 channels: the accumulator and the norm (384 TMEM columns)
+    // leave room for one buffer, and the first layer one input window
+    static constexpr bool kWide = kNorm && kNpad > 128;
+    static constexpr bool kDual = kNorm && !kGather && !kPair && !kWide;
     static constexpr int kRows = kDual ? 2 * kBM : kBM;  // output pixels per tile
     static constexpr int kA = kGather ? kBM * kGatherK * 2 : kRows * kBK * 2;
     // the scatter layer's weights (npad x cin, at most 4 K blocks) stay
@@ -142,7 +146,8 @@ struct Layout {
     // epilogues outweigh their short mainloops): two groups of 4 warps take alternate tiles, each with its own
     // accumulator buffer, x^2 / staging tile and GDN barrier, so one tile's
     // GDN GEMM and stores overlap the other's passes.
-    static constexpr bool kPingPong = (kGather && kNorm) || kEpi == kEpiScatter;
+    static constexpr bool kPingPong = (kGather && kNorm && !kWide) || kEpi == kEpiScatter;
+    static constexpr int kPatchBufs = kWide ? 1 : 2;  // first layer: input window buffers
     static constexpr int kX2One = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kX2 = kPingPong ? 2 * kX2One : kX2One;
     static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
@@ -164,7 +169,7 @@ struct Layout {
     static constexpr int kBiasB = kFoldBias ? kNB * kConstRow : 0;
     static constexpr int kBetaB = kNorm ? kNB * kConstRow : 0;
     static constexpr int kFixedBytes = kWResBytes + kOnes + kBiasB + kBetaB + kW + kG + kX2 +
-                                       kS + (kGather ? 2 * kPatchBuf : 0) +
+                                       kS + (kGather ? kPatchBufs * kPatchBuf : 0) +
                                        2 * kNpad * 4 + (2 * kMaxStages + 11) * 8 + 32 + 1024;
     static constexpr int kStagesRaw = (kSmemBudget - kFixedBytes) / kStage;
     static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
@@ -173,7 +178,7 @@ struct Layout {
     static constexpr int offG = offW + kW;
     static constexpr int offX2 = offG + kG;
     static constexpr int offS = offX2 + kX2;
-    static constexpr int kP = kGather ? 2 * kPatchBuf : 0;
+    static constexpr int kP = kGather ? kPatchBufs * kPatchBuf : 0;
     static constexpr int offPatch = offS + kS;
     static constexpr int offOnes = offPatch + kP;
     static constexpr int offBiasB = offOnes + kOnes;
@@ -184,7 +189,7 @@ struct Layout {
     // TMEM accumulator buffers: 2, or 4 for the scatter layer (128 columns
     // each), whose short tiles would otherwise make the MMA wait for the
     // epilogue of the tile before last
-    static constexpr int kAccBufs = kEpi == kEpiScatter ? 4 : 2;
+    static constexpr int kAccBufs = kEpi == kEpiScatter ? 4 : (kWide ? 1 : 2);
     static constexpr int kBars = 2 * kStages + 2 * kAccBufs + 4 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
     static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
@@ -212,7 +217,8 @@ struct Layout {
     static_assert(offOnes % 128 == 0 && kOnes % 128 == 0 && kBiasB % 128 == 0, "constant tile alignment");
     static_assert(kB % 1024 == 0, "B stage alignment");
     static_assert(kWResBytes % 1024 == 0 && (kNpad * kBK * 2) % 1024 == 0 || !kWRes, "resident weight alignment");
-    static_assert(!kNorm || kNpad == 128, "GDN fusion is built for 128 channels");
+    static_assert(!kNorm || kNpad == 128 || kNpad == 192, "GDN fusion is built for 128 or 192 channels");
+    static_assert(!kWide || !kPair, "192-channel GDN has no CTA-pair instance");
     static_assert(!kFp8 || (!kGather && !kPair && kEpi != kEpiScatter), "FP8 instances: TMA-fed single-CTA layers");
     static_assert(!kPair || (!kGather && kEpi != kEpiScatter && kNB % 8 == 0), "pair instances: TMA operands");
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
@@ -419,8 +425,9 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             if (cbytes) {
                 mbar_arrive_expect_tx(cbar, cbytes);
                 if (kNorm) {  // pairs: this CTA's half of the gamma rows
-                    tma_load_3d(smem + Lay::offG, &tmG, cbar, 0, (int)rank * Lay::kNB, 0);
-                    tma_load_3d(smem + Lay::offG + Lay::kG / 2, &tmG, cbar, kBK, (int)rank * Lay::kNB, 0);
+                    for (int kb = 0; kb < kNpad / kBK; ++kb)
+                        tma_load_3d(smem + Lay::offG + kb * (Lay::kNB * 128), &tmG, cbar, kb * kBK,
+                                    (int)rank * Lay::kNB, 0);
                 }
                 if (kGather) bulk_load(smem + Lay::offW, p.wgather, Lay::kW, cbar);
                 if (Lay::kWRes)
@@ -479,14 +486,14 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             }
         }
         if (kGather && p.patch_tma && lane == 0) {
-            // input windows: patch buffer it % 2 for the CTA's it-th tile
+            // input windows: patch buffer it % kPatchBufs for the CTA's it-th tile
             uint32_t it = 0;
             int last_round[2] = {-1, -1};
             for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
                 int b, ph, gy0, gx0;
                 tile_coords(p, tile, b, ph, gy0, gx0);
-                const int pb = it & 1;
-                const uint32_t r = it >> 1;
+                const int pb = (int)(it % Lay::kPatchBufs);
+                const uint32_t r = it / Lay::kPatchBufs;
                 if (!mbar_wait(&pempty[pb], (r & 1) ^ 1, abort, kWaitNs)) {
                     fail(p, abort, kErrProducer);
                     break;
@@ -749,11 +756,11 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                     const int hy = gy0 + h * (p.TY / 2);
                     if (p.tma_store == 2) {
                         const int yrow = b * p.GH + hy;
-                        tma_store_5d(&tmO, stg, 0, ph & 1, gx0, ph >> 1, yrow);
-                        tma_store_5d(&tmO, stg + kBM * 128, kBK, ph & 1, gx0, ph >> 1, yrow);
+                        for (int kb = 0; kb < kNpad / kBK; ++kb)
+                            tma_store_5d(&tmO, stg + kb * (kBM * 128), kb * kBK, ph & 1, gx0, ph >> 1, yrow);
                     } else {
-                        tma_store_4d(&tmO, stg, 0, gx0, hy, b);
-                        tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, hy, b);
+                        for (int kb = 0; kb < kNpad / kBK; ++kb)
+                            tma_store_4d(&tmO, stg + kb * (kBM * 128), kb * kBK, gx0, hy, b);
                     }
                     bulk_commit_group();
                 }
@@ -1008,11 +1015,11 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             // transposed conv: phase (py, px) of the output viewed as
                             // [B * Hout / 2][py][Wout / 2][px][C]
                             const int yrow = b * p.GH + gy0;
-                            tma_store_5d(&tmO, stg, 0, ph & 1, gx0, ph >> 1, yrow);
-                            tma_store_5d(&tmO, stg + kBM * 128, kBK, ph & 1, gx0, ph >> 1, yrow);
+                            for (int kb = 0; kb < kNpad / kBK; ++kb)
+                                tma_store_5d(&tmO, stg + kb * (kBM * 128), kb * kBK, ph & 1, gx0, ph >> 1, yrow);
                         } else {
-                            tma_store_4d(&tmO, stg, 0, gx0, gy0, b);
-                            tma_store_4d(&tmO, stg + kBM * 128, kBK, gx0, gy0, b);
+                            for (int kb = 0; kb < kNpad / kBK; ++kb)
+                                tma_store_4d(&tmO, stg + kb * (kBM * 128), kb * kBK, gx0, gy0, b);
                         }
                         bulk_commit_group();
                     }
@@ -1056,7 +1063,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                         float y = __uint_as_float(v[e]);
                         if (kFp8) y = fmaf(y, sc, s_bias[c]);
                         if (kEpi == kEpiF32Clamp) y = fminf(fmaxf(y, 0.f), 1.f);
-                        if (valid && c < p.cout) out[((int64_t)b * p.cout + c) * plane + pix] = y;
+                        if (valid && c < p.cout) out[((int64_t)b * p.cout_total + p.out_c0 + c) * plane + pix] = y;
                     }
                 }
             }
@@ -1091,8 +1098,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             }
             const uint32_t a0 = smem_u32(smem + s * Lay::kStage) + row_off;
             if (p.patch_tma) {
-                const int pb = it & 1;
-                if (!mbar_wait(&pfull[pb], (it >> 1) & 1, abort, kWaitNs)) {
+                const int pb = (int)(it % Lay::kPatchBufs);
+                if (!mbar_wait(&pfull[pb], (it / Lay::kPatchBufs) & 1, abort, kWaitNs)) {
                     fail(p, abort, kErrGather);
                     break;
                 }
@@ -1303,7 +1310,8 @@ static int dispatch(int npad, int epi, bool gather, bool pair, bool fp8, const C
     }
     if (gather) {
         if (npad == 128 && epi == kEpiGdn) return launch<128, kEpiGdn, true>(a, w, g, o, p, stream);
-        return fcai::fail(FCAI_ERR_INVALID, "first-layer kernel is built for 128 channels with GDN");
+        if (npad == 192 && epi == kEpiGdn) return launch<192, kEpiGdn, true>(a, w, g, o, p, stream);
+        return fcai::fail(FCAI_ERR_INVALID, "first-layer kernel is built for 128 or 192 channels with GDN");
     }
     switch (npad) {
         case 128:
@@ -1318,6 +1326,11 @@ static int dispatch(int npad, int epi, bool gather, bool pair, bool fp8, const C
         case 192:
             if (epi == kEpiF32) return launch<192, kEpiF32, false>(a, w, g, o, p, stream);
             if (epi == kEpiBf16) return launch<192, kEpiBf16, false>(a, w, g, o, p, stream);
+            if (epi == kEpiGdn) return launch<192, kEpiGdn, false>(a, w, g, o, p, stream);
+            if (epi == kEpiIgdn) return launch<192, kEpiIgdn, false>(a, w, g, o, p, stream);
+            break;
+        case 160:  // half of a 320-channel latent layer
+            if (epi == kEpiF32) return launch<160, kEpiF32, false>(a, w, g, o, p, stream);
             break;
         case 16:
             if (epi == kEpiF32Clamp) return launch<16, kEpiF32Clamp, false>(a, w, g, o, p, stream);
@@ -1437,7 +1450,7 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         return fcai::fail(FCAI_ERR_INVALID, "unknown layer algorithm %d", (int)L->algorithm);
     const bool pair = L->algorithm == FCAI_ALGO_IMPLICIT_GEMM_PAIR;
     // the kernel instance takes 256-pixel dual tiles exactly when this holds
-    const bool dual = norm && !gather && !pair;
+    const bool dual = norm && !gather && !pair && npad <= 128;
     if (L->precision != FCAI_PREC_BF16 && L->precision != FCAI_PREC_FP8_E4M3)
         return fcai::fail(FCAI_ERR_INVALID, "unknown layer precision %d", (int)L->precision);
     const bool fp8 = L->precision == FCAI_PREC_FP8_E4M3;
@@ -1510,6 +1523,11 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.stride = deconv ? 1 : 2;
     p.cin = L->cin;
     p.cout = L->cout;
+    p.out_c0 = L->out_channel_offset;
+    p.cout_total = L->out_channels_total ? L->out_channels_total : L->cout;
+    if (p.out_c0 < 0 || p.out_c0 + p.cout > p.cout_total ||
+        ((p.out_c0 || L->out_channels_total) && L->out_format != FCAI_FMT_NCHW_F32))
+        return fcai::fail(FCAI_ERR_INVALID, "output channel range outside the fp32 NCHW output");
     p.cin_blocks = gather ? 1 : L->cin / (fp8 ? 2 * kBK : kBK);  // 128-byte K blocks
     p.act_scale = fp8 ? L->act_scale : nullptr;
     if (L->amax_out && L->out_format != FCAI_FMT_NHWC_BF16)
@@ -1529,7 +1547,8 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     uint32_t stride = 32;
     while (stride < (uint32_t)per_buf) stride <<= 1;
     p.buf_stride = stride;
-    p.tmem_cols = (scatter ? 4 : 2) * stride;  // the kernel's accumulator buffer count
+    // the kernel's accumulator buffer count (Layout::kAccBufs)
+    p.tmem_cols = (scatter ? 4 : (norm && npad > 128 ? 1 : 2)) * stride;
     if (p.tmem_cols > 512) return fcai::fail(FCAI_ERR_INVALID, "accumulators exceed tensor memory");
     if (scatter) {
         p.taps[0].n = 1;  // one K pass over the halo tile, all taps are GEMM columns

@@ -62,8 +62,10 @@ class FcaiLayer(ctypes.Structure):
         ("gdn_gamma", ctypes.c_void_p),
         ("act_scale", ctypes.c_void_p),
         ("weight_scale", ctypes.c_float),
-        ("reserved", ctypes.c_int32),
+        ("out_channel_offset", ctypes.c_int32),
         ("amax_out", ctypes.c_void_p),
+        ("out_channels_total", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -148,10 +150,15 @@ class _Layer:
     out_format: int
     name: str = ""
     precision: str = "bf16"
+    # a layer wider than one MMA (cout > 256, fp32 NCHW output) runs as parts
+    # that read the same input and write disjoint channel ranges
+    parts: tuple = ()
 
     def flops(self, batch: int, h_in: int, w_in: int) -> float:
         """Algorithmic FLOPs: 2 * cin * 25 * cout per output (conv) or input
         (deconv) pixel, plus 2 * cout^2 per output pixel for GDN."""
+        if self.parts:
+            return sum(part.flops(batch, h_in, w_in) for part in self.parts)
         d = self.desc
         if self.kind == FCAI_LAYER_DECONV5S2:
             pix_in, pix_out = h_in * w_in, 4 * h_in * w_in
@@ -200,6 +207,9 @@ def fp8_supported(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f3
 def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool,
                 pair: bool = False, precision: str = "bf16") -> _Layer:
     transposed = isinstance(conv, nn.ConvTranspose2d)
+    if (not transposed and not first and gdn is None and out_f32 and not pair and precision == "bf16"
+            and conv.out_channels > 256 and conv.bias is not None):
+        return _make_split_layer(conv, clamp=clamp)
     if tuple(conv.kernel_size) != (5, 5) or tuple(conv.stride) != (2, 2) or tuple(conv.padding) != (2, 2):
         raise ConfigurationError("B200 transforms support 5x5 stride-2 padding-2 layers only")
     if transposed and tuple(conv.output_padding) != (1, 1):
@@ -212,8 +222,8 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
     scatter = transposed and out_f32 and gdn is None and cout <= 10
     if scatter:
         npad = _round16(25 * cout)
-    if gdn is not None and npad != 128:
-        raise ConfigurationError("B200 GDN fusion is built for 128-channel layers")
+    if gdn is not None and npad not in (128, 192):
+        raise ConfigurationError("B200 GDN fusion is built for 128- and 192-channel layers")
     if first:
         if cin != 3 or transposed:
             raise ConfigurationError("the first analysis layer must be a 3-channel convolution")
@@ -256,6 +266,9 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         precision=FCAI_PREC_FP8_E4M3 if precision == "fp8" else FCAI_PREC_BF16,
         act_scale=None,
         weight_scale=w_scale,
+        out_channel_offset=0,
+        amax_out=None,
+        out_channels_total=0,
         reserved=0,
         weight=weight.data_ptr(),
         bias=bias.data_ptr(),
@@ -263,6 +276,28 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         gdn_gamma=gamma_ptr,
     )
     return _Layer(desc, tuple(keep), desc.kind, cout, npad, out_format, precision=precision)
+
+
+def _make_split_layer(conv: nn.Conv2d, *, clamp: bool) -> _Layer:
+    """A convolution to fp32 NCHW with more output channels than one MMA
+    takes (the 320-channel latent layer of FactorizedPrior(192, 320)): equal
+    parts of at most 256 channels, each its own launch on the same input,
+    writing its channel range of the shared output."""
+    cout = conv.out_channels
+    nparts = (cout + 255) // 256
+    width = _round16((cout + nparts - 1) // nparts)
+    parts = []
+    for c0 in range(0, cout, width):
+        c1 = min(c0 + width, cout)
+        sub = nn.Conv2d(conv.in_channels, c1 - c0, 5, 2, 2).to(conv.weight.device)
+        with torch.no_grad():
+            sub.weight.copy_(conv.weight[c0:c1])
+            sub.bias.copy_(conv.bias[c0:c1])
+        part = _make_layer(sub, None, first=False, out_f32=True, clamp=clamp)
+        part.desc.out_channel_offset = c0
+        part.desc.out_channels_total = cout
+        parts.append(part)
+    return _Layer(None, (), FCAI_LAYER_CONV5S2, cout, parts[0].npad, FCAI_FMT_NCHW_F32, parts=tuple(parts))
 
 
 def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
@@ -280,7 +315,7 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
         # an FP8 next layer takes its input's amax from this layer's epilogue
         nxt = layers[i + 1] if i + 1 < len(layers) else None
         feeds_fp8 = (nxt is not None and nxt.precision == "fp8" and layer.out_format == FCAI_FMT_NHWC_BF16
-                     and layer.desc.algorithm != FCAI_ALGO_SCATTER)
+                     and not layer.parts and layer.desc.algorithm != FCAI_ALGO_SCATTER)
         if layer.out_format == FCAI_FMT_NHWC_BF16:
             out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=x.device)
         else:
@@ -304,15 +339,22 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
             _native.count_launches(1 if ready else 2)
             layer.desc.act_scale = scal.data_ptr()
         next_scal = None
-        if feeds_fp8:
-            next_scal = torch.zeros(2, dtype=torch.float32, device=x.device)
-            layer.desc.amax_out = next_scal.data_ptr() + 4
-        try:
-            _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
-                                                 ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
-        finally:
-            layer.desc.amax_out = None  # the buffer is this call's
-        _native.count_launches(1)
+        if layer.parts:
+            for part in layer.parts:
+                _native.check(lib.fcai_layer_forward(ctypes.byref(part.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
+                                                     ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
+                _native.count_launches(1)
+        else:
+            if feeds_fp8:
+                next_scal = torch.zeros(2, dtype=torch.float32, device=x.device)
+                layer.desc.amax_out = next_scal.data_ptr() + 4
+            try:
+                _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w,
+                                                     ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                                     None, ctypes.c_void_p(stream)))
+            finally:
+                layer.desc.amax_out = None  # the buffer is this call's
+            _native.count_launches(1)
         scal = next_scal
         if timing is not None:
             ev1.record()

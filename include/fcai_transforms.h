@@ -76,7 +76,7 @@ typedef struct {
     int32_t kind;       /* FCAI_LAYER_CONV5S2 or FCAI_LAYER_DECONV5S2 */
     int32_t cin;        /* input channels (3 with in_format NCHW_F32, else a multiple of 64) */
     int32_t cout;       /* output channels */
-    int32_t npad;       /* MMA width: cout rounded up to 16 (<= 256; 128 with GDN/IGDN) */
+    int32_t npad;       /* MMA width: cout rounded up to 16 (<= 256; 128 or 192 with GDN/IGDN) */
     int32_t epilogue;   /* FCAI_EPI_* */
     int32_t in_format;  /* FCAI_FMT_*: NCHW_F32 only for the cin == 3 first analysis layer */
     int32_t out_format; /* FCAI_FMT_*: NHWC_BF16 stores npad channels; NCHW_F32 stores cout */
@@ -89,9 +89,12 @@ typedef struct {
     const void *gdn_gamma;
     const float *act_scale; /* FP8: device float, the input's scale (written by fcai_quantize_e4m3) */
     float weight_scale;     /* FP8: the weights' scale */
-    int32_t reserved;
+    int32_t out_channel_offset; /* NCHW_F32 output: channel of the output tensor this layer's channel 0
+                                   lands on (0); a wider layer runs as several launches */
     uint32_t *amax_out;     /* optional (bf16 NHWC outputs): device word the layer raises to the float bits of
                                max |output| over the tensor (caller zeroes it), for an FP8 consumer's scale */
+    int32_t out_channels_total; /* NCHW_F32 output: channels per image of the output tensor (0: cout) */
+    int32_t reserved;
 } fcai_layer;
 
 /* Output spatial size of a layer for an input of h_in x w_in. */
