@@ -63,6 +63,9 @@ def parse_args(argv=None):
                     help="BASELINE config 3 instead: the coder alone on 64 x 192 x 32 x 48 Laplacian symbols, "
                          "P in {1, 2, 4, 8, 16, 48, 192}")
     ap.add_argument("--sweep-p", type=str, default="1,2,4,8,16,48,192")
+    ap.add_argument("--config4", action="store_true",
+                    help="BASELINE config 4 instead: FactorizedPrior(192, 320), 4 x 3 x 2048 x 2048, P = 8, with "
+                         "FP32, bf16 and fp8 transforms")
     return ap.parse_args(argv)
 
 
@@ -708,12 +711,107 @@ def run_ans_sweep(args):
     return 0
 
 
+def run_config4(args):
+    """FactorizedPrior(192, 320), random-init weights with update(force=True), 4 x 3 x
+    2048 x 2048 seeded smoothed-noise images, P = 8.  Compress + decompress throughput (fp32 input-image
+    bytes per second, input resident on the device, each step bracketed by CUDA events) with the FP32
+    transforms (the model's own torch modules, cuDNN with PyTorch's default conv settings, as the
+    reference runs them without a precision config), the B200 bf16 transforms and the B200 fp8
+    transforms; per variant the PSNR of the reconstruction, its drop against FP32, the payload size
+    against FP32's and the per-layer kernel times.  Each step's working set (> 3 GB of activations)
+    exceeds the 126 MB L2."""
+    import torch
+
+    import fast_compressai
+    from fast_compressai import _native, transforms
+    from fast_compressai.balle import FactorizedPrior
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    model = FactorizedPrior(192, 320).eval()
+    model.update(force=True)
+    B, H, W, P = 4, 2048, 2048, 8
+    x = smooth_noise_images(B, H, W, seed=4321).to(dev)
+    in_bytes = x.numel() * 4
+    peaks = read_peaks()
+    rows = {}
+    ref_psnr = ref_bytes = None
+    clock_info = None
+    for name in ("fp32", "bf16", "fp8"):
+        fast = fast_compressai.accelerate(model, P=P, device=str(dev), transforms=name)
+        with torch.inference_mode():
+            for _ in range(max(args.warmup, 1)):
+                out = fast.compress(x)
+                x_hat = fast.decompress(out["strings"], out["shape"])["x_hat"]
+            torch.cuda.synchronize()
+            clocks = ClockSampler(dev.index)
+            launches0 = _native.LAUNCHES["kernels"]
+            transforms.LAYER_TIMING = layer_events = []
+            events = []
+            for _ in range(args.steps):
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                e0.record()
+                out = fast.compress(x)
+                e1.record()
+                x_hat = fast.decompress(out["strings"], out["shape"])["x_hat"]
+                e2.record()
+                events.append((e0, e1, e2))
+            torch.cuda.synchronize()
+            transforms.LAYER_TIMING = None
+            launches = _native.LAUNCHES["kernels"] - launches0
+            info = clocks.stop()
+            if name == "bf16":
+                clock_info = info
+        ms = sum(a.elapsed_time(c) for a, _, c in events) / args.steps
+        comp = sum(a.elapsed_time(b) for a, b, _ in events) / args.steps
+        q = psnr(x_hat, x)
+        nbytes = out["strings"][0].packed.numel()
+        if name == "fp32":
+            ref_psnr, ref_bytes = q, nbytes
+        per_layer = {}
+        for lname, flops, a, b in layer_events:
+            d = per_layer.setdefault(lname, {"ms": 0.0, "n": 0, "flops": flops})
+            d["ms"] += a.elapsed_time(b)
+            d["n"] += 1
+        layers = {k: {"ms": round(v["ms"] / v["n"], 4),
+                      "tflops": round(v["flops"] / (v["ms"] / v["n"] / 1e3) / 1e12, 1)} for k, v in per_layer.items()}
+        row = {"value": in_bytes / (ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": ms, "compress_ms": comp,
+               "decompress_ms": ms - comp, "psnr_db": q, "psnr_drop_db_vs_fp32": ref_psnr - q,
+               "payload_bytes": nbytes, "payload_ratio_vs_fp32": nbytes / ref_bytes,
+               "bpp_per_value": nbytes * 8 / x.numel(), "gpu_launches_per_step": launches / args.steps}
+        if layers:
+            row["layers"] = layers
+        rep = fast.acceleration_report
+        if rep.precision_applications:
+            row["fp8_modules"] = [m for m, _, got, _ in rep.precision_applications if got == "fp8"]
+        rows[name] = row
+        del fast, out, x_hat
+        torch.cuda.empty_cache()
+    line = {
+        "metric": "compress+decompress GB/s (fp32 input image bytes), FactorizedPrior(192,320) P=8, BASELINE config 4",
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "bf16 / e4m3 operands, fp32 accumulate (fp32: the torch modules)",
+        "data": "synthetic: seeded smoothed-noise images (config 4), random-init weights",
+        "config": {"workload": "config 4", "model": "FactorizedPrior(192,320)", "batch": B, "image": [H, W],
+                   "p_ch": P, "l2": "working set > L2 (activations > 3 GB per step)",
+                   "cudnn_allow_tf32": bool(torch.backends.cudnn.allow_tf32)},
+        "variants": rows, "clocks": clock_info, "peaks": {k: peaks.get(k) for k in ("bf16_tflops", "bf16_tflops_sustained")},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
     if args.ans_sweep:
         return run_ans_sweep(args)
+    if args.config4:
+        return run_config4(args)
     return run_b200(args)
 
 

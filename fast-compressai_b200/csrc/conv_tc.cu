@@ -895,8 +895,13 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             uint32_t w[4];
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
-                                const float a = __uint_as_float(v[k & 1][q * 8 + e * 2]);
-                                const float bb = __uint_as_float(v[k & 1][q * 8 + e * 2 + 1]);
+                                float a = __uint_as_float(v[k & 1][q * 8 + e * 2]);
+                                float bb = __uint_as_float(v[k & 1][q * 8 + e * 2 + 1]);
+                                if (kFp8) {  // x = (s_x s_w) * accumulator + bias
+                                    const int c = c_lo + k * 16 + q * 8 + e * 2;
+                                    a = fmaf(a, sc, s_bias[c]);
+                                    bb = fmaf(bb, sc, s_bias[c + 1]);
+                                }
                                 w[e] = pack_bf16x2(a * a, bb * bb);
                             }
                             const int k0 = c_lo + k * 16 + q * 8;
@@ -982,8 +987,12 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             // GDN: x / sqrt(n); IGDN: x * sqrt(n)
                             const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
                             const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
-                            const float x0 = __uint_as_float(v[k & 1][2 * e]);
-                            const float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
+                            float x0 = __uint_as_float(v[k & 1][2 * e]);
+                            float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
+                            if (kFp8) {
+                                x0 = fmaf(x0, sc, s_bias[c0 + 2 * e]);
+                                x1 = fmaf(x1, sc, s_bias[c0 + 2 * e + 1]);
+                            }
                             o[e] = pack_bf16x2(x0 * r0, x1 * r1);
                             if (valid) am2 = amax_bf16x2(am2, o[e]);
                         }
@@ -1288,8 +1297,12 @@ static int dispatch(int npad, int epi, bool gather, bool pair, bool fp8, const C
                 case kEpiIgdn: return launch<128, kEpiIgdn, false, false, true>(a, w, g, o, p, stream);
                 default: break;
             }
-        } else if (npad == 192 && epi == kEpiF32) {
-            return launch<192, kEpiF32, false, false, true>(a, w, g, o, p, stream);
+        } else if (npad == 192) {
+            if (epi == kEpiF32) return launch<192, kEpiF32, false, false, true>(a, w, g, o, p, stream);
+            if (epi == kEpiGdn) return launch<192, kEpiGdn, false, false, true>(a, w, g, o, p, stream);
+            if (epi == kEpiIgdn) return launch<192, kEpiIgdn, false, false, true>(a, w, g, o, p, stream);
+        } else if (npad == 160 && epi == kEpiF32) {
+            return launch<160, kEpiF32, false, false, true>(a, w, g, o, p, stream);
         }
         return fcai::fail(FCAI_ERR_INVALID, "no FP8 kernel for npad=%d epilogue=%d", npad, epi);
     }
@@ -1455,12 +1468,13 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
         return fcai::fail(FCAI_ERR_INVALID, "unknown layer precision %d", (int)L->precision);
     const bool fp8 = L->precision == FCAI_PREC_FP8_E4M3;
     if (fp8) {
-        if (gather || scatter || pair || L->cin % (2 * kBK))
+        if (gather || scatter || pair || L->cin % kBK)
             return fcai::fail(FCAI_ERR_INVALID,
-                              "FP8 layers take e4m3 NHWC input with a multiple of 128 channels (no first-layer, "
+                              "FP8 layers take e4m3 NHWC input with a multiple of 64 channels (no first-layer, "
                               "scatter or CTA-pair algorithm)");
+        const bool f32_out = L->epilogue == FCAI_EPI_NONE && L->out_format == FCAI_FMT_NCHW_F32;
         if (!((npad == 128 && (L->epilogue != FCAI_EPI_NONE || L->out_format == FCAI_FMT_NHWC_BF16)) ||
-              (npad == 192 && L->epilogue == FCAI_EPI_NONE && L->out_format == FCAI_FMT_NCHW_F32)))
+              (npad == 192 && (norm || f32_out)) || (npad == 160 && f32_out)))
             return fcai::fail(FCAI_ERR_INVALID, "no FP8 kernel for npad=%d with this epilogue / output", npad);
         if (!L->act_scale || !(L->weight_scale > 0.f) || !(L->weight_scale < 3.0e38f))
             return fcai::fail(FCAI_ERR_INVALID, "FP8 layers need act_scale and a positive finite weight_scale");
@@ -1528,7 +1542,9 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     if (p.out_c0 < 0 || p.out_c0 + p.cout > p.cout_total ||
         ((p.out_c0 || L->out_channels_total) && L->out_format != FCAI_FMT_NCHW_F32))
         return fcai::fail(FCAI_ERR_INVALID, "output channel range outside the fp32 NCHW output");
-    p.cin_blocks = gather ? 1 : L->cin / (fp8 ? 2 * kBK : kBK);  // 128-byte K blocks
+    // 128-byte K blocks.  FP8: 128 channels each; a last block past cin
+    // (cin = 192, 320) reads as zeros (TMA fills elements outside the tensor)
+    p.cin_blocks = gather ? 1 : (fp8 ? (L->cin + 2 * kBK - 1) / (2 * kBK) : L->cin / kBK);
     p.act_scale = fp8 ? L->act_scale : nullptr;
     if (L->amax_out && L->out_format != FCAI_FMT_NHWC_BF16)
         return fcai::fail(FCAI_ERR_INVALID, "amax_out is for layers with a bf16 NHWC output");

@@ -11,7 +11,9 @@ Differences, all additive:
     this package's FP32 restatement ``fast_compressai.balle.FactorizedPrior``;
   * ``transforms="bf16"`` swaps g_a / g_s for this package's sm_100a
     tensor-core layers (default ``"fp32"`` keeps the model's own modules, as
-    the reference does without a precision config);
+    the reference does without a precision config); ``transforms="fp8"``
+    does the same with e4m3 operands (per-tensor scales, as the reference's
+    FP8 candidates) for every convolution that has an e4m3 kernel;
   * a saved precision map (``precision_config_path``, the reference's
     schema-4 JSON) is applied to the B200 transforms: convolutions mapped to
     "fp8" run the e4m3 tensor-core kernels where one exists, all other
@@ -109,7 +111,7 @@ def _is_factorized_prior(model: nn.Module) -> bool:
     return type(model) is FactorizedPrior
 
 
-_TRANSFORMS = ("fp32", "bf16")
+_TRANSFORMS = ("fp32", "bf16", "fp8")
 
 
 def accelerate(
@@ -162,9 +164,13 @@ def accelerate(
         if transforms != "fp32" or precision_config is not None:
             from .transforms import convert_factorized_prior
 
-            runtime_model = convert_factorized_prior(runtime_model, precision="bf16",
+            if precision_config is not None and transforms != "fp32":
+                raise ConfigurationError("a precision config selects the transform precisions; leave "
+                                         "transforms at its default")
+            runtime_model = convert_factorized_prior(runtime_model,
+                                                     precision="fp8" if transforms == "fp8" else "bf16",
                                                      layer_precisions=layer_precisions)
-            transforms = "bf16" if precision_config is None else "precision_map"
+            transforms = transforms if precision_config is None else "precision_map"
         p_ch = cfg.p_ch if cfg.p_ch is not None else 1
         if precision_config is not None:
             p_ch = precision_config.p_ch
@@ -221,6 +227,9 @@ def accelerate(
             p_ch_sweep=tuple((precision_config.p_ch_selection or {}).get("measurements", ())),
             precision_applications=apps,
         )
+    elif codec is not None and transforms == "fp8":
+        apps = tuple(runtime_model.g_a.precision_notes) + tuple(runtime_model.g_s.precision_notes)
+        wrapped.acceleration_report = replace(wrapped.acceleration_report, precision_applications=apps)
     return wrapped
 
 

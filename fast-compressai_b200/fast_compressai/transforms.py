@@ -97,11 +97,15 @@ def fp8_weight_scale(weight: torch.Tensor) -> float:
     return float(torch.clamp(amax * inv, min=FP8_SCALE_MIN))
 
 
-def pack_tma_weight_fp8(weight: torch.Tensor, transposed: bool, npad: int) -> tuple[torch.Tensor, float]:
+def pack_tma_weight_fp8(weight: torch.Tensor, transposed: bool, npad: int,
+                        scale: float | None = None) -> tuple[torch.Tensor, float]:
     """[25][npad][cin] e4m3 (as uint8) and its per-tensor scale: the bf16
-    packing's layout with q = e4m3(clamp(w / scale, +-448))."""
+    packing's layout with q = e4m3(clamp(w / scale, +-448)).  ``scale``
+    defaults to the weight's own (a slice of a wider layer passes the whole
+    layer's)."""
     w = weight.detach().float()
-    scale = fp8_weight_scale(w)
+    if scale is None:
+        scale = fp8_weight_scale(w)
     if transposed:
         cin, cout = w.shape[0], w.shape[1]
         packed = w.permute(2, 3, 1, 0).reshape(25, cout, cin)
@@ -191,25 +195,26 @@ def fp8_supported(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f3
     not (the layer then runs with bf16 operands)."""
     if first:
         return "the first analysis layer (cin = 3) has no FP8 kernel"
-    if conv.in_channels % 128:
-        return "FP8 layers need a multiple of 128 input channels"
+    if conv.in_channels % 64:
+        return "FP8 layers need a multiple of 64 input channels"
     npad = _round16(conv.out_channels)
     transposed = isinstance(conv, nn.ConvTranspose2d)
     if transposed and out_f32 and gdn is None and conv.out_channels <= 10:
         return "the scatter algorithm of the last synthesis layer has no FP8 kernel"
-    if npad == 128 and not out_f32:
+    if not out_f32 and (npad == 128 or (gdn is not None and npad == 192)):
         return None
-    if npad == 192 and out_f32 and gdn is None:
+    # latents: 192 channels, or 320 as two launches of 160
+    if out_f32 and gdn is None and (npad in (160, 192) or (not transposed and conv.out_channels == 320)):
         return None
     return f"no FP8 kernel for {conv.out_channels} output channels with this epilogue"
 
 
 def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32: bool, clamp: bool,
-                pair: bool = False, precision: str = "bf16") -> _Layer:
+                pair: bool = False, precision: str = "bf16", fp8_scale: float | None = None) -> _Layer:
     transposed = isinstance(conv, nn.ConvTranspose2d)
-    if (not transposed and not first and gdn is None and out_f32 and not pair and precision == "bf16"
+    if (not transposed and not first and gdn is None and out_f32 and not pair
             and conv.out_channels > 256 and conv.bias is not None):
-        return _make_split_layer(conv, clamp=clamp)
+        return _make_split_layer(conv, clamp=clamp, precision=precision)
     if tuple(conv.kernel_size) != (5, 5) or tuple(conv.stride) != (2, 2) or tuple(conv.padding) != (2, 2):
         raise ConfigurationError("B200 transforms support 5x5 stride-2 padding-2 layers only")
     if transposed and tuple(conv.output_padding) != (1, 1):
@@ -239,7 +244,7 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
         reason = fp8_supported(conv, gdn, first=first, out_f32=out_f32)
         if reason is not None or pair:
             raise ConfigurationError(reason or "FP8 layers do not use CTA pairs")
-        weight, w_scale = pack_tma_weight_fp8(conv.weight, transposed, npad)
+        weight, w_scale = pack_tma_weight_fp8(conv.weight, transposed, npad, fp8_scale)
     if npad > 256:
         raise ConfigurationError("B200 transforms support up to 256 output channels per layer")
     bias = conv.bias.detach().float().contiguous()
@@ -278,26 +283,32 @@ def _make_layer(conv: nn.Module, gdn: nn.Module | None, *, first: bool, out_f32:
     return _Layer(desc, tuple(keep), desc.kind, cout, npad, out_format, precision=precision)
 
 
-def _make_split_layer(conv: nn.Conv2d, *, clamp: bool) -> _Layer:
+def _make_split_layer(conv: nn.Conv2d, *, clamp: bool, precision: str = "bf16") -> _Layer:
     """A convolution to fp32 NCHW with more output channels than one MMA
-    takes (the 320-channel latent layer of FactorizedPrior(192, 320)): equal
-    parts of at most 256 channels, each its own launch on the same input,
-    writing its channel range of the shared output."""
+    takes (the 320-channel latent layer of FactorizedPrior(192, 320)): two
+    halves of 160 channels, each its own launch on the same input, writing
+    its channel range of the shared output.  FP8: both halves use the whole
+    weight's per-tensor scale, as one scaled GEMM would."""
     cout = conv.out_channels
-    nparts = (cout + 255) // 256
-    width = _round16((cout + nparts - 1) // nparts)
+    if cout != 320:
+        raise ConfigurationError("layers wider than 256 channels are built for the 320-channel latent "
+                                 "(two launches of 160 channels)")
+    width = cout // 2
+    fp8_scale = fp8_weight_scale(conv.weight) if precision == "fp8" else None
     parts = []
     for c0 in range(0, cout, width):
-        c1 = min(c0 + width, cout)
+        c1 = c0 + width
         sub = nn.Conv2d(conv.in_channels, c1 - c0, 5, 2, 2).to(conv.weight.device)
         with torch.no_grad():
             sub.weight.copy_(conv.weight[c0:c1])
             sub.bias.copy_(conv.bias[c0:c1])
-        part = _make_layer(sub, None, first=False, out_f32=True, clamp=clamp)
+        part = _make_layer(sub, None, first=False, out_f32=True, clamp=clamp, precision=precision,
+                           fp8_scale=fp8_scale)
         part.desc.out_channel_offset = c0
         part.desc.out_channels_total = cout
         parts.append(part)
-    return _Layer(None, (), FCAI_LAYER_CONV5S2, cout, parts[0].npad, FCAI_FMT_NCHW_F32, parts=tuple(parts))
+    return _Layer(None, (), FCAI_LAYER_CONV5S2, cout, parts[0].npad, FCAI_FMT_NCHW_F32, precision=precision,
+                  parts=tuple(parts))
 
 
 def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
@@ -337,7 +348,8 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
                                                  ctypes.c_void_p(scal.data_ptr() + 4), 1 if ready else 0,
                                                  cur.numel(), ctypes.c_void_p(stream)))
             _native.count_launches(1 if ready else 2)
-            layer.desc.act_scale = scal.data_ptr()
+            for target in layer.parts or (layer,):
+                target.desc.act_scale = scal.data_ptr()
         next_scal = None
         if layer.parts:
             for part in layer.parts:
@@ -502,9 +514,13 @@ def convert_factorized_prior(model: nn.Module, precision: str = "bf16",
 
     ``layer_precisions`` (module path -> "fp8" / "fp16" / "bf16" / "fp32",
     e.g. a loaded precision map) selects the e4m3 kernels per convolution
-    where they exist; the modules' ``precision_notes`` record what ran."""
-    if precision != "bf16":
+    where they exist; the modules' ``precision_notes`` record what ran.
+    ``precision="fp8"`` without a map requests e4m3 for every convolution
+    (those without an e4m3 kernel run bf16 and say why)."""
+    if precision not in ("bf16", "fp8"):
         raise ConfigurationError(f"unsupported transform precision {precision!r}")
+    if precision == "fp8" and layer_precisions is None:
+        layer_precisions = {f"{t}.{i}": "fp8" for t in ("g_a", "g_s") for i in (0, 2, 4, 6)}
     if not torch.cuda.is_available():
         raise ConfigurationError("B200 transforms require CUDA")
     dev = next(model.parameters()).device

@@ -67,9 +67,11 @@ enum { FCAI_ALGO_IMPLICIT_GEMM = 0, FCAI_ALGO_SCATTER = 1, FCAI_ALGO_IMPLICIT_GE
  * input is e4m3 NHWC (fcai_quantize_e4m3) with its scale at act_scale, the
  * weights are e4m3 packed like the bf16 TMA layers with scale weight_scale,
  * the accumulator is multiplied by act_scale * weight_scale before the bias
- * and epilogue.  TMA algorithm only, cin a multiple of 128; npad 128 (bf16
- * NHWC output, optionally GDN / IGDN, whose norm GEMM stays bf16) or npad
- * 192 without epilogue to fp32 NCHW (the latent layer). */
+ * and epilogue.  TMA algorithm only, cin a multiple of 64 (K runs in blocks
+ * of 128 channels; the part of the last block past cin reads as zeros);
+ * npad 128 (bf16 NHWC output, optionally GDN / IGDN, whose norm GEMM stays
+ * bf16), npad 192 with GDN / IGDN, or npad 192 / 160 without epilogue to
+ * fp32 NCHW (latent layers). */
 enum { FCAI_PREC_BF16 = 0, FCAI_PREC_FP8_E4M3 = 1 };
 
 typedef struct {

@@ -95,9 +95,20 @@ def test_fp8_kernel_coverage_rules():
     g_a, g_s = list(model.g_a), list(model.g_s)
     assert fp8_supported(g_a[0], g_a[1], first=True, out_f32=False) is not None  # cin = 3
     assert fp8_supported(g_a[2], g_a[3], first=False, out_f32=False) is None
-    assert fp8_supported(g_s[0], g_s[1], first=False, out_f32=False) is not None  # cin = 192
+    # cin = 192: two 128-channel K blocks, the second half zero-filled by TMA
+    assert fp8_supported(g_s[0], g_s[1], first=False, out_f32=False) is None
     assert fp8_supported(g_s[2], g_s[3], first=False, out_f32=False) is None
     assert fp8_supported(g_s[6], None, first=False, out_f32=True) is not None  # scatter layer
     assert fp8_supported(g_a[6], None, first=False, out_f32=True) is None
+    # FactorizedPrior(192, 320): 192-channel GDN / IGDN, the split 320-channel latent, g_s.0 (cin = 320)
+    big = FactorizedPrior(192, 320)
+    b_a, b_s = list(big.g_a), list(big.g_s)
+    assert fp8_supported(b_a[2], b_a[3], first=False, out_f32=False) is None
+    assert fp8_supported(b_a[6], None, first=False, out_f32=True) is None
+    assert fp8_supported(b_s[0], b_s[1], first=False, out_f32=False) is None
+    assert fp8_supported(b_s[4], b_s[5], first=False, out_f32=False) is None
+    assert fp8_supported(b_a[0], b_a[1], first=True, out_f32=False) is not None
+    odd = torch.nn.Conv2d(96, 128, 5, 2, 2)
+    assert "multiple of 64" in fp8_supported(odd, None, first=False, out_f32=False)
     with pytest.raises(Exception, match="unknown precision"):
         resolve_precisions("g_a", g_a, {"g_a.2": "int4"}, first_conv=0, last_f32=True)
