@@ -128,9 +128,13 @@ struct Layout {
     // pixels, one A box of 256 rows per K step, and each K step issues two
     // M = 128 MMAs that share the B tile, so each byte of weights loaded
     // feeds twice the MMA work.
-    // GDN over 192 channels: the accumulator and the norm (384 TMEM columns)
-    // leave room for one buffer, and the first layer one input window
+    // GDN over 192 channels.  TMA-fed layers (kXReg): 8 epilogue warps, two
+    // column halves of 96, each thread keeps its pixel's conv outputs in
+    // registers and the GDN GEMM writes the norm over them, so a buffer is
+    // 192 TMEM columns and two fit.  The first layer keeps x in TMEM beside
+    // the norm (384 columns, one buffer) and one input window.
     static constexpr bool kWide = kNorm && kNpad > 128;
+    static constexpr bool kXReg = kWide && !kGather;
     static constexpr bool kDual = kNorm && !kGather && !kPair && !kWide;
     static constexpr int kRows = kDual ? 2 * kBM : kBM;  // output pixels per tile
     static constexpr int kA = kGather ? kBM * kGatherK * 2 : kRows * kBK * 2;
@@ -189,7 +193,7 @@ struct Layout {
     // TMEM accumulator buffers: 2, or 4 for the scatter layer (128 columns
     // each), whose short tiles would otherwise make the MMA wait for the
     // epilogue of the tile before last
-    static constexpr int kAccBufs = kEpi == kEpiScatter ? 4 : (kWide ? 1 : 2);
+    static constexpr int kAccBufs = kEpi == kEpiScatter ? 4 : (kWide && !kXReg ? 1 : 2);
     static constexpr int kBars = 2 * kStages + 2 * kAccBufs + 4 + (kGather ? 4 : 0) + (kPair ? 1 : 0);
     static_assert(kStages >= 2, "operand ring");
     static constexpr int offSlot = offBar + kBars * 8;
@@ -200,7 +204,7 @@ struct Layout {
     // layer (fewer warps competing with the MMA warp for issue slots), two
     // (column halves) where the epilogue is the heavy part: the first layer
     // (K = 80) and the scatter layer.
-    static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter || kDual) ? 8 : 4;
+    static constexpr int kEpiWarps = (kGather || kEpi == kEpiScatter || kDual || kXReg) ? 8 : 4;
     static constexpr int kEpiThreads = kEpiWarps * 32;
     // column split between the two epilogue warps of a lane quarter
     static constexpr int kSplit = kEpiWarps == 8 && !kPingPong && kNpad >= 32 ? (kNpad / 2) / 16 * 16 : kNpad;
@@ -880,9 +884,43 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 named_barrier_sync(gbar, Lay::kGroupThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
                 // pass 1: x^2 (bf16) into the 128-byte-swizzled operand tile.
-                // 16-column chunks, the next chunk's TMEM load in flight while
-                // this one is converted and stored.
-                {
+                // kXReg: the thread's columns all load at once and stay in
+                // registers (the GDN GEMM then overwrites them in TMEM).
+                // Otherwise 16-column chunks, the next chunk's TMEM load in
+                // flight while this one is converted and stored.
+                uint32_t xv[Lay::kXReg ? kEpiChunks : 1][16];
+                if constexpr (Lay::kXReg) {
+#pragma unroll
+                    for (int k = 0; k < kEpiChunks; ++k) tmem_ld16(d1 + c_lo + k * 16, xv[k]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < kEpiChunks; ++k) tmem_regs_ready(xv[k]);
+                    if (kFp8) {  // x = (s_x s_w) * accumulator + bias
+#pragma unroll
+                        for (int k = 0; k < kEpiChunks; ++k)
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                xv[k][e] = __float_as_uint(fmaf(__uint_as_float(xv[k][e]), sc, s_bias[c_lo + k * 16 + e]));
+                    }
+#pragma unroll
+                    for (int k = 0; k < kEpiChunks; ++k) {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a = __uint_as_float(xv[k][q * 8 + 2 * e]);
+                                const float bb = __uint_as_float(xv[k][q * 8 + 2 * e + 1]);
+                                w[e] = pack_bf16x2(a * a, bb * bb);
+                            }
+                            const int k0 = c_lo + k * 16 + q * 8;
+                            const int kb = k0 / kBK, chunk = (k0 % kBK) / 8;
+                            st_shared_v4(x2 + kb * (kBM * 128) + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2],
+                                         w[3]);
+                        }
+                    }
+                    tc_fence_before();  // the TMEM loads above precede the GEMM that overwrites those columns
+                } else {
                     uint32_t v[2][16];
                     tmem_ld16(d1 + c_lo, v[0]);
 #pragma unroll
@@ -915,7 +953,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 named_barrier_sync(gbar, Lay::kGroupThreads);
                 if (gleader) {
                     const uint32_t g0 = smem_u32(smem + Lay::offG);
-                    const uint32_t d2 = tmem_base + buf * p.buf_stride + kNpad;
+                    // the norm: over x (kXReg) or in the columns beside it
+                    const uint32_t d2 = tmem_base + buf * p.buf_stride + (Lay::kXReg ? 0 : kNpad);
                     bool ok = true;
                     if (kPair) {
                         // norm = x^2 (each CTA its 128 rows) x gamma^T (each CTA half
@@ -962,21 +1001,23 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 if (!*g_ok) break;
                 tc_fence_after();
                 // pass 2: y = x * rsqrt(beta + norm)  (IGDN: x * sqrt(beta + norm)),
-                // pipelined like pass 1
+                // pipelined like pass 1 (kXReg: x from registers, the norm
+                // from the columns x was in)
                 __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
                                       (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
                 {
+                    constexpr uint32_t kNormCol = Lay::kXReg ? 0 : kNpad;
                     uint32_t v[2][16], nv[2][16];
-                    tmem_ld16(d1 + c_lo, v[0]);
-                    tmem_ld16(d1 + kNpad + c_lo, nv[0]);
+                    if (!Lay::kXReg) tmem_ld16(d1 + c_lo, v[0]);
+                    tmem_ld16(d1 + kNormCol + c_lo, nv[0]);
 #pragma unroll
                     for (int k = 0; k < kEpiChunks; ++k) {
                         tmem_wait_ld();
-                        tmem_regs_ready(v[k & 1]);
+                        if (!Lay::kXReg) tmem_regs_ready(v[k & 1]);
                         tmem_regs_ready(nv[k & 1]);
                         if (k + 1 < kEpiChunks) {
-                            tmem_ld16(d1 + c_lo + (k + 1) * 16, v[(k + 1) & 1]);
-                            tmem_ld16(d1 + kNpad + c_lo + (k + 1) * 16, nv[(k + 1) & 1]);
+                            if (!Lay::kXReg) tmem_ld16(d1 + c_lo + (k + 1) * 16, v[(k + 1) & 1]);
+                            tmem_ld16(d1 + kNormCol + c_lo + (k + 1) * 16, nv[(k + 1) & 1]);
                         }
                         const int c0 = c_lo + k * 16;
                         uint32_t o[8];
@@ -987,11 +1028,17 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             // GDN: x / sqrt(n); IGDN: x * sqrt(n)
                             const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
                             const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
-                            float x0 = __uint_as_float(v[k & 1][2 * e]);
-                            float x1 = __uint_as_float(v[k & 1][2 * e + 1]);
-                            if (kFp8) {
-                                x0 = fmaf(x0, sc, s_bias[c0 + 2 * e]);
-                                x1 = fmaf(x1, sc, s_bias[c0 + 2 * e + 1]);
+                            float x0, x1;
+                            if constexpr (Lay::kXReg) {  // scaled in pass 1
+                                x0 = __uint_as_float(xv[k][2 * e]);
+                                x1 = __uint_as_float(xv[k][2 * e + 1]);
+                            } else {
+                                x0 = __uint_as_float(v[k & 1][2 * e]);
+                                x1 = __uint_as_float(v[k & 1][2 * e + 1]);
+                                if (kFp8) {
+                                    x0 = fmaf(x0, sc, s_bias[c0 + 2 * e]);
+                                    x1 = fmaf(x1, sc, s_bias[c0 + 2 * e + 1]);
+                                }
                             }
                             o[e] = pack_bf16x2(x0 * r0, x1 * r1);
                             if (valid) am2 = amax_bf16x2(am2, o[e]);
@@ -1559,12 +1606,15 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     const int64_t tiles = (int64_t)batch * p.phases * p.tiles_x * p.tiles_y;
     if (tiles > INT32_MAX) return fcai::fail(FCAI_ERR_INVALID, "too many tiles");
     p.tiles_total = (int)tiles;
-    const int per_buf = npad + (norm ? npad : 0);
+    // GDN layers over 192 channels fed by TMA keep x in registers and write
+    // the norm over it (npad columns a buffer); other GDN layers hold both
+    const bool xreg = norm && npad > 128 && !gather;
+    const int per_buf = npad + (norm && !xreg ? npad : 0);
     uint32_t stride = 32;
     while (stride < (uint32_t)per_buf) stride <<= 1;
     p.buf_stride = stride;
     // the kernel's accumulator buffer count (Layout::kAccBufs)
-    p.tmem_cols = (scatter ? 4 : (norm && npad > 128 ? 1 : 2)) * stride;
+    p.tmem_cols = (scatter ? 4 : (norm && npad > 128 && gather ? 1 : 2)) * stride;
     if (p.tmem_cols > 512) return fcai::fail(FCAI_ERR_INVALID, "accumulators exceed tensor memory");
     if (scatter) {
         p.taps[0].n = 1;  // one K pass over the halo tile, all taps are GEMM columns
