@@ -934,9 +934,22 @@ __device__ __forceinline__ void decode_chunk(const DecParams &p, const Tab &tab,
     if (start64 >= p.N) return;
     const int start = (int)start64;
     const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
+    // the chunk's word offset: from the prep kernel's scan, or (payloads
+    // the host has validated, few chunks) summed here by the whole warp over
+    // the rounds of the chunks before it
+    uint64_t off;
+    if (p.offsets) {
+        off = p.offsets[chunk];
+    } else {
+        uint64_t sum = 0;
+        for (int64_t c = lane; c < chunk; c += kLanes) sum += (uint64_t)__ldg(p.max_rounds + c);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        off = sum * kLanes;
+    }
     const int first = start + lane;
     if (first >= end) return;
-    LaneReader rd{body + p.offsets[chunk] + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    LaneReader rd{body + off + lane, 0, (int)p.max_rounds[chunk], false, 0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
     rd.start();
     uint64_t x = (uint64_t)rd.next();
     x |= (uint64_t)rd.next() << 32;
@@ -1462,6 +1475,10 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     return FCAI_OK;
 }
 
+// Unchecked decodes up to this many chunks sum their offsets in the decode
+// kernel (at most 64 loads per lane) instead of launching the prep kernel.
+constexpr int64_t kInlineOffsetChunks = 2048;
+
 // Shared body of the decode entry points.
 static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, const uint32_t *max_rounds, int32_t K,
                        int64_t header_bytes, int32_t chunk_len, const int32_t *indexes, int32_t B, int32_t N,
@@ -1491,9 +1508,15 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     Control *ctrl = reinterpret_cast<Control *>(ws);
     unsigned long long *offs = reinterpret_cast<unsigned long long *>(ws + dl.offsets);
 
-    DecPrepParams pp{packed, max_rounds, chunks, B, N, K, chunk_len, header_bytes, packed_bytes, ctrl, offs};
-    decode_prep_kernel<<<1, 1024, 0, stream>>>(pp);
-    FCAI_CUDA_TRY(cudaGetLastError());
+    // Unchecked decodes of few chunks (payloads whose header the caller has
+    // validated on the host) need no prep launch: each warp sums its chunk's
+    // offset itself.  Otherwise the prep kernel checks the header and scans.
+    const bool prep = check || chunks > kInlineOffsetChunks;
+    if (prep) {
+        DecPrepParams pp{packed, max_rounds, chunks, B, N, K, chunk_len, header_bytes, packed_bytes, ctrl, offs};
+        decode_prep_kernel<<<1, 1024, 0, stream>>>(pp);
+        FCAI_CUDA_TRY(cudaGetLastError());
+    }
 
     DecParams p;
     p.packed = packed;
@@ -1510,7 +1533,7 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     p.HW = N / C;
     p.chunks = chunks;
     p.ctrl = ctrl;
-    p.offsets = offs;
+    p.offsets = prep ? offs : nullptr;
     p.out = symbols_out;
     const int HW = N / C;
     if (mode == kModeIdx || chunk_len % HW != 0) {

@@ -10,6 +10,8 @@ import ctypes
 import threading
 from pathlib import Path
 
+import torch
+
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libfcai_b200.so"
 
 # status codes of include/fcai_warp_div.h
@@ -112,6 +114,43 @@ LAUNCHES = {"kernels": 0}
 
 def count_launches(n: int) -> None:
     LAUNCHES["kernels"] += n
+
+
+# Unchecked decodes of at most this many chunks run without the prep kernel
+# (kInlineOffsetChunks in warp_div.cu).
+INLINE_OFFSET_CHUNKS = 2048
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def stream_handle(device: torch.device) -> int:
+    """The handle of ``device``'s current CUDA stream.  Uses torch's raw
+    query where it exists: ``torch.cuda.current_stream(device)`` builds a
+    Stream object and costs microseconds on a path that issues launches."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _Nothing:
+    __slots__ = ()
+
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NOTHING = _Nothing()
+
+
+def on_device(device: torch.device):
+    """``torch.cuda.device(device)``, or a no-op context when ``device`` is
+    already the current one (the common case, and a cheaper one)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NOTHING
+    return torch.cuda.device(device)
 
 
 def available() -> bool:

@@ -32,7 +32,8 @@ _MAX_SYMBOL_WORDS = 10
 
 
 def _ptr(t: torch.Tensor | None):
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    # the native functions declare their argtypes, so an int address passes
+    return None if t is None else t.data_ptr()
 
 
 def workspace(kind: str, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -91,8 +92,8 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
     """Workspace sizing, the encode call (retried once with the exact staging
     need if the first workspace was short), payload allocation and pack."""
     lib = _native.lib()
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
+    with _native.on_device(dev):
+        stream = _native.stream_handle(dev)
         plan = _plan(B, N, C, int(P))
         K = plan.chunks
         chunks = B * K
@@ -106,7 +107,7 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
         info = _native.WarpDivEncodeInfo()
         for attempt in range(2):
             ws = workspace("encode", dev, stream, nbytes)
-            rc = call(lib, ws, max_rounds, info, ctypes.c_void_p(stream))
+            rc = call(lib, ws, max_rounds, info, stream)
             _native.count_launches(1)
             if rc == _native.FCAI_ERR_WORKSPACE and attempt == 0 and info.required_workspace_bytes > ws.numel():
                 nbytes = info.required_workspace_bytes
@@ -115,7 +116,7 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
             break
         packed = torch.empty(int(info.packed_bytes), dtype=torch.uint8, device=dev)
         _native.check(lib.fcai_warp_div_encode_pack(_ptr(ws), ws.numel(), B, N, C, int(P), _ptr(packed),
-                                                    packed.numel(), ctypes.c_void_p(stream)))
+                                                    packed.numel(), stream))
         _native.count_launches(1)
     return EncodeResult(packed, max_rounds, int(info.header_bytes), int(info.chunk_len), int(info.p_ch),
                         bool(info.index_layout_is_channel))
@@ -199,16 +200,18 @@ def decode_latent(packed: torch.Tensor, max_rounds: torch.Tensor, header_bytes: 
         raise RuntimeError("max_rounds dim0 mismatch")
     K = int(max_rounds.shape[1])
     dev = out.device
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
+    with _native.on_device(dev):
+        stream = _native.stream_handle(dev)
         nbytes = 256 + ((B * K * 8 + 255) // 256) * 256
         ws = workspace("decode", dev, stream, nbytes)
         rc = _native.lib().fcai_warp_div_decode_latent(
             _ptr(packed), packed.numel(), _ptr(max_rounds), K, int(header_bytes), int(chunk_len), B, N, _ptr(cdfs),
             C, L, _ptr(cdf_sizes), _ptr(offsets), _ptr(medians), _ptr(out), _ptr(ws), ws.numel(), 1 if check else 0,
-            ctypes.c_void_p(stream))
-        _native.count_launches(2)
-        _native.check(rc)
+            stream)
+        # the prep kernel runs for checked decodes and for many chunks
+        _native.count_launches(2 if check or B * K > _native.INLINE_OFFSET_CHUNKS else 1)
+        if rc:
+            _native.check(rc)
     return out
 
 

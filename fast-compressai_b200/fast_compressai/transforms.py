@@ -157,6 +157,11 @@ class _Layer:
     # a layer wider than one MMA (cout > 256, fp32 NCHW output) runs as parts
     # that read the same input and write disjoint channel ranges
     parts: tuple = ()
+    ref: object = None  # ctypes reference to desc, made once
+
+    def __post_init__(self) -> None:
+        if self.desc is not None:
+            self.ref = ctypes.byref(self.desc)
 
     def flops(self, batch: int, h_in: int, w_in: int) -> float:
         """Algorithmic FLOPs: 2 * cin * 25 * cout per output (conv) or input
@@ -312,8 +317,13 @@ def _make_split_layer(conv: nn.Conv2d, *, clamp: bool, precision: str = "bf16") 
 
 
 def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
+    # The host issues these launches while the GPU runs the previous ones;
+    # plain ints go to the native calls (their argtypes are declared).
     lib = _native.lib()
-    stream = torch.cuda.current_stream(x.device).cuda_stream
+    forward = lib.fcai_layer_forward
+    dev = x.device
+    stream = _native.stream_handle(dev)
+    launches = 0
     B = x.shape[0]
     if first_is_nchw:
         h, w = x.shape[2], x.shape[3]
@@ -328,9 +338,9 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
         feeds_fp8 = (nxt is not None and nxt.precision == "fp8" and layer.out_format == FCAI_FMT_NHWC_BF16
                      and not layer.parts and layer.desc.algorithm != FCAI_ALGO_SCATTER)
         if layer.out_format == FCAI_FMT_NHWC_BF16:
-            out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=x.device)
+            out = torch.empty((B, ho, wo, layer.npad), dtype=torch.bfloat16, device=dev)
         else:
-            out = torch.empty((B, layer.cout, ho, wo), dtype=torch.float32, device=x.device)
+            out = torch.empty((B, layer.cout, ho, wo), dtype=torch.float32, device=dev)
         timing = LAYER_TIMING
         if timing is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -339,39 +349,43 @@ def _run(layers, x: torch.Tensor, first_is_nchw: bool) -> torch.Tensor:
         if layer.precision == "fp8":
             # the input's per-tensor e4m3 copy and its scale (amax / 448); the
             # amax came with the input when the previous layer produced it
-            src = torch.empty(cur.shape, dtype=torch.uint8, device=x.device)
+            src = torch.empty(cur.shape, dtype=torch.uint8, device=dev)
             ready = scal is not None
             if not ready:
-                scal = torch.zeros(2, dtype=torch.float32, device=x.device)
-            _native.check(lib.fcai_quantize_e4m3(ctypes.c_void_p(cur.data_ptr()), ctypes.c_void_p(src.data_ptr()),
-                                                 ctypes.c_void_p(scal.data_ptr()),
-                                                 ctypes.c_void_p(scal.data_ptr() + 4), 1 if ready else 0,
-                                                 cur.numel(), ctypes.c_void_p(stream)))
-            _native.count_launches(1 if ready else 2)
+                scal = torch.zeros(2, dtype=torch.float32, device=dev)
+            _native.check(lib.fcai_quantize_e4m3(cur.data_ptr(), src.data_ptr(), scal.data_ptr(), scal.data_ptr() + 4,
+                                                 1 if ready else 0, cur.numel(), stream))
+            launches += 1 if ready else 2
             for target in layer.parts or (layer,):
                 target.desc.act_scale = scal.data_ptr()
         next_scal = None
         if layer.parts:
             for part in layer.parts:
-                _native.check(lib.fcai_layer_forward(ctypes.byref(part.desc), B, h, w, ctypes.c_void_p(src.data_ptr()),
-                                                     ctypes.c_void_p(out.data_ptr()), None, ctypes.c_void_p(stream)))
-                _native.count_launches(1)
-        else:
-            if feeds_fp8:
-                next_scal = torch.zeros(2, dtype=torch.float32, device=x.device)
-                layer.desc.amax_out = next_scal.data_ptr() + 4
+                rc = forward(part.ref, B, h, w, src.data_ptr(), out.data_ptr(), None, stream)
+                if rc:
+                    _native.check(rc)
+                launches += 1
+        elif feeds_fp8:
+            next_scal = torch.zeros(2, dtype=torch.float32, device=dev)
+            layer.desc.amax_out = next_scal.data_ptr() + 4
             try:
-                _native.check(lib.fcai_layer_forward(ctypes.byref(layer.desc), B, h, w,
-                                                     ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                                                     None, ctypes.c_void_p(stream)))
+                rc = forward(layer.ref, B, h, w, src.data_ptr(), out.data_ptr(), None, stream)
             finally:
                 layer.desc.amax_out = None  # the buffer is this call's
-            _native.count_launches(1)
+            if rc:
+                _native.check(rc)
+            launches += 1
+        else:
+            rc = forward(layer.ref, B, h, w, src.data_ptr(), out.data_ptr(), None, stream)
+            if rc:
+                _native.check(rc)
+            launches += 1
         scal = next_scal
         if timing is not None:
             ev1.record()
             timing.append((layer.name, layer.flops(B, h, w), ev0, ev1))
         cur, h, w = out, ho, wo
+    _native.count_launches(launches)
     return cur
 
 
@@ -381,8 +395,21 @@ class _Packed(nn.Sequential):
     from them; the packs are rebuilt if a parameter is modified in place."""
 
     def _signature(self):
-        # inference tensors have no version counter (and cannot change in place)
-        return tuple((id(t), -1 if t.is_inference() else t._version) for t in self.parameters())
+        # The children, and each parameter's identity and version counter
+        # (inference tensors have none, and cannot change in place).  The
+        # parameters are read from the dicts of the modules that own them,
+        # collected again whenever a child is replaced: a walk through
+        # parameters() on every call costs more than a layer launch.
+        children = tuple(id(m) for m in self._modules.values())
+        if getattr(self, "_owner_key", None) != children:
+            self._owners = [m for m in self.modules() if m._parameters]
+            self._owner_key = children
+        sig = [children]
+        for owner in self._owners:
+            for t in owner._parameters.values():
+                if t is not None:
+                    sig.append((id(t), -1 if t.is_inference() else t._version))
+        return tuple(sig)
 
     def _refresh_if_stale(self) -> None:
         if self._sig != self._signature():
@@ -457,7 +484,7 @@ class B200Analysis(_Packed):
             raise ValueError("B200Analysis expects a CUDA [B, 3, H, W] tensor")
         self._refresh_if_stale()
         x = x.float().contiguous()
-        with torch.cuda.device(x.device):
+        with _native.on_device(x.device):
             return _run(self._layers, x, first_is_nchw=True)
 
 
@@ -499,11 +526,10 @@ class B200Synthesis(_Packed):
         self._refresh_if_stale()
         y = y.float().contiguous()
         B, C, h, w = y.shape
-        with torch.cuda.device(y.device):
+        with _native.on_device(y.device):
             nhwc = torch.empty((B, h, w, C), dtype=torch.bfloat16, device=y.device)
-            stream = torch.cuda.current_stream(y.device).cuda_stream
-            _native.check(_native.lib().fcai_nchw_f32_to_nhwc_bf16(
-                ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(nhwc.data_ptr()), B, C, h, w, ctypes.c_void_p(stream)))
+            stream = _native.stream_handle(y.device)
+            _native.check(_native.lib().fcai_nchw_f32_to_nhwc_bf16(y.data_ptr(), nhwc.data_ptr(), B, C, h, w, stream))
             _native.count_launches(1)
             return _run(self._layers + [self._last_clamped if clamp else self._last], nhwc, first_is_nchw=False)
 
