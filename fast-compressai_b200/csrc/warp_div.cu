@@ -1116,9 +1116,14 @@ static bool g_magic_ready[64];
 // host waits for the stream only.  A cudaMemcpy of those few bytes would be
 // queued on a copy engine behind whatever bulk transfers other streams have
 // issued (a batch's upload or download), and the host would wait for those.
+// Two slots: [0, 8) for the synchronous read-backs, [8, 16) for the status
+// of a submitted encode (fcai_warp_div_encode_latent_submit), which the host
+// collects later in fcai_warp_div_encode_finish by waiting on `done` alone.
 struct MappedStatus {
     volatile long long *host;
     long long *dev;
+    cudaEvent_t done;
+    int *pending;  // a submitted encode awaits its finish (shared flag)
 };
 static std::mutex g_status_mutex;
 static std::unordered_map<uint64_t, MappedStatus> g_status;
@@ -1139,12 +1144,17 @@ static int mapped_status(cudaStream_t stream, MappedStatus *out) {
     }
     void *h = nullptr;
     void *d = nullptr;
-    FCAI_CUDA_TRY(cudaHostAlloc(&h, 64, cudaHostAllocMapped | cudaHostAllocPortable));
+    FCAI_CUDA_TRY(cudaHostAlloc(&h, 128, cudaHostAllocMapped | cudaHostAllocPortable));
     if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess || !d) {
         cudaFreeHost(h);
         return fcai::fail(FCAI_ERR_CUDA, "mapped status buffer has no device address");
     }
-    MappedStatus m{static_cast<volatile long long *>(h), static_cast<long long *>(d)};
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+        cudaFreeHost(h);
+        return fcai::fail(FCAI_ERR_CUDA, "status event creation failed");
+    }
+    MappedStatus m{static_cast<volatile long long *>(h), static_cast<long long *>(d), ev, new int(0)};
     g_status.emplace(key, m);
     *out = m;
     return FCAI_OK;
@@ -1400,23 +1410,48 @@ static int encode_scratch(void **out) {
 }
 
 // Shared body of the encode entry points.
+// The encode's size and status from its status words (kSt* slots).
+static int encode_info_from_status(const Dims &d, const EncLayout &el, const long long *status,
+                                   int64_t workspace_bytes, fcai_warp_div_encode_info *info) {
+    const long long flags = status[kStFlags];
+    info->header_bytes = d.header_bytes;
+    info->chunk_len = d.chunk_len;
+    info->p_ch = d.P;
+    info->index_layout_is_channel = (flags & kFlagNonChannel) ? 0 : 1;
+    info->packed_bytes = d.header_bytes + 4 * (int64_t)status[kStTotalWords];
+    info->required_workspace_bytes = el.fixed_bytes + d.chunks * (int64_t)status[kStMaxUsed] * kLanes * 4;
+    if (int rc = flags_to_status(flags, true)) return rc;
+    if (flags & kFlagOverflow)
+        return fcai::fail(FCAI_ERR_WORKSPACE, "encode staging needs %lld workspace bytes, %lld given",
+                          (long long)info->required_workspace_bytes, (long long)workspace_bytes);
+    return FCAI_OK;
+}
+
+// submit: enqueue the encode and the copy of its status words to the mapped
+// buffer's second slot, record the stream's status event and return at once
+// (info untouched); fcai_warp_div_encode_finish collects the status.
 static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes, const float *y,
                        const float *medians, int32_t B, int32_t N, const int32_t *cdfs, int32_t C, int32_t L,
                        const int32_t *cdf_sizes, const int32_t *offsets, int32_t P, void *workspace,
                        int64_t workspace_bytes, uint32_t *max_rounds, fcai_warp_div_encode_info *info,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, bool submit = false) {
     Dims d;
     int rc = make_dims(B, N, C, P, d);
     if (rc) return rc;
     if ((rc = check_tables_args(cdfs, C, L, cdf_sizes, offsets))) return rc;
-    if (!workspace || !max_rounds || !info) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    if (!workspace || !max_rounds || (!info && !submit)) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    MappedStatus ms{};
+    if ((rc = mapped_status(stream, &ms))) return rc;
+    if (*ms.pending)
+        return fcai::fail(FCAI_ERR_INVALID,
+                          "an encode submitted on this stream awaits fcai_warp_div_encode_finish");
     if (mode == kModeLatent ? (!y || !medians) : !symbols) return fcai::fail(FCAI_ERR_INVALID, "null input");
     EncLayout el = enc_layout(d.chunks);
     int64_t avail = workspace_bytes - el.fixed_bytes;
     int64_t rows_cap = avail > 0 ? avail / (d.chunks * kLanes * 4) : 0;
     if (rows_cap > rows_worst(d)) rows_cap = rows_worst(d);
     if (rows_cap < 2) {
-        info->required_workspace_bytes = el.fixed_bytes + d.chunks * rows_worst(d) * kLanes * 4;
+        if (info) info->required_workspace_bytes = el.fixed_bytes + d.chunks * rows_worst(d) * kLanes * 4;
         return fcai::fail(FCAI_ERR_WORKSPACE, "encode workspace of %lld bytes is too small",
                           (long long)workspace_bytes);
     }
@@ -1458,21 +1493,16 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
                     : launch_encode_group<kModeLatent, false>(p, smem, stream);
     }
     if (rc) return rc;
+    if (submit) {
+        status_to_host_kernel<<<1, 32, 0, stream>>>(p.ctrl->status, ms.dev + 8, 8);
+        FCAI_CUDA_TRY(cudaGetLastError());
+        FCAI_CUDA_TRY(cudaEventRecord(ms.done, stream));
+        *ms.pending = 1;
+        return FCAI_OK;
+    }
     long long status[8];
     if ((rc = read_status(p.ctrl->status, 8, stream, status))) return rc;
-
-    const long long flags = status[kStFlags];
-    info->header_bytes = d.header_bytes;
-    info->chunk_len = d.chunk_len;
-    info->p_ch = d.P;
-    info->index_layout_is_channel = (flags & kFlagNonChannel) ? 0 : 1;
-    info->packed_bytes = d.header_bytes + 4 * (int64_t)status[kStTotalWords];
-    info->required_workspace_bytes = el.fixed_bytes + d.chunks * (int64_t)status[kStMaxUsed] * kLanes * 4;
-    if ((rc = flags_to_status(flags, true))) return rc;
-    if (flags & kFlagOverflow)
-        return fcai::fail(FCAI_ERR_WORKSPACE, "encode staging needs %lld workspace bytes, %lld given",
-                          (long long)info->required_workspace_bytes, (long long)workspace_bytes);
-    return FCAI_OK;
+    return encode_info_from_status(d, el, status, workspace_bytes, info);
 }
 
 // Unchecked decodes up to this many chunks sum their offsets in the decode
@@ -1609,6 +1639,34 @@ int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B,
     fcai::clear_error();
     return encode_impl(kModeLatent, nullptr, nullptr, y, medians, B, N, cdfs, C, L, cdf_sizes, offsets, P, workspace,
                        workspace_bytes, max_rounds, info, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fcai_warp_div_encode_latent_submit(const float *y, const float *medians, int32_t B, int32_t N,
+                                       const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                                       const int32_t *offsets, int32_t P, void *workspace, int64_t workspace_bytes,
+                                       uint32_t *max_rounds, fcai_stream_t stream) {
+    fcai::clear_error();
+    return encode_impl(kModeLatent, nullptr, nullptr, y, medians, B, N, cdfs, C, L, cdf_sizes, offsets, P, workspace,
+                       workspace_bytes, max_rounds, nullptr, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int fcai_warp_div_encode_finish(int32_t B, int32_t N, int32_t C, int32_t P, int64_t workspace_bytes,
+                                fcai_warp_div_encode_info *info, fcai_stream_t stream_) {
+    fcai::clear_error();
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    Dims d;
+    int rc = make_dims(B, N, C, P, d);
+    if (rc) return rc;
+    if (!info) return fcai::fail(FCAI_ERR_INVALID, "null argument");
+    MappedStatus ms{};
+    if ((rc = mapped_status(stream, &ms))) return rc;
+    if (!*ms.pending) return fcai::fail(FCAI_ERR_INVALID, "no encode was submitted on this stream");
+    *ms.pending = 0;
+    // the submitted encode's status words, not the work enqueued after them
+    FCAI_CUDA_TRY(cudaEventSynchronize(ms.done));
+    long long status[8];
+    for (int i = 0; i < 8; ++i) status[i] = ms.host[8 + i];
+    return encode_info_from_status(d, enc_layout(d.chunks), status, workspace_bytes, info);
 }
 
 int fcai_warp_div_encode_pack(const void *workspace, int64_t workspace_bytes, int32_t B, int32_t N, int32_t C,

@@ -87,6 +87,14 @@ SIGNATURES: dict[str, tuple] = {
         ctypes.c_int,
         [_P, _P, _I32, _I32, _P, _I32, _I32, _P, _P, _I32, _P, _I64, _P, ctypes.POINTER(WarpDivEncodeInfo), _P],
     ),
+    "fcai_warp_div_encode_latent_submit": (
+        ctypes.c_int,
+        [_P, _P, _I32, _I32, _P, _I32, _I32, _P, _P, _I32, _P, _I64, _P, _P],
+    ),
+    "fcai_warp_div_encode_finish": (
+        ctypes.c_int,
+        [_I32, _I32, _I32, _I32, _I64, ctypes.POINTER(WarpDivEncodeInfo), _P],
+    ),
     "fcai_warp_div_decode_latent": (
         ctypes.c_int,
         [_P, _I64, _P, _I32, _I64, _I32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _I64, _I32, _P],

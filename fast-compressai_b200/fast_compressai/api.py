@@ -296,6 +296,12 @@ class FastModel(nn.Module):
             return coder.decompress(*args, **kwargs)
         return self.model.decompress(*args, **kwargs)
 
+    def compress_async(self, x) -> Any:
+        """Enqueue compress() and return a handle whose result() waits for
+        the payload size alone (warp_div coder only): the overlap of
+        execution_mode="overlap", see FactorizedWarpDivCodec.compress_async."""
+        return self._host_coder("compress_async").compress_async(x)
+
     def upload_host(self, x, **kwargs: Any) -> Any:
         """Start the upload of a host batch and return a handle for compress() (warp_div coder only)."""
         return self._host_coder("upload_host").upload_host(x, **kwargs)

@@ -88,38 +88,106 @@ def _check_encode_inputs(symbols, indexes, cdfs, cdf_sizes, offsets) -> None:
         raise RuntimeError("CDF metadata length mismatch")
 
 
+def _encode_sizes(B: int, N: int, C: int, P: int) -> tuple[int, int]:
+    """(K, first workspace size): one staged word per symbol per lane covers
+    any practical table; an encode that needs more reports the exact size."""
+    plan = _plan(B, N, C, int(P))
+    K = plan.chunks
+    chunks = B * K
+    lane_symbols = (plan.chunk_len + _LANES - 1) // _LANES
+    rows_worst = _MAX_SYMBOL_WORDS * lane_symbols + 2
+    fixed = plan.encode_workspace_bytes - chunks * rows_worst * _LANES * 4
+    return K, fixed + chunks * min(rows_worst, lane_symbols + 4) * _LANES * 4
+
+
+def _pack(B: int, N: int, C: int, P: int, ws: torch.Tensor, max_rounds: torch.Tensor, info, stream: int,
+          dev: torch.device) -> EncodeResult:
+    packed = torch.empty(int(info.packed_bytes), dtype=torch.uint8, device=dev)
+    _native.check(_native.lib().fcai_warp_div_encode_pack(_ptr(ws), ws.numel(), B, N, C, int(P), _ptr(packed),
+                                                          packed.numel(), stream))
+    _native.count_launches(1)
+    return EncodeResult(packed, max_rounds, int(info.header_bytes), int(info.chunk_len), int(info.p_ch),
+                        bool(info.index_layout_is_channel))
+
+
 def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> EncodeResult:
     """Workspace sizing, the encode call (retried once with the exact staging
     need if the first workspace was short), payload allocation and pack."""
     lib = _native.lib()
     with _native.on_device(dev):
         stream = _native.stream_handle(dev)
-        plan = _plan(B, N, C, int(P))
-        K = plan.chunks
-        chunks = B * K
-        lane_symbols = (plan.chunk_len + _LANES - 1) // _LANES
-        rows_worst = _MAX_SYMBOL_WORDS * lane_symbols + 2
-        fixed = plan.encode_workspace_bytes - chunks * rows_worst * _LANES * 4
-        # one staged word per symbol per lane covers any practical table; the
-        # call reports the exact need otherwise and is repeated once
-        nbytes = fixed + chunks * min(rows_worst, lane_symbols + 4) * _LANES * 4
+        K, nbytes = _encode_sizes(B, N, C, P)
         max_rounds = torch.empty((B, K), dtype=torch.uint32, device=dev)
         info = _native.WarpDivEncodeInfo()
         for attempt in range(2):
             ws = workspace("encode", dev, stream, nbytes)
             rc = call(lib, ws, max_rounds, info, stream)
-            _native.count_launches(1)
+            _native.count_launches(2)  # the encode and the copy of its status words
             if rc == _native.FCAI_ERR_WORKSPACE and attempt == 0 and info.required_workspace_bytes > ws.numel():
                 nbytes = info.required_workspace_bytes
                 continue
             _native.check(rc)
             break
-        packed = torch.empty(int(info.packed_bytes), dtype=torch.uint8, device=dev)
-        _native.check(lib.fcai_warp_div_encode_pack(_ptr(ws), ws.numel(), B, N, C, int(P), _ptr(packed),
-                                                    packed.numel(), stream))
-        _native.count_launches(1)
-    return EncodeResult(packed, max_rounds, int(info.header_bytes), int(info.chunk_len), int(info.p_ch),
-                        bool(info.index_layout_is_channel))
+        return _pack(B, N, C, P, ws, max_rounds, info, stream, dev)
+
+
+@dataclass
+class PendingEncode:
+    """An encode enqueued by encode_latent_submit, awaiting encode_finish."""
+    B: int
+    N: int
+    C: int
+    P: int
+    dev: torch.device
+    stream: int
+    ws: torch.Tensor
+    max_rounds: torch.Tensor
+    inputs: tuple  # (y, medians, cdfs, cdf_sizes, offsets): kept until the finish
+    done: bool = False
+
+
+def encode_latent_submit(y: torch.Tensor, medians: torch.Tensor, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,
+                         offsets: torch.Tensor, P: int) -> PendingEncode:
+    """Enqueue encode_latent's work on the current stream and return at once;
+    encode_finish returns its EncodeResult.  The caller may enqueue other
+    work on the stream in between (not another encode)."""
+    _check_latent(y, medians, cdfs, cdf_sizes, offsets)
+    B = int(y.shape[0])
+    N = int(y.numel() // max(B, 1))
+    C, L = (int(v) for v in cdfs.shape)
+    if B <= 0 or N <= 0 or y.shape[1] != C:
+        raise RuntimeError("latent channels must equal the CDF count")
+    dev = y.device
+    with _native.on_device(dev):
+        stream = _native.stream_handle(dev)
+        K, nbytes = _encode_sizes(B, N, C, P)
+        max_rounds = torch.empty((B, K), dtype=torch.uint32, device=dev)
+        ws = workspace("encode", dev, stream, nbytes)
+        rc = _native.lib().fcai_warp_div_encode_latent_submit(
+            _ptr(y), _ptr(medians), B, N, _ptr(cdfs), C, L, _ptr(cdf_sizes), _ptr(offsets), int(P), _ptr(ws),
+            ws.numel(), _ptr(max_rounds), stream)
+        if rc:
+            _native.check(rc)
+        _native.count_launches(2)
+    return PendingEncode(B, N, C, int(P), dev, stream, ws, max_rounds, (y, medians, cdfs, cdf_sizes, offsets))
+
+
+def encode_finish(pending: PendingEncode) -> EncodeResult:
+    """Wait for a submitted encode (only), then allocate and pack its payload
+    on the stream it was submitted on.  A staging overflow repeats the encode
+    synchronously with the workspace it needs."""
+    if pending.done:
+        raise RuntimeError("this encode was already finished")
+    pending.done = True
+    p = pending
+    with _native.on_device(p.dev):
+        info = _native.WarpDivEncodeInfo()
+        rc = _native.lib().fcai_warp_div_encode_finish(p.B, p.N, p.C, p.P, p.ws.numel(), ctypes.byref(info), p.stream)
+        if rc == _native.FCAI_ERR_WORKSPACE:
+            with torch.cuda.stream(torch.cuda.ExternalStream(p.stream, device=p.dev)):
+                return encode_latent(*p.inputs, p.P)
+        _native.check(rc)
+        return _pack(p.B, p.N, p.C, p.P, p.ws, p.max_rounds, info, p.stream, p.dev)
 
 
 def encode(symbols: torch.Tensor, indexes: torch.Tensor | None, cdfs: torch.Tensor, cdf_sizes: torch.Tensor,

@@ -39,6 +39,28 @@ def _copy_stream(device: torch.device, compute: torch.cuda.Stream, direction: st
     return stream
 
 
+class PendingCompress:
+    """A compress whose device work is enqueued (``compress_async``)."""
+
+    __slots__ = ("_codec", "_pending", "_shape", "_result")
+
+    def __init__(self, codec, pending, shape) -> None:
+        self._codec = codec
+        self._pending = pending
+        self._shape = shape
+        self._result = None
+
+    def result(self) -> dict:
+        """Wait for the encode, pack the payload and return
+        ``{"strings": [payload], "shape": (h, w)}`` (once; later calls
+        return the same dict)."""
+        if self._result is None:
+            payload = self._codec.backend._encode_latent_finish(self._pending)
+            self._result = {"strings": [payload], "shape": self._shape}
+            self._pending = None
+        return self._result
+
+
 @dataclass(frozen=True)
 class HostUpload:
     """A host batch being copied to the device (``upload_host``).
@@ -120,6 +142,34 @@ class FactorizedWarpDivCodec:
                 end.synchronize()
                 timing["compress_codec_ms"] = float(start.elapsed_time(end))
             return {"strings": [payload], "shape": tuple(y.shape[-2:])}
+
+    def compress_async(self, x: torch.Tensor | HostUpload) -> "PendingCompress":
+        """``compress`` in two halves, for overlapped batches (the
+        reference's ``execution_mode="overlap"``, accepted there but not
+        implemented).  This enqueues g_a and the encode on the current stream
+        and returns at once; ``result()`` waits for the encode alone (not for
+        work enqueued after it), packs the payload and returns what
+        ``compress`` returns.  In between, the caller can enqueue the next
+        batch's or an earlier batch's work, so that the device stays busy
+        while the host learns the payload size.  One pending compress per
+        stream at a time."""
+        if isinstance(x, HostUpload):
+            compute = torch.cuda.current_stream(x.tensor.device)
+            compute.wait_event(x.ready)
+            x.tensor.record_stream(compute)
+            x = x.tensor
+        if not isinstance(x, torch.Tensor) or x.device.type != "cuda" or x.ndim != 4:
+            raise CoderInputError("warp_div FactorizedPrior.compress expects a CUDA NCHW tensor")
+        with torch.no_grad():
+            y = self.model.g_a(x)
+            entropy = self.model.entropy_bottleneck
+            if y.size(1) != entropy.channels:
+                raise CoderInputError("latent channel count does not match entropy bottleneck")
+            cdfs, lengths, offsets = self._tables(entropy)
+            y = y.float().contiguous()
+            medians = self._medians(entropy)
+            pending = self.backend._encode_latent_submit(y, medians, cdfs, lengths, offsets, self.p_ch)
+        return PendingCompress(self, pending, tuple(y.shape[-2:]))
 
     def _device(self) -> torch.device:
         return self.model.entropy_bottleneck._quantized_cdf.device

@@ -450,6 +450,26 @@ class WarpDivBackend:
             r = self._extension.encode_latent(y, medians, cdfs, cdf_sizes, offsets, int(p_ch))
         except (_native.NativeCallError, RuntimeError) as exc:
             _raise_coder_error(exc, "encode")
+        return self._latent_payload(r, y, cdfs, cdf_sizes, offsets)
+
+    def _encode_latent_submit(self, y: torch.Tensor, medians: torch.Tensor, cdfs, cdf_sizes, offsets, p_ch: int):
+        """``_encode_latent`` in two halves: this enqueues the encode and
+        returns at once; ``_encode_latent_finish`` waits for it alone and
+        returns the payload."""
+        try:
+            return self._extension.encode_latent_submit(y, medians, cdfs, cdf_sizes, offsets, int(p_ch))
+        except (_native.NativeCallError, RuntimeError) as exc:
+            _raise_coder_error(exc, "encode")
+
+    def _encode_latent_finish(self, pending) -> WarpDivPayload:
+        try:
+            r = self._extension.encode_finish(pending)
+        except (_native.NativeCallError, RuntimeError) as exc:
+            _raise_coder_error(exc, "encode")
+        y, _, cdfs, cdf_sizes, offsets = pending.inputs
+        return self._latent_payload(r, y, cdfs, cdf_sizes, offsets)
+
+    def _latent_payload(self, r, y: torch.Tensor, cdfs, cdf_sizes, offsets) -> WarpDivPayload:
         B = int(y.shape[0])
         N = int(y.numel() // B)
         _remember_rounds(r.max_rounds, (r.packed.numel() - r.header_bytes) // 128)

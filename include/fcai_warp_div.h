@@ -136,6 +136,25 @@ int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B,
                                 void *workspace, int64_t workspace_bytes, uint32_t *max_rounds,
                                 fcai_warp_div_encode_info *info, fcai_stream_t stream);
 
+/* The encode of fcai_warp_div_encode_latent in two halves, so that the
+ * host's wait for the payload size overlaps device work.  _submit enqueues
+ * the encode and the copy of its status words and returns at once (same
+ * arguments, no info); the caller may then enqueue other work on the stream
+ * (the next batch's analysis transform, an earlier batch's decode).
+ * _finish waits for the submitted encode alone, not for that later work,
+ * and fills *info as fcai_warp_div_encode_latent does (FCAI_ERR_WORKSPACE
+ * included: repeat the encode with the larger workspace).  One submitted
+ * encode per stream at a time: until its _finish, any other encode on the
+ * stream is refused (FCAI_ERR_INVALID).  The workspace and max_rounds stay
+ * in use until the _finish and the _pack.  No counterpart in the
+ * reference, whose encode always blocks (warp_ans_kernel_v2.cu:183-306). */
+int fcai_warp_div_encode_latent_submit(const float *y, const float *medians, int32_t B, int32_t N,
+                                       const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,
+                                       const int32_t *offsets, int32_t P, void *workspace, int64_t workspace_bytes,
+                                       uint32_t *max_rounds, fcai_stream_t stream);
+int fcai_warp_div_encode_finish(int32_t B, int32_t N, int32_t C, int32_t P, int64_t workspace_bytes,
+                                fcai_warp_div_encode_info *info, fcai_stream_t stream);
+
 /* Encode without a caller workspace and without allocating: the work of
  * fcai_warp_div_encode followed by fcai_warp_div_encode_pack, with the
  * encode workspace taken from a static device array of
