@@ -771,7 +771,17 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(PackParams p) {
         if (lane == 0) hdr[8 + chunk] = (uint32_t)rounds;
         const uint32_t *st = p.stage + chunk * (int64_t)rows_cap * kLanes + lane;
         uint32_t *out = body + p.offsets[chunk] + lane;
-        for (int r = 0; r < rounds; ++r) out[r * kLanes] = r < used ? st[(used - 1 - r) * kLanes] : 0u;
+        // eight rounds at a time, their loads issued before the stores, so
+        // a warp has eight independent loads in flight instead of one
+        int r = 0;
+        for (; r + 8 <= rounds; r += 8) {
+            uint32_t v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = r + i < used ? __ldcs(st + (int64_t)(used - 1 - r - i) * kLanes) : 0u;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) out[(int64_t)(r + i) * kLanes] = v[i];
+        }
+        for (; r < rounds; ++r) out[(int64_t)r * kLanes] = r < used ? st[(int64_t)(used - 1 - r) * kLanes] : 0u;
     }
 }
 
