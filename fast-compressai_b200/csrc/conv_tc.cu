@@ -154,7 +154,10 @@ struct Layout {
     static constexpr int kPatchBufs = kWide ? 1 : 2;  // first layer: input window buffers
     static constexpr int kX2One = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kX2 = kPingPong ? 2 * kX2One : kX2One;
-    static constexpr int kSRow = kNpad + 1;  // scatter buffer: fp32 words per pixel (+1 against bank conflicts)
+    // scatter buffer: fp32 words per pixel, a multiple of 4 whose quarter is
+    // odd (84 for 80 columns), so that a warp's 16-byte row stores hit every
+    // bank group once
+    static constexpr int kSRow = ((kNpad / 4) | 1) * 4;
     static constexpr int kSOne = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
     static constexpr int kS = kPingPong ? 2 * kSOne : kSOne;
     // operand ring: as many stages as the shared memory left over holds
@@ -833,13 +836,21 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 // of the 12 x 28 core block sums the 4-9 contributions that
                 // land on it; one work item = one output pixel.
                 float *S = reinterpret_cast<float *>(smem + Lay::offS + grp * Lay::kSOne);
-#pragma unroll 1
-                for (int c = c_lo; c < c_hi; c += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(d1 + c, v);
+                {
+                    constexpr int kChunks = kNpad / 16;
+                    uint32_t v[kChunks][16];
+#pragma unroll
+                    for (int c = 0; c < kChunks; ++c) tmem_ld16(d1 + c * 16, v[c]);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) S[m * Lay::kSRow + c + e] = __uint_as_float(v[e]);
+                    for (int c = 0; c < kChunks; ++c) {
+                        tmem_regs_ready(v[c]);
+                        float4 *row = reinterpret_cast<float4 *>(S + m * Lay::kSRow + c * 16);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            row[q] = make_float4(__uint_as_float(v[c][4 * q]), __uint_as_float(v[c][4 * q + 1]),
+                                                 __uint_as_float(v[c][4 * q + 2]), __uint_as_float(v[c][4 * q + 3]));
+                    }
                 }
                 named_barrier_sync(gbar, Lay::kGroupThreads);
                 float *out = reinterpret_cast<float *>(p.out);
