@@ -79,6 +79,14 @@ constexpr uint32_t kBypassBits = 4;
 constexpr uint32_t kBypassMax = 15;
 constexpr int kLutShift = 9;              // decode LUT bucket = slot >> 9
 constexpr int kLutBuckets = 65536 >> kLutShift;
+// The chunk-group decode stages only its P rows, so its bucket table can be
+// finer: slot >> group_lut_shift(P), from 2048 buckets a row for P <= 4 (a
+// bucket then rarely holds more than one symbol, and the linear step after
+// the lookup rarely runs) to the 128 of the full table for P > 32; at most
+// 16 KB a CTA.
+__host__ __device__ inline int group_lut_shift(int P) {
+    return P <= 4 ? 5 : P <= 8 ? 6 : P <= 16 ? 7 : P <= 32 ? 8 : kLutShift;
+}
 constexpr int kMaxSymbolWords = 10;       // <= 8 nibbles + count + symbol puts
 constexpr int64_t kCtrlBytes = 256;
 constexpr int kMaxSmemBytes = 200 * 1024;
@@ -273,6 +281,7 @@ struct GroupTables {
     const uint16_t *s_lut;  // [nc][kLutBuckets] (decode)
     const float *s_med;     // [nc] (latent modes)
     int c0, Ls;
+    int lut_shift;          // bucket = slot >> lut_shift, 65536 >> lut_shift buckets a row
 
     __device__ __forceinline__ int2 chan(int c) const { return s_ch[c - c0]; }
     __device__ __forceinline__ uint32_t entry(int c, int v, uint32_t &) const { return s_tab[(c - c0) * Ls + v]; }
@@ -280,7 +289,7 @@ struct GroupTables {
     __device__ __forceinline__ float median(int c) const { return s_med[c - c0]; }
     __device__ __forceinline__ int search(int c, int maxv, uint32_t slot, uint32_t &ent, uint32_t &) const {
         const int cl = c - c0;
-        int s = s_lut[cl * kLutBuckets + (slot >> kLutShift)];
+        int s = s_lut[(cl << (16 - lut_shift)) + (slot >> lut_shift)];
         if (s > maxv) s = maxv;
         const uint32_t *row = s_tab + cl * Ls;
         uint32_t e = row[s];
@@ -293,7 +302,8 @@ struct GroupTables {
 // Stages rows [c0, c0 + nc) (entries, {offset, maxv}, optional magic, slot
 // buckets and medians) and validates them.  Ends with __syncthreads().
 __device__ void stage_group(const TableArgs &t, int c0, int nc, uint32_t *s_tab, uint64_t *s_mag, int2 *s_ch,
-                            uint16_t *s_lut, float *s_med, const float *medians, uint32_t &flags) {
+                            uint16_t *s_lut, float *s_med, const float *medians, uint32_t &flags, int lut_shift) {
+    const int buckets = 65536 >> lut_shift;
     const int Ls = t.L - 1;
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
         int32_t size = __ldg(t.sizes + c0 + c);
@@ -316,10 +326,10 @@ __device__ void stage_group(const TableArgs &t, int c0, int nc, uint32_t *s_tab,
             if (s_lut) {
                 const int lo = v == 0 ? 0 : (int)(ent & 0xFFFFu);
                 const int hi = v == maxv ? 65536 : (int)(ent & 0xFFFFu) + (int)(ent >> 16) + 1;
-                int u0 = (lo + (1 << kLutShift) - 1) >> kLutShift;
-                int u1 = (hi + (1 << kLutShift) - 1) >> kLutShift;
-                if (u1 > kLutBuckets) u1 = kLutBuckets;
-                for (int u = u0; u < u1; ++u) s_lut[c * kLutBuckets + u] = (uint16_t)v;
+                int u0 = (lo + (1 << lut_shift) - 1) >> lut_shift;
+                int u1 = (hi + (1 << lut_shift) - 1) >> lut_shift;
+                if (u1 > buckets) u1 = buckets;
+                for (int u = u0; u < u1; ++u) s_lut[c * buckets + u] = (uint16_t)v;
             }
         }
         s_tab[e] = ent;
@@ -686,7 +696,7 @@ __host__ __device__ inline GroupSmem group_smem(int P, int L, bool encode) {
     g.ch = (g.tab + ent * 4 + 7) & ~7ll;
     g.med = g.ch + (int64_t)P * 8;
     g.lut = (g.med + (int64_t)P * 4 + 7) & ~7ll;
-    g.bytes = g.lut + (encode ? 0 : (int64_t)P * kLutBuckets * 2);
+    g.bytes = g.lut + (encode ? 0 : (int64_t)P * (65536 >> group_lut_shift(P)) * 2);
     return g;
 }
 
@@ -705,7 +715,7 @@ __global__ void __launch_bounds__(kThreads) encode_group_kernel(EncParams p) {
     const GroupSmem gs = group_smem(p.P, p.t.L, true);
     GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), reinterpret_cast<const uint64_t *>(smem + gs.mag),
                    reinterpret_cast<const int2 *>(smem + gs.ch), nullptr, reinterpret_cast<const float *>(smem + gs.med),
-                   0, p.t.L - 1};
+                   0, p.t.L - 1, kLutShift};
     Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
     if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
     for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
@@ -715,7 +725,8 @@ __global__ void __launch_bounds__(kThreads) encode_group_kernel(EncParams p) {
             __syncthreads();  // the previous group's rows are no longer read
             stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), reinterpret_cast<uint64_t *>(smem + gs.mag),
                         reinterpret_cast<int2 *>(smem + gs.ch), nullptr,
-                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags);
+                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags,
+                        kLutShift);
             gt.c0 = c0;
         }
         const int b = bb * W + warp;
@@ -1090,7 +1101,7 @@ __global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
     const GroupSmem gs = group_smem(P, p.t.L, false);
     GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), nullptr, reinterpret_cast<const int2 *>(smem + gs.ch),
                    reinterpret_cast<const uint16_t *>(smem + gs.lut), reinterpret_cast<const float *>(smem + gs.med), 0,
-                   p.t.L - 1};
+                   p.t.L - 1, group_lut_shift(P)};
     Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
     if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
     for (int64_t g = blockIdx.x; g < groups && !skip; g += gridDim.x) {
@@ -1100,7 +1111,8 @@ __global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
             __syncthreads();
             stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), nullptr,
                         reinterpret_cast<int2 *>(smem + gs.ch), reinterpret_cast<uint16_t *>(smem + gs.lut),
-                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags);
+                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags,
+                        group_lut_shift(P));
             gt.c0 = c0;
         }
         const int b = bb * W + warp;
