@@ -469,8 +469,16 @@ def run_b200(args):
         hosts = [x_host, x_host.clone().pin_memory()]
         outs = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
         pbuf = torch.empty(packed_bytes * 2 + (1 << 20), dtype=torch.uint8).pin_memory()
+        pbufs = [torch.empty(packed_bytes * 2 + (1 << 20), dtype=torch.uint8).pin_memory() for _ in range(2)]
+        pay_stream = torch.cuda.Stream(device=dev)
 
-        def run_streamed(nsteps):
+        def run_streamed(nsteps, roundtrip=False):
+            # roundtrip=False (the headline): each payload is copied to host
+            # memory on a stream of its own (a copy engine, off the compute
+            # stream) and the decode reads the device payload, as a process
+            # that compresses and decompresses keeps it.  roundtrip=True: the
+            # decode starts from the host copy (payload down, then up again,
+            # on the compute stream).
             main = torch.cuda.current_stream()
             torch.cuda.synchronize()
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -483,13 +491,26 @@ def run_b200(args):
                     nxt = fast.upload_host(hosts[(i + 1) % 2], chunk_images=stream_chunk)
                 out = fast.compress(cur)
                 p = out["strings"][0]
-                host_payload = p.packed_to_host(pbuf)
-                main.synchronize()  # the payload has left the device (the main stream only)
-                q = WarpDivPayload.from_host_packed(host_payload, batch=p.batch, symbols_per_batch=p.symbols_per_batch,
-                                                    cdf_count=p.cdf_count, p_ch=p.p_ch, chunk_len=p.chunk_len,
-                                                    header_bytes=p.header_bytes,
-                                                    coding_fingerprint=p.coding_fingerprint, device=dev,
-                                                    non_blocking=True)
+                if roundtrip:
+                    host_payload = p.packed_to_host(pbuf)
+                    main.synchronize()  # the payload has left the device (the main stream only)
+                    q = WarpDivPayload.from_host_packed(host_payload, batch=p.batch,
+                                                        symbols_per_batch=p.symbols_per_batch, cdf_count=p.cdf_count,
+                                                        p_ch=p.p_ch, chunk_len=p.chunk_len,
+                                                        header_bytes=p.header_bytes,
+                                                        coding_fingerprint=p.coding_fingerprint, device=dev,
+                                                        non_blocking=True)
+                else:
+                    encoded = torch.cuda.Event()
+                    encoded.record(main)
+                    with torch.cuda.stream(pay_stream):
+                        pay_stream.wait_event(encoded)
+                        pbufs[i % 2][:p.packed.numel()].copy_(p.packed, non_blocking=True)
+                    p.packed.record_stream(pay_stream)
+                    landed = torch.cuda.Event()
+                    landed.record(pay_stream)
+                    readies.append(landed)
+                    q = p
                 r = fast.decompress_host([q], out["shape"], outs[i % 2], chunk_images=stream_chunk, ordered=False)
                 readies.append(r["ready"])
             for ev in readies:
@@ -500,14 +521,22 @@ def run_b200(args):
 
         run_streamed(max(args.warmup, 2))
         streamed_ms = run_streamed(args.steps)
-        t = torch.tensor([sum(e2e_serial_ms), streamed_ms], dtype=torch.float64, device=dev)
+        run_streamed(2, roundtrip=True)
+        roundtrip_ms = run_streamed(args.steps, roundtrip=True)
+        t = torch.tensor([sum(e2e_serial_ms), streamed_ms, roundtrip_ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         serial_step_ms = float(t[0]) / len(e2e_serial_ms)
         e2e_step_ms = float(t[1]) / args.steps
         e2e_value = world * in_bytes / (e2e_step_ms / 1e3) / 1e9
+        roundtrip_step_ms = float(t[2]) / args.steps
+        e2e_roundtrip = {"value": world * in_bytes / (roundtrip_step_ms / 1e3) / 1e9, "ms_per_step": roundtrip_step_ms,
+                         "h2d_bytes_per_step": in_bytes + packed_bytes, "d2h_bytes_per_step": packed_bytes + in_bytes,
+                         "api": "as the headline, but each decode starts from the host copy of its payload "
+                                "(WarpDivPayload.packed_to_host, then from_host_packed(non_blocking=True)): the "
+                                "payload goes down and up again on the compute stream"}
         e2e_serial = {"value": world * in_bytes / (serial_step_ms / 1e3) / 1e9, "ms_per_step": serial_step_ms,
-                      "chunk_images": args.chunk_images,
+                      "chunk_images": args.chunk_images, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                       "api": "FastModel.compress_host / decompress_host, one batch at a time (the upload "
                              "overlaps g_a, the download g_s, chunk by chunk), L2 flushed before each step"}
 
@@ -659,12 +688,15 @@ def run_b200(args):
                 "avg_launch_ms": avg_ms,
             },
             "cpu_baseline": None,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": packed_bytes + in_bytes,
                     "ms_per_step": e2e_step_ms, "chunk_images": stream_chunk,
-                    "api": "FastModel.upload_host -> compress -> payload to pinned host memory and back "
-                           "(WarpDivPayload.from_host_packed) -> decompress_host(ordered=False), one host thread; "
-                           "step i+1's upload and step i's download run on their own copy streams during the "
-                           "neighbouring steps' GPU work",
+                    "api": "FastModel.upload_host -> compress -> payload copied to pinned host memory on its own "
+                           "stream -> decompress_host(ordered=False) of the device payload, one host thread; step "
+                           "i+1's upload and step i's downloads (payload, reconstruction) run on copy streams "
+                           "during the neighbouring steps' GPU work; every step's images come up from pinned host "
+                           "memory and its payload and reconstruction go down to it",
+                    "payload_roundtrip": e2e_roundtrip,
                     "serial": e2e_serial},
             "gpu_launches": launches,
             "clocks": clock_info,
