@@ -2,7 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY (the parity checker of the GPU tests and of the
 golden fixtures).  Sources are compiled where they lie in the reference
-checkout (default /root/reference, or $FCAI_REFERENCE); nothing is copied
+checkout ($FCAI_REFERENCE, else the build environment's read-only checkout
+below); nothing is copied
 into this repository.  Output: oracle/_ref/_warp_div_ref.so, a torch
 extension exposing the reference's pybind entry points ``encode_warp_div``
 and ``decode_warp_div`` (coders/cuda/ans_gpu.cpp:25-30).
