@@ -1449,24 +1449,35 @@ static int encode_info_from_status(const Dims &d, const EncLayout &el, const lon
     return FCAI_OK;
 }
 
-// submit: enqueue the encode and the copy of its status words to the mapped
+// How an encode returns its status words to the host.
+enum class StatusPath {
+    kMapped,  // one-warp kernel into the stream's mapped pinned slot, then a stream wait
+    kSubmit,  // as kMapped into the second slot, collected by fcai_warp_div_encode_finish
+    kCopy,    // cudaMemcpyAsync into the caller's stack, then a stream wait: creates
+              // nothing (no pinned slot, no event) on any call
+};
+
+// kSubmit: enqueue the encode and the copy of its status words to the mapped
 // buffer's second slot, record the stream's status event and return at once
 // (info untouched); fcai_warp_div_encode_finish collects the status.
 static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes, const float *y,
                        const float *medians, int32_t B, int32_t N, const int32_t *cdfs, int32_t C, int32_t L,
                        const int32_t *cdf_sizes, const int32_t *offsets, int32_t P, void *workspace,
                        int64_t workspace_bytes, uint32_t *max_rounds, fcai_warp_div_encode_info *info,
-                       cudaStream_t stream, bool submit = false) {
+                       cudaStream_t stream, StatusPath path = StatusPath::kMapped) {
+    const bool submit = path == StatusPath::kSubmit;
     Dims d;
     int rc = make_dims(B, N, C, P, d);
     if (rc) return rc;
     if ((rc = check_tables_args(cdfs, C, L, cdf_sizes, offsets))) return rc;
     if (!workspace || !max_rounds || (!info && !submit)) return fcai::fail(FCAI_ERR_INVALID, "null argument");
     MappedStatus ms{};
-    if ((rc = mapped_status(stream, &ms))) return rc;
-    if (*ms.pending)
-        return fcai::fail(FCAI_ERR_INVALID,
-                          "an encode submitted on this stream awaits fcai_warp_div_encode_finish");
+    if (path != StatusPath::kCopy) {
+        if ((rc = mapped_status(stream, &ms))) return rc;
+        if (*ms.pending)
+            return fcai::fail(FCAI_ERR_INVALID,
+                              "an encode submitted on this stream awaits fcai_warp_div_encode_finish");
+    }
     if (mode == kModeLatent ? (!y || !medians) : !symbols) return fcai::fail(FCAI_ERR_INVALID, "null input");
     EncLayout el = enc_layout(d.chunks);
     int64_t avail = workspace_bytes - el.fixed_bytes;
@@ -1523,7 +1534,12 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
         return FCAI_OK;
     }
     long long status[8];
-    if ((rc = read_status(p.ctrl->status, 8, stream, status))) return rc;
+    if (path == StatusPath::kCopy) {
+        FCAI_CUDA_TRY(cudaMemcpyAsync(status, p.ctrl->status, sizeof(status), cudaMemcpyDeviceToHost, stream));
+        FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+    } else if ((rc = read_status(p.ctrl->status, 8, stream, status))) {
+        return rc;
+    }
     return encode_info_from_status(d, el, status, workspace_bytes, info);
 }
 
@@ -1669,7 +1685,8 @@ int fcai_warp_div_encode_latent_submit(const float *y, const float *medians, int
                                        uint32_t *max_rounds, fcai_stream_t stream) {
     fcai::clear_error();
     return encode_impl(kModeLatent, nullptr, nullptr, y, medians, B, N, cdfs, C, L, cdf_sizes, offsets, P, workspace,
-                       workspace_bytes, max_rounds, nullptr, reinterpret_cast<cudaStream_t>(stream), true);
+                       workspace_bytes, max_rounds, nullptr, reinterpret_cast<cudaStream_t>(stream),
+                       StatusPath::kSubmit);
 }
 
 int fcai_warp_div_encode_finish(int32_t B, int32_t N, int32_t C, int32_t P, int64_t workspace_bytes,
@@ -1750,8 +1767,12 @@ int fcai_warp_div_encode_noalloc(const int32_t *symbols, const int32_t *indexes,
     // The array keeps the previous call's contents; the control block must
     // start at zero (a call that stopped early may have left it set).
     FCAI_CUDA_TRY(cudaMemsetAsync(scratch, 0, kCtrlBytes, stream));
+    // Status words come back by a plain copy into this frame: the mapped
+    // pinned slot of the other entry points is created on a stream's first
+    // encode (cudaHostAlloc, cudaEventCreate), which this entry point must
+    // never do.
     rc = encode_impl(indexes ? kModeIdx : kModeChannel, symbols, indexes, nullptr, nullptr, B, N, cdfs, C, L,
-                     cdf_sizes, offsets, P, scratch, need, max_rounds, info, stream);
+                     cdf_sizes, offsets, P, scratch, need, max_rounds, info, stream, StatusPath::kCopy);
     if (rc) return rc;
     if (info->packed_bytes > packed_capacity)
         return fcai::fail(FCAI_ERR_INVALID, "packed buffer of %lld bytes cannot hold the %lld-byte payload",

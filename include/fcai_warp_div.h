@@ -183,7 +183,23 @@ int fcai_warp_div_encode_finish(int32_t B, int32_t N, int32_t C, int32_t P, int6
  * Calls whose GPU work overlaps (issued on different streams, or from
  * different threads, with nothing ordering them) race on the array and
  * corrupt each other's payloads: issue them on one stream or serialise
- * them. */
+ * them.
+ *
+ * No call allocates: no cudaMalloc, cudaFree, cudaHostAlloc or event
+ * creation, on the first call on a device or stream as on any other.  The
+ * status words that size the payload come back by a cudaMemcpyAsync into
+ * the call's own stack frame followed by a wait for `stream`.  The first
+ * call on each device does a one-time set-up with that device current: it
+ * looks up the array's device address (cudaGetSymbolAddress; under CUDA's
+ * lazy module loading, the default, this is also when the array is
+ * reserved in the device's memory), and, if no other coder call has run on
+ * the device yet, fills the library's division table with one kernel and a
+ * wait for `stream`.  Make that first call early, before another allocator
+ * takes the device's memory (or run with CUDA_MODULE_LOADING=EAGER, which
+ * reserves the array when the library's kernels load), and before any
+ * stream capture.  The set-up is cached per device ordinal for the life of
+ * the process: a cudaDeviceReset invalidates it, and is not supported while
+ * this library is in use. */
 #define FCAI_WARP_DIV_SCRATCH_BYTES (16 * 1024 * 1024)
 int fcai_warp_div_encode_noalloc(const int32_t *symbols, const int32_t *indexes, int32_t B, int32_t N,
                                  const int32_t *cdfs, int32_t C, int32_t L, const int32_t *cdf_sizes,

@@ -2,9 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY (the parity checker of the GPU tests and of the
 golden fixtures).  Sources are compiled where they lie in the reference
-checkout ($FCAI_REFERENCE, else the build environment's read-only checkout
-below); nothing is copied
-into this repository.  Output: oracle/_ref/_warp_div_ref.so, a torch
+checkout: $FCAI_REFERENCE, else the ``reference_path`` that BASELINE.json at
+the repository root records.  Nothing is copied into this repository.  Output: oracle/_ref/_warp_div_ref.so, a torch
 extension exposing the reference's pybind entry points ``encode_warp_div``
 and ``decode_warp_div`` (coders/cuda/ans_gpu.cpp:25-30).
 
@@ -14,6 +13,7 @@ and ``decode_warp_div`` (coders/cuda/ans_gpu.cpp:25-30).
 from __future__ import annotations
 
 import importlib.util
+import json
 import os
 import shutil
 import sys
@@ -25,8 +25,16 @@ NAME = "_warp_div_ref"
 SOURCES = ["ans_gpu.cpp", "warp_ans_kernel.cu", "warp_ans_kernel_v2.cu", "warp_index_check.cu"]
 
 
-def reference_root() -> Path:
-    return Path(os.environ.get("FCAI_REFERENCE", "/root/reference"))
+def reference_root() -> Path | None:
+    env = os.environ.get("FCAI_REFERENCE")
+    if env:
+        return Path(env)
+    try:
+        rec = json.loads((HERE.parent / "BASELINE.json").read_text())
+    except (OSError, ValueError):
+        return None
+    path = rec.get("reference_path")
+    return Path(path) if path else None
 
 
 def built_path() -> Path:
@@ -35,8 +43,9 @@ def built_path() -> Path:
 
 def build(force: bool = False) -> Path | None:
     """Compile the reference extension if its sources are present; returns the .so path."""
-    src_dir = reference_root() / "src" / "fast_compressai" / "coders" / "cuda"
-    if not src_dir.is_dir():
+    root = reference_root()
+    src_dir = root / "src" / "fast_compressai" / "coders" / "cuda" if root else None
+    if src_dir is None or not src_dir.is_dir():
         return built_path() if built_path().exists() else None
     if built_path().exists() and not force:
         return built_path()

@@ -12,6 +12,12 @@ already seen a process that ran every other test.
 from __future__ import annotations
 
 import ctypes
+import json
+import os
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -146,3 +152,67 @@ def test_rejects_a_short_payload_buffer_then_recovers(cuda_device):
     assert rc == N.FCAI_ERR_INVALID
     assert "cannot hold" in N.lib().fcai_last_error().decode()
     _check_same(c, cuda_device)
+
+
+# Run in a child process, so that the no-allocation call is the first coder
+# call of the process and runs on streams that no earlier call has used.
+_FRESH_PROCESS = textwrap.dedent("""
+    import ctypes, json, sys
+    sys.path[:0] = [sys.argv[1], sys.argv[1] + "/fast-compressai_b200"]
+    import numpy as np, torch
+    from fast_compressai import _native as N
+    from oracle import oracle as O
+    from tests.coder_inputs import channel_indexes, laplacian_symbols, laplacian_tables
+
+    dev = torch.device("cuda:0")
+    B, C, HW, P = 2, 96, 40, 4
+    cdfs, sizes, offs, scales = laplacian_tables(C, seed=51)
+    sym = laplacian_symbols(B, C, HW, scales, seed=52, escape_rate=0.01)
+    d = [torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in (sym, cdfs, sizes, offs)]
+    plan = N.WarpDivPlan()
+    lib = N.lib()
+    N.check(lib.fcai_warp_div_plan_create(B, C * HW, C, P, ctypes.byref(plan)))
+    outs = [(torch.full((plan.max_packed_bytes,), 0x5A, dtype=torch.uint8, device=dev),
+             torch.zeros(B * plan.chunks, dtype=torch.int32, device=dev)) for _ in range(2)]
+    torch.cuda.synchronize()
+
+    def call(stream, packed, mr):
+        info = N.WarpDivEncodeInfo()
+        p = lambda t: ctypes.c_void_p(t.data_ptr())
+        rc = lib.fcai_warp_div_encode_noalloc(p(d[0]), None, B, C * HW, p(d[1]), C, cdfs.shape[1], p(d[2]),
+                                              p(d[3]), P, p(packed), packed.numel(), p(mr), ctypes.byref(info),
+                                              ctypes.c_void_p(stream.cuda_stream))
+        stream.synchronize()
+        return rc, info
+
+    res = {}
+    a0 = torch.cuda.memory_allocated(dev)
+    rc, info = call(torch.cuda.Stream(dev), *outs[0])     # first coder call of the process
+    res["first"] = [rc, torch.cuda.memory_allocated(dev) - a0]
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    rc2, info2 = call(torch.cuda.Stream(dev), *outs[1])   # another fresh stream
+    res["second"] = [rc2, torch.cuda.memory_allocated(dev) - a0, torch.cuda.mem_get_info(dev)[0] - free0]
+    want, want_mr, _, _ = O.warp_div_encode(sym, None, cdfs, sizes, offs, P)
+    n = info.packed_bytes
+    res["match"] = [bool(np.array_equal(o[0][:n].cpu().numpy(), want)) and
+                    bool(np.array_equal(o[1].cpu().numpy().view(np.uint32), want_mr.reshape(-1)))
+                    for o in outs] + [n == info2.packed_bytes == want.size]
+    print(json.dumps(res))
+""")
+
+
+def test_first_call_in_a_fresh_process_on_fresh_streams():
+    # The first call of a process on a stream that has seen no coder call is
+    # where the other entry points create their per-stream pinned status slot
+    # and event; this one must create nothing there, or on a second fresh
+    # stream.  Torch's allocator must not move, and the device's free memory
+    # must not change across the second call.
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, FCAI_SKIP_BUILD="1")
+    proc = subprocess.run([sys.executable, "-c", _FRESH_PROCESS, str(root)], capture_output=True, text=True,
+                          timeout=600, env=env)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    res = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert res["first"] == [0, 0], res
+    assert res["second"] == [0, 0, 0], res
+    assert all(res["match"]), res
