@@ -90,14 +90,18 @@ def smooth_noise_images(B, H, W, seed):
 
 
 def build_model():
-    import torch
+    """FactorizedPrior(128, 192), random init from seed 0, with its latent
+    spread over its CDF tables (tests/model_inputs.py: the last analysis
+    convolution scaled so that y has standard deviation 12 on two seeded
+    calibration images, the first synthesis convolution by the inverse, the
+    entropy bottleneck's quantiles set from the latent and update(force=True)).
+    A plain random-init model quantises every latent value to symbol 0, which
+    would time the coder on a constant stream; trained weights are not
+    available offline."""
+    from tests.model_inputs import spread_latent_prior
 
-    from fast_compressai.balle import FactorizedPrior
-
-    torch.manual_seed(0)
-    model = FactorizedPrior(128, 192).eval()
-    model.update(force=True)
-    return model
+    calib = smooth_noise_images(2, 256, 384, seed=7)
+    return spread_latent_prior(128, 192, calib, target_std=12.0, seed=0)
 
 
 def psnr(a, b):
@@ -160,6 +164,62 @@ def time_cpu(model, args, steps, warmup):
         "ms_per_step": sec * 1e3,
         "payload_bytes": payload,
     }
+
+
+def time_gpu_transforms_cpu_rans(model_gpu, x, steps):
+    """The reference's own baseline arrangement (examples/balle_example.py:
+    171-174 of the reference: CompressAI's model.compress on the CUDA model):
+    FP32 transforms on the GPU (the model's torch modules, cuDNN with TF32
+    off), the latent's symbols brought to the host, the single-stream rANS
+    coder on the host cores (one stream per image), the decoded latent sent
+    back for the synthesis.  Timed on 1 core and on all cores, with the
+    coder's encode and decode times reported apart.  Wall-clock medians."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    eb = model_gpu.entropy_bottleneck
+    cdfs, sizes, offs = (t.cpu().numpy() for t in (eb._quantized_cdf, eb._cdf_length, eb._offset))
+    med = eb._get_medians().detach().reshape(1, -1, 1, 1)
+    cores = os.cpu_count() or 1
+    tf32 = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    rows = {}
+    try:
+        with torch.no_grad():
+            for threads in (1, cores):
+                ts = {"g_a": [], "encode": [], "decode": [], "g_s": []}
+                for i in range(steps + 1):
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    sym = torch.round(model_gpu.g_a(x) - med).int().cpu()
+                    t1 = time.perf_counter()
+                    B = sym.shape[0]
+                    words, n = O.rans_encode_batch(sym.reshape(B, -1).numpy(), None, cdfs, sizes, offs,
+                                                   threads=threads)
+                    t2 = time.perf_counter()
+                    dec = O.rans_decode_batch(words, n, None, cdfs, sizes, offs, B, sym[0].numel(),
+                                              threads=threads)
+                    t3 = time.perf_counter()
+                    y_hat = torch.from_numpy(np.ascontiguousarray(dec)).reshape(sym.shape).to(x.device).float() + med
+                    model_gpu.g_s(y_hat).clamp_(0, 1).cpu()
+                    t4 = time.perf_counter()
+                    if i > 0:  # the first pass warms cuDNN and the coder up
+                        for k, v in zip(ts, (t1 - t0, t2 - t1, t3 - t2, t4 - t3)):
+                            ts[k].append(v)
+                med_s = {k: statistics.median(v) for k, v in ts.items()}
+                total = sum(med_s.values())
+                rows["1_core" if threads == 1 else "all_cores"] = {
+                    "value": x.numel() * 4 / total / 1e9, "cores": threads, "ms_per_step": total * 1e3,
+                    "coder_encode_ms": med_s["encode"] * 1e3, "coder_decode_ms": med_s["decode"] * 1e3,
+                    "gpu_transforms_ms": (med_s["g_a"] + med_s["g_s"]) * 1e3}
+    finally:
+        torch.backends.cudnn.allow_tf32 = tf32
+    return {"unit": UNIT, "images": int(x.shape[0]), **rows,
+            "sample": f"the step's {int(x.shape[0])} images, median of {steps} steps",
+            "api": "FP32 torch g_a / g_s on the GPU + single-stream rANS on the host (one stream per image), "
+                   "symbols and decoded latent copied between them"}
 
 
 def run_reference(args):
@@ -309,6 +369,64 @@ def read_traffic():
     return out
 
 
+def measure_link_ceiling(dev, host_in, down_bytes, steps, warmup, world):
+    """The host-link ceiling of one step: every rank copies one step's input
+    bytes up (pinned host -> device) and its payload + reconstruction bytes
+    down (device -> pinned host) with plain cudaMemcpyAsync on two streams at
+    once, nothing else running, all ranks together.  Also each direction
+    alone.  Device time with CUDA events around K steps, max over ranks.
+    Returns ms per step and the input-image GB/s that a step limited by
+    these copies alone would reach (the e2e metric's units)."""
+    import torch
+    import torch.distributed as dist
+
+    up_dst = torch.empty_like(host_in, device=dev)
+    down_src = torch.empty(down_bytes, dtype=torch.uint8, device=dev)
+    down_dst = torch.empty(down_bytes, dtype=torch.uint8).pin_memory()
+    s_up, s_down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    main = torch.cuda.current_stream(dev)
+
+    def run(n, up, down):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(main)
+        for s in (s_up, s_down):
+            s.wait_event(a)
+        for _ in range(n):
+            if up:
+                with torch.cuda.stream(s_up):
+                    up_dst.copy_(host_in, non_blocking=True)
+            if down:
+                with torch.cuda.stream(s_down):
+                    down_dst.copy_(down_src, non_blocking=True)
+        for s in (s_up, s_down):
+            main.wait_stream(s)
+        b.record(main)
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    out = {}
+    for name, up, down in (("both", True, True), ("h2d", True, False), ("d2h", False, True)):
+        run(max(warmup, 1), up, down)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = run(steps, up, down)
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = float(t[0]) / steps
+    in_bytes = host_in.numel() * host_in.element_size()
+    res = {"value": world * in_bytes / (out["both"] / 1e3) / 1e9, "unit": UNIT, "ms_per_step": out["both"],
+           "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": down_bytes,
+           "link_gbs_per_gpu": {"both": (in_bytes + down_bytes) / (out["both"] / 1e3) / 1e9,
+                                "h2d_alone": in_bytes / (out["h2d"] / 1e3) / 1e9,
+                                "d2h_alone": down_bytes / (out["d2h"] / 1e3) / 1e9},
+           "api": "cudaMemcpyAsync of one step's bytes, up and down on two streams at once, all ranks at once, "
+                  "no compute (max over ranks)"}
+    del up_dst, down_src, down_dst
+    return res
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -326,6 +444,13 @@ def run_b200(args):
     dev = torch.device("cuda", local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def sync_ranks():
+        # every rank starts a timed loop together, so that loops that share
+        # the host link contend as they do in a real job
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
 
     model = build_model()
     x_cpu = smooth_noise_images(args.batch, args.height, args.width, seed=1234 + rank)
@@ -445,6 +570,7 @@ def run_b200(args):
         # (a) one batch at a time, each step bracketed by events, L2 flushed before it
         bufs = new_bufs()
         e2e_serial_ms = []
+        sync_ranks()
         for i in range(args.warmup + args.steps):
             flush.fill_(1.0)
             torch.cuda.synchronize()
@@ -520,9 +646,15 @@ def run_b200(args):
             return t0.elapsed_time(t1)
 
         run_streamed(max(args.warmup, 2))
+        sync_ranks()
         streamed_ms = run_streamed(args.steps)
         run_streamed(2, roundtrip=True)
+        sync_ranks()
         roundtrip_ms = run_streamed(args.steps, roundtrip=True)
+
+        # ---- the host-link ceiling of the same step's bytes ----------------
+        sync_ranks()
+        link = measure_link_ceiling(dev, x_host, packed_bytes + in_bytes, args.steps, args.warmup, world)
         t = torch.tensor([sum(e2e_serial_ms), streamed_ms, roundtrip_ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -541,39 +673,84 @@ def run_b200(args):
                              "overlaps g_a, the download g_s, chunk by chunk), L2 flushed before each step"}
 
         # ---- coder kernels alone on this batch's latent (ANS roofline) ------
+        # Host-call times bracket each call (launches, the encode's size
+        # read-back and its pack); kernel times bracket the kernels alone:
+        # the encode kernel (with the one-warp copy of its status words) as
+        # enqueued by the submit half, the pack kernel after the host has
+        # learnt the size, and the decode kernel of a payload this library
+        # wrote (no prep kernel below 2048 chunks).  L2 flushed before each.
+        from fast_compressai.coders import _warp_div as wd_ext
+
         fc = fast._coder
         eb = fast.model.entropy_bottleneck
         cdfs, lengths, offs = fc._tables(eb)
         med = fc._medians(eb)
         y = fast.model.g_a(x).float().contiguous()
         be = fc.backend
-        enc_ev, dec_ev = [], []
+        call_ev, kern_ev = [], []
         y_hat = torch.empty_like(y)
         for i in range(args.warmup + args.steps):
             flush.fill_(1.0)
-            a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-            a.record()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
             pl = be._encode_latent(y, med, cdfs, lengths, offs, args.p_ch)
-            b.record()
+            ev[1].record()
             be._decode_latent(pl, cdfs, lengths, offs, med, y_hat)
-            c.record()
+            ev[2].record()
+            flush.fill_(1.0)
+            kv = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            kv[0].record()
+            pend = wd_ext.encode_latent_submit(y, med, cdfs, lengths, offs, args.p_ch)
+            kv[1].record()
+            # the host waits for the size here, so kv[2] is recorded on an idle stream
+            torch.cuda.current_stream().synchronize()
+            kv[2].record()
+            r = wd_ext.encode_finish(pend)
+            kv[3].record()
+            flush.fill_(1.0)
+            kv[4].record()
+            be._decode_latent(pl, cdfs, lengths, offs, med, y_hat)
+            kv[5].record()
             if i >= args.warmup:
-                enc_ev.append((a, b))
-                dec_ev.append((b, c))
+                call_ev.append(ev)
+                kern_ev.append(kv)
         torch.cuda.synchronize()
-        enc_ms = statistics.median(a.elapsed_time(b) for a, b in enc_ev)
-        dec_ms = statistics.median(a.elapsed_time(b) for a, b in dec_ev)
+        if not torch.equal(r.packed, pl.packed):
+            raise SystemExit("kernel-timed encode wrote another payload than the host-call encode")
+        enc_ms = statistics.median(e[0].elapsed_time(e[1]) for e in call_ev)
+        dec_ms = statistics.median(e[1].elapsed_time(e[2]) for e in call_ev)
+        enc_kernel_ms = statistics.median(k[0].elapsed_time(k[1]) for k in kern_ev)
+        pack_kernel_ms = statistics.median(k[2].elapsed_time(k[3]) for k in kern_ev)
+        dec_kernel_ms = statistics.median(k[4].elapsed_time(k[5]) for k in kern_ev)
         sym_bytes = y.numel() * 4
         ans_bytes = sym_bytes + pl.packed.numel()
 
         # ---- quality: B200 path vs the FP32 reference path -----------------
         # accelerate() converted a deep copy; `model` still holds the FP32 modules
-        nq = min(2, args.batch)
+        nq = min(4, args.batch)
         ref = model.to(dev)
         medr = ref.entropy_bottleneck._get_medians().detach().reshape(1, -1, 1, 1)
         xs = x[:nq]
-        x_ref = ref.g_s(torch.round(ref.g_a(xs) - medr) + medr).clamp(0, 1)
-        psnr_drop = psnr(x_ref, xs) - psnr(x_hat[:nq], xs)
+        tf32 = torch.backends.cudnn.allow_tf32
+        torch.backends.cudnn.allow_tf32 = False  # FP32 convolutions for the FP32 path
+        try:
+            sym_ref = torch.round(ref.g_a(xs) - medr)
+            x_ref = ref.g_s(sym_ref + medr).clamp(0, 1)
+            fast_ref = fast_compressai.accelerate(model, P=args.p_ch, device=str(dev), transforms="fp32")
+            ref_payload = fast_ref.compress(xs)["strings"][0].packed.numel()
+        finally:
+            torch.backends.cudnn.allow_tf32 = tf32
+        q_out = fast.compress(xs)
+        x_hat_q = fast.decompress(q_out["strings"], q_out["shape"])["x_hat"]
+        sym_b200 = torch.round(fast.model.g_a(xs).float() - medr)
+        psnr_drop = psnr(x_ref, xs) - psnr(x_hat_q, xs)
+        quality = {"images": nq, "psnr_drop_db": psnr_drop,
+                   "bpp_ratio": q_out["strings"][0].packed.numel() / ref_payload,
+                   "symbol_mismatch_rate": float((sym_b200 != sym_ref).float().mean()),
+                   "symbol_std": float(sym_ref.std()),
+                   "psnr_vs_fp32_reconstruction_db": psnr(x_hat_q, x_ref),
+                   "reference": "the model's FP32 torch modules (cuDNN, TF32 off) through the same coder"}
+        del fast_ref
 
         # ---- the reference's example precision map ------------------------
         # (examples/precision_configs/FactorizedPrior of the reference, kept as
@@ -634,11 +811,13 @@ def run_b200(args):
     dom = per_layer[dominant]
     avg_ms = dom["ms"] / dom["n"]
     achieved = dom["flops"] / (avg_ms / 1e3) / 1e12
+    # The per-layer events come from the serial loop, a timed region of
+    # K steps of ~2 ms (well under a second): the burst peak applies.
     peaks = read_peaks()
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured burst bf16 (MEASURED_PEAKS.json)"
     if peak is None:
-        peak, peak_src = 1400.0, "fallback sustained bf16"
+        peak, peak_src = 1590.0, "fallback burst bf16"
     traffic = read_traffic().get(dominant)
     if traffic is not None and args.batch != 24:
         traffic = traffic * args.batch / 24
@@ -657,7 +836,9 @@ def run_b200(args):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic: seeded smoothed-noise images (Kodak shape stand-in), random-init weights",
+            "data": "synthetic: seeded smoothed-noise images (Kodak shape stand-in), random-init weights with "
+                    "the latent spread over the CDF tables (last analysis conv scaled, quantiles set from the "
+                    "latent)",
             "config": {
                 "workload": "BASELINE config 2 per GPU: FactorizedPrior(N=128,M=192) compress+decompress",
                 "batch_per_gpu": args.batch,
@@ -691,6 +872,7 @@ def run_b200(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": in_bytes,
                     "d2h_bytes_per_step": packed_bytes + in_bytes,
                     "ms_per_step": e2e_step_ms, "chunk_images": stream_chunk,
+                    "link_ceiling": link, "frac_of_link_ceiling": e2e_value / link["value"],
                     "api": "FastModel.upload_host -> compress -> payload copied to pinned host memory on its own "
                            "stream -> decompress_host(ordered=False) of the device payload, one host thread; step "
                            "i+1's upload and step i's downloads (payload, reconstruction) run on copy streams "
@@ -703,17 +885,27 @@ def run_b200(args):
             "bpp_per_input_value": total_payload * 8 / (world * x.numel()),
             "bpp_per_pixel": total_payload * 8 / (world * x.numel() / 3),
             "psnr_drop_db_vs_fp32": psnr_drop,
+            "quality_vs_fp32": quality,
             "precision_map": pmap,
             "ans": {
-                "encode_ms": enc_ms,
-                "decode_ms": dec_ms,
-                "encode_gbs": ans_bytes / (enc_ms / 1e3) / 1e9,
-                "decode_gbs": ans_bytes / (dec_ms / 1e3) / 1e9,
                 "bytes_per_call": ans_bytes,
+                "bytes_note": "algorithmic: 4 B per latent value (fp32 y read / y_hat written) + the payload",
                 "hbm_peak_gbs": hbm,
-                "encode_frac": ans_bytes / (enc_ms / 1e3) / 1e9 / hbm,
-                "decode_frac": ans_bytes / (dec_ms / 1e3) / 1e9 / hbm,
-                "note": "host-call times incl. launch and the one size read-back per encode",
+                "kernel": {
+                    "encode_ms": enc_kernel_ms, "pack_ms": pack_kernel_ms, "decode_ms": dec_kernel_ms,
+                    "encode_gbs": ans_bytes / ((enc_kernel_ms + pack_kernel_ms) / 1e3) / 1e9,
+                    "decode_gbs": ans_bytes / (dec_kernel_ms / 1e3) / 1e9,
+                    "encode_frac": ans_bytes / ((enc_kernel_ms + pack_kernel_ms) / 1e3) / 1e9 / hbm,
+                    "decode_frac": ans_bytes / (dec_kernel_ms / 1e3) / 1e9 / hbm,
+                    "note": "CUDA events around the kernels alone: encode (+ its status-word copy) and pack "
+                            "count together for encode; L2 flushed before each",
+                },
+                "host_call": {
+                    "encode_ms": enc_ms, "decode_ms": dec_ms,
+                    "encode_gbs": ans_bytes / (enc_ms / 1e3) / 1e9,
+                    "decode_gbs": ans_bytes / (dec_ms / 1e3) / 1e9,
+                    "note": "whole calls: launches, the encode's size read-back and its pack",
+                },
             },
             "layers_ms": {k: v["ms"] / v["n"] for k, v in per_layer.items()},
         }
@@ -721,6 +913,9 @@ def run_b200(args):
             cpu_model = build_model()
             res = time_cpu(cpu_model, args, steps=3, warmup=1)
             line["cpu_baseline"] = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            with torch.inference_mode():
+                line["cpu_baseline"]["gpu_fp32_transforms_cpu_rans"] = time_gpu_transforms_cpu_rans(
+                    build_model().to(dev), x, steps=3)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

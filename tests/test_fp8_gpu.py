@@ -174,9 +174,11 @@ def test_precision_map_through_accelerate(cuda_device, tmp_path):
     def psnr(a, b):
         return float(10 * torch.log10(1.0 / F.mse_loss(a.float(), b.float())))
 
-    assert abs(psnr(x_hat, x) - psnr(x_ref, x)) < 1.0
+    # the north star's gates (the same gates on latents that span the CDF
+    # tables: tests/test_quality_gpu.py)
+    assert psnr(x_ref, x) - psnr(x_hat, x) <= 0.1
     bpp = out["strings"][0].packed.numel() / out_ref["strings"][0].packed.numel()
-    assert 0.9 < bpp < 1.1
+    assert abs(bpp - 1.0) <= 0.01
     with pytest.raises(Exception, match="model fingerprint"):
         other = FactorizedPrior(128, 192).to(cuda_device)
         accelerate(other, P=4, device="cuda:0", precision_config_path=str(path))

@@ -187,6 +187,11 @@ def test_accelerate_bf16_end_to_end(cuda_device):
     assert _psnr(x_hat, x_ref) > 25.0, _psnr(x_hat, x_ref)
     drop = _psnr(x_ref, x) - _psnr(x_hat, x)
     assert drop <= 0.1, drop
+    # and its payload stays within 1% of the FP32 path's (bpp gate)
+    ref_fast = accelerate(model, P=4, device="cuda:0", transforms="fp32")
+    with torch.inference_mode():
+        ref_bytes = ref_fast.compress(x)["strings"][0].packed.numel()
+    assert abs(out["strings"][0].packed.numel() / ref_bytes - 1.0) <= 0.01
 
 
 @pytest.mark.parametrize("transforms", ["bf16", "fp32"])
