@@ -702,8 +702,11 @@ def run_b200(args):
             kv[0].record()
             pend = wd_ext.encode_latent_submit(y, med, cdfs, lengths, offs, args.p_ch)
             kv[1].record()
-            # the host waits for the size here, so kv[2] is recorded on an idle stream
+            # the host waits for the size here; the flush keeps the GPU busy
+            # while the host enqueues the pack, so kv[2] .. kv[3] brackets the
+            # pack kernel and not the host's launch latency
             torch.cuda.current_stream().synchronize()
+            flush.fill_(1.0)
             kv[2].record()
             r = wd_ext.encode_finish(pend)
             kv[3].record()

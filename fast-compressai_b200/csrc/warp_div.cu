@@ -10,23 +10,31 @@
 // r*32 + L) and every chunk is padded to the longest lane (max_rounds).
 //
 // Design (B200-first, not a translation of the reference):
-//  * encode is one persistent kernel: each warp codes one chunk at a time,
-//    with every CDF row of the batch staged once per CTA in shared memory as
-//    packed {start, freq-1} u32 entries.  Renormalisation words go to a
-//    transposed staging area [chunk][emission j][lane] so that both the
-//    lanes' writes and the later pack are 128-byte row accesses.  The last
-//    CTA to finish computes the chunk offsets (exclusive scan of
-//    max_rounds * 32) and a status block, so the host needs one small
-//    device-to-host read to size the payload.
-//  * pack writes each chunk's rounds as full 128-byte rows (coalesced), plus
-//    the header, in one kernel.
-//  * decode is a validation/scan kernel (header words, round table, length)
-//    followed by one persistent kernel whose CDF search starts from a
-//    128-bucket slot->symbol table per CDF row in shared memory, so a lookup
-//    is one table read plus (on average < 1) linear steps instead of a
-//    binary search over global memory.
-//  * all loops over payload words are bounded by the chunk's rounds and by
-//    the escape limit (<= 8 nibbles), so corrupt payloads raise an error
+//  * encode (channel layout: the codec's latent path and NULL indexes) is one
+//    persistent kernel, encode_lanes_kernel: a CTA stages one chunk group's
+//    P CDF rows in shared memory as 16-byte entries {division magic, freq,
+//    start}, and each warp codes one chunk of the group.  Symbols are read
+//    8 ahead; a batch in one channel reads its entries before its coder
+//    steps, and when no lane escapes and every lane has room each step is a
+//    fixed sequence (predicated renormalisation store, one 64-bit high
+//    multiply, a 32-bit remainder correction).  Renormalisation words go to
+//    a staging area [chunk][emission j][lane]; the last CTA to finish
+//    computes the chunk offsets (exclusive scan of max_rounds * 32) and a
+//    status block, so the host needs one small device-to-host read to size
+//    the payload.
+//  * pack reads each chunk's staging rows in emission order (128-byte rows)
+//    and writes every lane's words in decode order, plus the header.
+//  * decode (channel layout) is one persistent kernel, decode_lanes_kernel:
+//    the group's rows and a slot-bucket table (8-byte entries that resolve a
+//    bucket of one or two symbols without a search) in shared memory; each
+//    step reads one bucket entry, and the refill word is loaded one step
+//    ahead so the refill is a register move.  A validation/scan kernel runs
+//    first for payloads from elsewhere (header words, round table, length).
+//  * explicit indexes use full-table kernels (every row of the batch staged
+//    per CTA); rows that do not fit in shared memory are read from global
+//    memory by fallback kernels.
+//  * all reads of payload words are bounded by the chunk's rounds and by the
+//    escape limit (<= 8 nibbles), so corrupt payloads raise an error
 //    instead of reading out of bounds.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -79,14 +87,6 @@ constexpr uint32_t kBypassBits = 4;
 constexpr uint32_t kBypassMax = 15;
 constexpr int kLutShift = 9;              // decode LUT bucket = slot >> 9
 constexpr int kLutBuckets = 65536 >> kLutShift;
-// The chunk-group decode stages only its P rows, so its bucket table can be
-// finer: slot >> group_lut_shift(P), from 2048 buckets a row for P <= 4 (a
-// bucket then rarely holds more than one symbol, and the linear step after
-// the lookup rarely runs) to the 128 of the full table for P > 32; at most
-// 16 KB a CTA.
-__host__ __device__ inline int group_lut_shift(int P) {
-    return P <= 4 ? 5 : P <= 8 ? 6 : P <= 16 ? 7 : P <= 32 ? 8 : kLutShift;
-}
 constexpr int kMaxSymbolWords = 10;       // <= 8 nibbles + count + symbol puts
 constexpr int64_t kCtrlBytes = 256;
 constexpr int kMaxSmemBytes = 200 * 1024;
@@ -270,76 +270,6 @@ struct Tables {
         return lo;
     }
 };
-
-// Group accessor: the rows [c0, c0 + nc) of one chunk group in shared memory,
-// with the division magic of every entry (encode) or the slot buckets
-// (decode) and the medians of the latent modes.
-struct GroupTables {
-    const uint32_t *s_tab;  // [nc][Ls]
-    const uint64_t *s_mag;  // [nc][Ls] (encode)
-    const int2 *s_ch;       // [nc]
-    const uint16_t *s_lut;  // [nc][kLutBuckets] (decode)
-    const float *s_med;     // [nc] (latent modes)
-    int c0, Ls;
-    int lut_shift;          // bucket = slot >> lut_shift, 65536 >> lut_shift buckets a row
-
-    __device__ __forceinline__ int2 chan(int c) const { return s_ch[c - c0]; }
-    __device__ __forceinline__ uint32_t entry(int c, int v, uint32_t &) const { return s_tab[(c - c0) * Ls + v]; }
-    __device__ __forceinline__ uint64_t magic(int c, int v, uint32_t) const { return s_mag[(c - c0) * Ls + v]; }
-    __device__ __forceinline__ float median(int c) const { return s_med[c - c0]; }
-    __device__ __forceinline__ int search(int c, int maxv, uint32_t slot, uint32_t &ent, uint32_t &) const {
-        const int cl = c - c0;
-        int s = s_lut[(cl << (16 - lut_shift)) + (slot >> lut_shift)];
-        if (s > maxv) s = maxv;
-        const uint32_t *row = s_tab + cl * Ls;
-        uint32_t e = row[s];
-        while (s < maxv && (e & 0xFFFFu) + (e >> 16) + 1u <= slot) e = row[++s];
-        ent = e;
-        return s;
-    }
-};
-
-// Stages rows [c0, c0 + nc) (entries, {offset, maxv}, optional magic, slot
-// buckets and medians) and validates them.  Ends with __syncthreads().
-__device__ void stage_group(const TableArgs &t, int c0, int nc, uint32_t *s_tab, uint64_t *s_mag, int2 *s_ch,
-                            uint16_t *s_lut, float *s_med, const float *medians, uint32_t &flags, int lut_shift) {
-    const int buckets = 65536 >> lut_shift;
-    const int Ls = t.L - 1;
-    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
-        int32_t size = __ldg(t.sizes + c0 + c);
-        if (size < 2 || size > t.L) {
-            flags |= kFlagTable;
-            size = size < 2 ? 2 : t.L;
-        }
-        s_ch[c] = make_int2(__ldg(t.offs + c0 + c), size - 2);
-        if (s_med) s_med[c] = __ldg(medians + c0 + c);
-    }
-    __syncthreads();
-    const int total = nc * Ls;
-    for (int e = threadIdx.x; e < total; e += blockDim.x) {
-        const int c = e / Ls, v = e - c * Ls;
-        const int maxv = s_ch[c].y;
-        uint32_t ent = 0u;
-        if (v <= maxv) {
-            const int32_t *row = t.cdfs + (int64_t)(c0 + c) * t.L;
-            ent = pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
-            if (s_lut) {
-                const int lo = v == 0 ? 0 : (int)(ent & 0xFFFFu);
-                const int hi = v == maxv ? 65536 : (int)(ent & 0xFFFFu) + (int)(ent >> 16) + 1;
-                int u0 = (lo + (1 << lut_shift) - 1) >> lut_shift;
-                int u1 = (hi + (1 << lut_shift) - 1) >> lut_shift;
-                if (u1 > buckets) u1 = buckets;
-                for (int u = u0; u < u1; ++u) s_lut[c * buckets + u] = (uint16_t)v;
-            }
-        }
-        s_tab[e] = ent;
-        if (s_mag) {
-            const uint32_t freq = (ent >> 16) + 1u;  // entries of valid rows have freq in [1, 65536]
-            s_mag[e] = (~0ull) / (uint64_t)freq;
-        }
-    }
-    __syncthreads();
-}
 
 // ---------------------------------------------------------------------------
 // rANS primitives (rans64_gpu.cuh:21-55, rans64_gpu_v2.cuh:90-120 semantics)
@@ -684,56 +614,22 @@ __global__ void __launch_bounds__(kThreads) encode_kernel(EncParams p) {
     finish_encode(p, flags, my_max_used);
 }
 
-// Shared-memory layout of one chunk group (rows [c0, c0 + P)).
-struct GroupSmem {
-    int64_t mag, tab, ch, med, lut, bytes;
-};
-__host__ __device__ inline GroupSmem group_smem(int P, int L, bool encode) {
-    const int64_t ent = (int64_t)P * (L - 1);
-    GroupSmem g;
-    g.mag = 0;
-    g.tab = encode ? ent * 8 : 0;
-    g.ch = (g.tab + ent * 4 + 7) & ~7ll;
-    g.med = g.ch + (int64_t)P * 8;
-    g.lut = (g.med + (int64_t)P * 4 + 7) & ~7ll;
-    g.bytes = g.lut + (encode ? 0 : (int64_t)P * (65536 >> group_lut_shift(P)) * 2);
-    return g;
-}
-
-// Channel-layout indexes: chunk k only uses rows [k*P, k*P + P).  A CTA of
-// W warps takes groups (k, images b0 .. b0+W-1); it stages just those rows,
-// with every entry's division magic, so a symbol costs shared-memory reads
-// only.
-template <int kMode, bool kSmem>
+// Channel-layout indexes with the CDF rows read from global memory: the
+// fallback of encode_lanes_kernel when a chunk group's rows do not fit in
+// shared memory.  A CTA of W warps takes groups (k, images b0 .. b0+W-1).
+template <int kMode>
 __global__ void __launch_bounds__(kThreads) encode_group_kernel(EncParams p) {
-    extern __shared__ __align__(16) unsigned char smem[];
     uint32_t flags = 0;
     unsigned int my_max_used = 0;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
     const int nbb = (p.B + W - 1) / W;
     const int64_t groups = (int64_t)p.K * nbb;
-    const GroupSmem gs = group_smem(p.P, p.t.L, true);
-    GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), reinterpret_cast<const uint64_t *>(smem + gs.mag),
-                   reinterpret_cast<const int2 *>(smem + gs.ch), nullptr, reinterpret_cast<const float *>(smem + gs.med),
-                   0, p.t.L - 1, kLutShift};
     Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
-    if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
+    if (blockIdx.x == 0) validate_tables_global(p.t, flags);
     for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
         const int k = (int)(g % p.K), bb = (int)(g / p.K);
-        if (kSmem) {
-            const int c0 = k * p.P, nc = min(p.P, p.t.C - c0);
-            __syncthreads();  // the previous group's rows are no longer read
-            stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), reinterpret_cast<uint64_t *>(smem + gs.mag),
-                        reinterpret_cast<int2 *>(smem + gs.ch), nullptr,
-                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags,
-                        kLutShift);
-            gt.c0 = c0;
-        }
         const int b = bb * W + warp;
-        if (b < p.B) {
-            if (kSmem) encode_chunk<kMode>(p, gt, (int64_t)b * p.K + k, lane, flags, my_max_used);
-            else encode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags, my_max_used);
-        }
+        if (b < p.B) encode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags, my_max_used);
     }
     finish_encode(p, flags, my_max_used);
 }
@@ -750,51 +646,6 @@ struct PackParams {
     int64_t packed_bytes;
     uint8_t *packed;
 };
-
-__global__ void __launch_bounds__(kThreads) pack_kernel(PackParams p) {
-    const long long total_words = p.ctrl->status[kStTotalWords];
-    const int rows_cap = (int)p.ctrl->status[kStRowsCap];
-    if (p.header_bytes + 4 * (int64_t)total_words != p.packed_bytes) return;  // not the last encode's size
-    uint32_t *hdr = reinterpret_cast<uint32_t *>(p.packed);
-    if (blockIdx.x == 0 && threadIdx.x < 8) {
-        uint32_t h = 0;
-        switch (threadIdx.x) {
-            case 0: h = (uint32_t)p.N; break;
-            case 1: h = (uint32_t)p.chunk_len; break;
-            case 2: h = ((uint32_t)p.K & 0xFFFFu) | (((uint32_t)p.B & 0xFFFFu) << 16); break;
-            case 3: h = 2u | (32u << 16); break;
-            default: h = 0u;
-        }
-        hdr[threadIdx.x] = h;
-    }
-    // zero the pad between the round table and header_bytes (<= 12 bytes)
-    const int64_t table_end = 32 + 4 * p.chunks;
-    if (blockIdx.x == 0 && threadIdx.x >= 8 && threadIdx.x < 8 + (p.header_bytes - table_end) / 4)
-        hdr[table_end / 4 + (threadIdx.x - 8)] = 0u;
-    const int lane = threadIdx.x & 31;
-    uint32_t *body = reinterpret_cast<uint32_t *>(p.packed + p.header_bytes);
-    const int warps = blockDim.x >> 5;
-    const int64_t warp_stride = (int64_t)gridDim.x * warps;
-    for (int64_t chunk = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); chunk < p.chunks; chunk += warp_stride) {
-        const int rounds = p.rounds[chunk];
-        int used = p.used[chunk * kLanes + lane];
-        if (used > rows_cap) used = 0;  // overflowed staging: never packed by the host
-        if (lane == 0) hdr[8 + chunk] = (uint32_t)rounds;
-        const uint32_t *st = p.stage + chunk * (int64_t)rows_cap * kLanes + lane;
-        uint32_t *out = body + p.offsets[chunk] + lane;
-        // eight rounds at a time, their loads issued before the stores, so
-        // a warp has eight independent loads in flight instead of one
-        int r = 0;
-        for (; r + 8 <= rounds; r += 8) {
-            uint32_t v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = r + i < used ? __ldcs(st + (int64_t)(used - 1 - r - i) * kLanes) : 0u;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) out[(int64_t)(r + i) * kLanes] = v[i];
-        }
-        for (; r < rounds; ++r) out[(int64_t)r * kLanes] = r < used ? st[(int64_t)(used - 1 - r) * kLanes] : 0u;
-    }
-}
 
 // ---------------------------------------------------------------------------
 // Decode
@@ -1082,15 +933,565 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(DecParams p) {
     finish_decode(p, flags);
 }
 
-// Channel-layout indexes: chunk groups with only their rows (and slot
-// buckets) staged, as in encode_group_kernel.
-template <int kMode, bool kSmem>
+// Channel-layout indexes with the CDF rows read from global memory: the
+// fallback of decode_lanes_kernel when a group's rows do not fit in shared
+// memory.
+template <int kMode>
 __global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
+    __shared__ int s_skip;
+    uint32_t flags = 0;
+    if (threadIdx.x == 0) s_skip = decode_skip(p) ? 1 : 0;
+    __syncthreads();
+    const bool skip = s_skip != 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int nbb = (p.B + W - 1) / W;
+    const int64_t groups = (int64_t)p.K * nbb;
+    Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
+    if (blockIdx.x == 0) validate_tables_global(p.t, flags);
+    for (int64_t g = blockIdx.x; g < groups && !skip; g += gridDim.x) {
+        const int k = (int)(g % p.K), bb = (int)(g / p.K);
+        const int b = bb * W + warp;
+        if (b < p.B) decode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags);
+    }
+    finish_decode(p, flags);
+}
+
+// ---------------------------------------------------------------------------
+// Chunk-group coder with per-symbol chains free of divergent branches
+// ---------------------------------------------------------------------------
+// The group kernels above resolve each symbol with table searches and a
+// look-ahead word queue whose refills branch per lane, so a warp executes
+// both sides of every renormalisation and search.  These kernels keep the
+// same decomposition (a CTA stages one chunk group's P rows, each warp codes
+// one chunk) and the same arithmetic, but every step of a symbol is a fixed
+// instruction sequence:
+//  * encode reads one 16-byte entry {magic lo, magic hi, freq, start} per
+//    symbol; the renormalisation word is a predicated store; the quotient
+//    estimate floor(x * magic / 2^64) is q or q - 1 and the remainder fits
+//    in 32 bits, so the correction is one compare on 32-bit values;
+//  * decode reads one 8-byte bucket entry {entry of the bucket's first
+//    symbol, first | last symbol of the bucket} per symbol: a bucket that
+//    holds one symbol (nearly every lookup) needs no search.  The refill
+//    word is a candidate loaded one symbol ahead, so the refill itself is a
+//    predicated register move; rows of the lane's stream are prefetched into
+//    L1 a few words ahead.
+// Channel-dependent values (row pointers, offset, escape symbol, median)
+// change only when a lane crosses into the next channel.
+
+// Shared-memory layout of one group's rows for the lanes kernels.
+struct LanesSmem {
+    int64_t ent, chan, lut, bytes;
+    int lut_shift;  // decode: bucket = slot >> lut_shift
+};
+
+// Decode buckets per row: the largest power of two in [32, 2048] with
+// P * buckets <= 8192 (64 KB of 8-byte entries).
+__host__ __device__ inline int lanes_lut_shift(int P) {
+    int shift = 5;
+    while (shift < 11 && (int64_t)(65536 >> shift) * P > 8192) ++shift;
+    return shift;
+}
+
+__host__ __device__ inline LanesSmem lanes_smem(int P, int L, bool encode) {
+    const int64_t ents = (int64_t)P * (L - 1);
+    LanesSmem s;
+    s.ent = 0;
+    s.chan = (ents * (encode ? 16 : 4) + 15) & ~15ll;
+    s.lut = s.chan + (int64_t)P * 16;
+    s.lut_shift = lanes_lut_shift(P);
+    s.bytes = s.lut + (encode ? 0 : (int64_t)P * (65536 >> s.lut_shift) * 8);
+    return s;
+}
+
+// First symbol s in [0, maxv] whose range reaches slot (end(s) - 1 >= slot),
+// maxv if none: the reference's warp_cdf_find_symbol (warp_ans_kernel.cu:
+// 28-39) over decode entries start | (end - 1) << 16.
+__device__ __forceinline__ int lanes_find(const uint32_t *row, int lo, int hi, uint32_t slot) {
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((row[mid] >> 16) >= slot) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+// Stages rows [c0, c0 + nc): channel info {median bits, offset, maxv}, the
+// per-symbol entries and (decode) the slot buckets.  Ends with a barrier.
+//
+// Decode bucket u of a row covers slots [u << shift, (u + 1) << shift).  Its
+// 8-byte entry holds the decode entry of s0, the symbol of the bucket's
+// first slot (the first symbol also owns the slots below cdf[0], the last
+// one those above cdf[size - 1]), and in its high word either
+//  * kPair: end(s0 + 1) - 1 | s0 << 16, so that a slot past s0's range
+//    resolves to s0 + 1 without another read; a slot past that one too (a
+//    bucket of three or more symbols) is searched in [s0 + 2, maxv];
+//  * otherwise: s0 | s1 << 16, s1 the symbol of the bucket's last slot, so
+//    that a slot past s0's range is searched in (s0, s1].
+// Each thread fills a run of consecutive buckets of one row, walking the
+// row's symbols forward, so a row costs its buckets plus its symbols.
+template <bool kPair>
+__device__ void stage_lanes(const TableArgs &t, int c0, int nc, bool encode, unsigned char *smem,
+                            const LanesSmem &ls, const float *medians, uint32_t &flags) {
+    const int Ls = t.L - 1;
+    int4 *chan = reinterpret_cast<int4 *>(smem + ls.chan);
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        int32_t size = __ldg(t.sizes + c0 + c);
+        if (size < 2 || size > t.L) {
+            flags |= kFlagTable;
+            size = size < 2 ? 2 : t.L;
+        }
+        chan[c] = make_int4(medians ? __float_as_int(__ldg(medians + c0 + c)) : 0, __ldg(t.offs + c0 + c), size - 2, 0);
+    }
+    __syncthreads();
+    const int total = nc * Ls;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        const int c = e / Ls, v = e - c * Ls;
+        uint32_t start = 0u, freq = 1u;
+        if (v <= chan[c].z) {
+            const int32_t *row = t.cdfs + (int64_t)(c0 + c) * t.L;
+            const uint32_t ent = pack_entry(__ldg(row + v), __ldg(row + v + 1), flags);
+            start = ent & 0xFFFFu;
+            freq = (ent >> 16) + 1u;
+        }
+        if (encode) {
+            const uint64_t m = (~0ull) / (uint64_t)freq;
+            reinterpret_cast<uint4 *>(smem + ls.ent)[e] = make_uint4((uint32_t)m, (uint32_t)(m >> 32), freq, start);
+        } else {
+            reinterpret_cast<uint32_t *>(smem + ls.ent)[e] = start | ((start + freq - 1u) << 16);
+        }
+    }
+    __syncthreads();
+    if (encode) return;
+    const uint32_t *ent = reinterpret_cast<const uint32_t *>(smem + ls.ent);
+    uint2 *lut = reinterpret_cast<uint2 *>(smem + ls.lut);
+    const int shift = ls.lut_shift, buckets = 65536 >> shift;
+    const int64_t all = (int64_t)nc * buckets;
+    const int64_t per = (all + blockDim.x - 1) / blockDim.x;
+    const int64_t i0 = (int64_t)threadIdx.x * per, i1 = min(all, i0 + per);
+    int c = -1, maxv = 0, s = 0;
+    const uint32_t *row = ent;
+    for (int64_t i = i0; i < i1; ++i) {
+        const int ci = (int)(i >> (16 - shift)), u = (int)(i & (buckets - 1));
+        const uint32_t first = (uint32_t)u << shift, last = first + (1u << shift) - 1u;
+        if (ci != c) {  // a new row: search the first bucket's symbol
+            c = ci;
+            maxv = chan[c].z;
+            row = ent + c * Ls;
+            s = lanes_find(row, 0, maxv, first);
+        }
+        while (s < maxv && (row[s] >> 16) < first) ++s;
+        const int s0 = s;
+        while (s < maxv && (row[s] >> 16) < last) ++s;
+        const uint32_t hi = kPair ? ((s0 < maxv ? row[s0 + 1] >> 16 : 0xFFFFu) | ((uint32_t)s0 << 16))
+                                  : ((uint32_t)s0 | ((uint32_t)s << 16));
+        lut[i] = make_uint2(row[s0], hi);
+    }
+    __syncthreads();
+}
+
+// One coder step of the encode (Rans64EncPutV2 semantics,
+// rans64_gpu_v2.cuh:35-65): the renormalisation word is a predicated store,
+// and floor(x * magic / 2^64) is floor(x / freq) or one less (x < 2^63
+// after renormalisation), so the remainder is below 2 * freq and its low 32
+// bits are exact.  kCheck bounds the staging store by the lane's capacity.
+template <bool kCheck>
+__device__ __forceinline__ void enc_step(uint64_t &x, int &j, uint32_t *__restrict__ wrow, int cap, const uint4 e) {
+    const uint32_t freq = e.z;
+    uint32_t xl = (uint32_t)x, xh = (uint32_t)(x >> 32);
+    const bool rn = xh >= (freq << 15);  // x >= ((L >> 16) << 32) * freq
+    if (rn && (!kCheck || j < cap)) wrow[(int64_t)j * kLanes] = xl;
+    j += rn ? 1 : 0;
+    xl = rn ? xh : xl;
+    xh = rn ? 0u : xh;
+    uint64_t q = __umul64hi(((uint64_t)xh << 32) | xl, ((uint64_t)e.y << 32) | e.x);
+    uint32_t r = xl - (uint32_t)q * freq;
+    const bool c = r >= freq;
+    q += c ? 1u : 0u;
+    r -= c ? freq : 0u;
+    x = (q << 16) + (uint64_t)(r + e.w);
+}
+
+// Escape code (bypass nibbles) of an out-of-range value, from the value
+// and its channel's escape symbol maxv: negative v gives raw = -2v - 1,
+// v >= maxv gives raw = 2(v - maxv) (warp_ans_kernel_v2.cu:148-164).
+__device__ __forceinline__ uint32_t escape_raw(int32_t value, int32_t maxv) {
+    return value < 0 ? 0u - 2u * (uint32_t)value - 1u : ((uint32_t)value - (uint32_t)maxv) * 2u;
+}
+
+// Encodes one chunk: each lane runs its symbols last to first, in batches
+// of 8 whose symbols are loaded one batch ahead.  A batch whose symbols lie
+// in one channel (every batch when HW is a multiple of 256) takes the fast
+// path: its table entries are read before its coder steps, and when no lane
+// of the warp escapes and every lane has room for 8 more words the steps
+// have no per-symbol checks.  Other batches, the ragged end and escapes go
+// through the checked per-symbol path.
+template <int kMode>
+__device__ __forceinline__ void encode_lanes(const EncParams &p, const uint4 *__restrict__ ent,
+                                             const int4 *__restrict__ chan, int c0, int Ls, int64_t chunk, int lane,
+                                             uint32_t &flags, unsigned int &my_max_used) {
+    constexpr int kB = 8, kH = 4;
+    const int b = (int)(chunk / p.K);
+    const int k = (int)(chunk - (int64_t)b * p.K);
+    const int start = k * p.chunk_len;
+    const int end = min(start + p.chunk_len, p.N);
+    const int first = start + lane;
+    uint32_t *const wrow = p.stage + chunk * (int64_t)p.rows_cap * kLanes + lane;
+    const int cap = p.rows_cap;
+    int j = 0;
+    const int n = first < end ? (end - 1 - first) / kLanes + 1 : 0;
+    // every lane runs the same number of batches (the warp's longest), so
+    // that the warp votes below always see all 32 lanes; a lane past its
+    // own symbols takes the guarded path and does nothing
+    int nmax = n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
+    {
+        const int last = first + (max(n, 1) - 1) * kLanes;
+        int ct = n > 0 ? last / p.HW : c0, rem = n > 0 ? last - ct * p.HW : 0;
+        int4 ch = chan[ct - c0];
+        const uint4 *row = ent + (ct - c0) * Ls;
+        const int64_t pos_last = (int64_t)b * p.N + last;
+        const int32_t *src = kMode == kModeLatent ? reinterpret_cast<const int32_t *>(p.y) + pos_last : p.sym + pos_last;
+        uint64_t x = kRansL;
+        int32_t cur[kB], nxt[kB];
+#pragma unroll
+        for (int u = 0; u < kB; ++u) cur[u] = u < n ? __ldg(src - u * kLanes) : 0;
+        for (int t0 = 0; t0 < nmax; t0 += kB) {
+            if (t0 + 2 * kB <= n) {
+#pragma unroll
+                for (int u = 0; u < kB; ++u) nxt[u] = __ldg(src - (t0 + kB + u) * kLanes);
+            } else {
+#pragma unroll
+                for (int u = 0; u < kB; ++u) nxt[u] = t0 + kB + u < n ? __ldg(src - (t0 + kB + u) * kLanes) : 0;
+            }
+            // this lane's symbols t0 .. t0 + 7 all lie in channel ct when the
+            // position of the 8th is still at or above the channel's start
+            const bool one_channel = t0 + kB <= n && rem >= (kB - 1) * kLanes;
+            if (__all_sync(0xffffffffu, one_channel)) {
+                const int32_t off = ch.y, maxv = ch.z;
+                // two halves of four: a half's entries are read before its
+                // coder steps (fewer live registers than a batch of eight)
+#pragma unroll
+                for (int h = 0; h < kB; h += kH) {
+                    uint4 e[kH];
+                    int32_t val[kH];
+                    uint32_t esc = 0u;
+#pragma unroll
+                    for (int u = 0; u < kH; ++u) {
+                        int32_t s;
+                        if (kMode == kModeLatent) s = __float2int_rn(__int_as_float(cur[h + u]) - __int_as_float(ch.x));
+                        else s = cur[h + u];
+                        val[u] = (int32_t)((uint32_t)s - (uint32_t)off);
+                        const bool oor = (uint32_t)val[u] >= (uint32_t)maxv;  // value < 0 or value >= maxv
+                        esc |= oor ? 1u << u : 0u;
+                        e[u] = row[oor ? maxv : val[u]];
+                    }
+                    if (__all_sync(0xffffffffu, esc == 0u && j + kH <= cap)) {
+#pragma unroll
+                        for (int u = 0; u < kH; ++u) enc_step<false>(x, j, wrow, cap, e[u]);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < kH; ++u) {
+                            if (esc & (1u << u)) {
+                                const EscOut r = put_escape_call(x, escape_raw(val[u], maxv), wrow, cap, j);
+                                x = r.x;
+                                j = r.j;
+                            }
+                            enc_step<true>(x, j, wrow, cap, e[u]);
+                        }
+                    }
+                }
+                rem -= kB * kLanes;
+                if (rem < 0 && t0 + kB < n) {
+                    do {
+                        rem += p.HW;
+                        --ct;
+                    } while (rem < 0);
+                    ch = chan[ct - c0];
+                    row = ent + (ct - c0) * Ls;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < kB; ++u) {
+                    if (t0 + u >= n) break;
+                    int32_t s;
+                    if (kMode == kModeLatent) s = __float2int_rn(__int_as_float(cur[u]) - __int_as_float(ch.x));
+                    else s = cur[u];
+                    const int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.y);
+                    const bool oor = (uint32_t)value >= (uint32_t)ch.z;
+                    if (oor) {
+                        const EscOut r = put_escape_call(x, escape_raw(value, ch.z), wrow, cap, j);
+                        x = r.x;
+                        j = r.j;
+                    }
+                    enc_step<true>(x, j, wrow, cap, row[oor ? ch.z : value]);
+                    if (t0 + u + 1 < n) {  // step to the next symbol's channel only when one follows
+                        rem -= kLanes;
+                        if (rem < 0) {
+                            do {
+                                rem += p.HW;
+                                --ct;
+                            } while (rem < 0);
+                            ch = chan[ct - c0];
+                            row = ent + (ct - c0) * Ls;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kB; ++u) cur[u] = nxt[u];
+        }
+        // flush: the decoder reads the low word first
+        if (n > 0) {
+            if (j < cap) wrow[(int64_t)j * kLanes] = (uint32_t)(x >> 32);
+            ++j;
+            if (j < cap) wrow[(int64_t)j * kLanes] = (uint32_t)x;
+            ++j;
+        }
+    }
+    int rounds = j;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, o));
+    p.used[chunk * kLanes + lane] = j;
+    if (lane == 0) {
+        p.rounds[chunk] = rounds;
+        p.max_rounds_out[chunk] = (uint32_t)rounds;
+    }
+    if ((unsigned)rounds > my_max_used) my_max_used = (unsigned)rounds;
+}
+
+// Three CTAs of eight warps per SM (at most 85 registers a thread), so that
+// a batch of 64 images at P_ch = 4 (384 groups) runs in one wave.
+template <int kMode>
+__global__ void __launch_bounds__(kThreads, 3) encode_lanes_kernel(EncParams p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint32_t flags = 0;
+    unsigned int my_max_used = 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int nbb = (p.B + W - 1) / W;
+    const int64_t groups = (int64_t)p.K * nbb;
+    const LanesSmem ls = lanes_smem(p.P, p.t.L, true);
+    const uint4 *ent = reinterpret_cast<const uint4 *>(smem + ls.ent);
+    const int4 *chan = reinterpret_cast<const int4 *>(smem + ls.chan);
+    for (int64_t g = blockIdx.x; g < groups; g += gridDim.x) {
+        const int k = (int)(g % p.K), bb = (int)(g / p.K);
+        const int c0 = k * p.P, nc = min(p.P, p.t.C - c0);
+        __syncthreads();  // the previous group's rows are no longer read
+        stage_lanes<false>(p.t, c0, nc, true, smem, ls, kMode == kModeLatent ? p.medians : nullptr, flags);
+        const int b = bb * W + warp;
+        if (b < p.B) encode_lanes<kMode>(p, ent, chan, c0, p.t.L - 1, (int64_t)b * p.K + k, lane, flags, my_max_used);
+    }
+    finish_encode(p, flags, my_max_used);
+}
+
+// One decode step (warp_ans_kernel.cu:219-329 semantics): the bucket of the
+// slot names the symbol unless the slot lies past the bucket's first
+// symbol, then a binary search over the rest of the bucket finds it.  The
+// refill word is `cand`, loaded during the previous step; reads are clamped
+// to the chunk's last round.
+struct DecLane {
+    uint64_t x;
+    int word;
+    uint32_t cand;
+};
+
+template <bool kPair>
+__device__ __forceinline__ int32_t dec_step(DecLane &d, const uint2 *__restrict__ lrow, const uint32_t *__restrict__ row,
+                                            int shift, int maxv, const uint32_t *__restrict__ base, int rm1) {
+    const uint32_t slot = (uint32_t)d.x & 0xFFFFu;
+    const uint2 le = lrow[slot >> shift];
+    int32_t s;
+    uint32_t st, endm1;
+    if (kPair) {
+        const uint32_t end0 = le.x >> 16;
+        const bool more = slot > end0;
+        s = (int32_t)(le.y >> 16) + (more ? 1 : 0);
+        st = more ? end0 + 1u : (le.x & 0xFFFFu);
+        endm1 = more ? (le.y & 0xFFFFu) : end0;
+        if (more && slot > endm1) {  // three or more symbols in the bucket (or s0 is the last symbol)
+            s = lanes_find(row, (int)(le.y >> 16), maxv, slot);
+            const uint32_t e = row[s];
+            st = e & 0xFFFFu;
+            endm1 = e >> 16;
+        }
+    } else {
+        uint32_t e = le.x;
+        s = (int32_t)(le.y & 0xFFFFu);
+        if (slot > (e >> 16)) {  // past the bucket's first symbol: search the rest of it
+            s = lanes_find(row, s + 1, (int)(le.y >> 16), slot);
+            e = row[s];
+        }
+        st = e & 0xFFFFu;
+        endm1 = e >> 16;
+    }
+    const uint32_t freq = endm1 - st + 1u;
+    d.x = (uint64_t)freq * (d.x >> 16) + (uint64_t)(int64_t)(int32_t)(slot - st);
+    const bool need = d.x < kRansL;
+    d.x = need ? (d.x << 32) | (uint64_t)d.cand : d.x;
+    d.word += need ? 1 : 0;
+    d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+    return s;
+}
+
+// Escape decode inlined into the decode loop (warp_ans_kernel.cu:308-325):
+// the count nibbles, then the value nibbles low to high.  Words are read
+// straight from the lane's stream, bounded by its rounds; returns false on
+// a corrupt stream (more than 8 value nibbles, or words past the rounds).
+__device__ __forceinline__ bool dec_escape(DecLane &d, const uint32_t *__restrict__ base, int rounds, int32_t maxv,
+                                           int32_t &value) {
+    bool bad = false;
+    auto nibble = [&]() -> uint32_t {
+        const uint32_t v = (uint32_t)d.x & kBypassMax;
+        d.x >>= kBypassBits;
+        if (d.x < kRansL) {
+            uint32_t w = 0u;
+            if (d.word < rounds) w = __ldg(base + (int64_t)d.word * kLanes);
+            else bad = true;
+            ++d.word;
+            d.x = (d.x << 32) | (uint64_t)w;
+        }
+        return v;
+    };
+    uint32_t v = nibble();
+    uint32_t n_bypass = v;
+    while (v == kBypassMax && !bad && n_bypass <= 8u) {
+        v = nibble();
+        n_bypass += v;
+    }
+    if (n_bypass > 8u || bad) return false;
+    uint32_t raw = 0;
+    for (uint32_t i = 0; i < n_bypass; ++i) raw |= nibble() << (i * kBypassBits);
+    int32_t val = (int32_t)raw >> 1;  // int32 arithmetic shift, as in the reference
+    if (raw & 1u) val = -val - 1;
+    else val = (int32_t)((uint32_t)val + (uint32_t)maxv);
+    value = val;
+    return !bad;
+}
+
+// Decodes one chunk: each lane reads its state, then its symbols first to
+// last, four at a time.  A group of four symbols in one channel (every
+// group when HW is a multiple of 128) has no channel bookkeeping; the ragged
+// end and groups that cross a channel step per symbol.  A lane that
+// consumes more words than its chunk holds marks the payload corrupt.
+template <int kMode, bool kPair>
+__device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t *__restrict__ ent,
+                                             const int4 *__restrict__ chan, const uint2 *__restrict__ lut, int shift,
+                                             int c0, int Ls, int64_t chunk, int lane, uint32_t &flags) {
+    constexpr int kG = 4;
+    const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
+    const int b = (int)(chunk / p.K);
+    const int k = (int)(chunk - (int64_t)b * p.K);
+    const int64_t start64 = (int64_t)k * p.chunk_len;
+    if (start64 >= p.N) return;
+    const int start = (int)start64;
+    const int end = (int)min(start64 + p.chunk_len, (int64_t)p.N);
+    uint64_t off;
+    if (p.offsets) {
+        off = p.offsets[chunk];
+    } else {
+        uint64_t sum = 0;
+        for (int64_t c = lane; c < chunk; c += kLanes) sum += (uint64_t)__ldg(p.max_rounds + c);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        off = sum * kLanes;
+    }
+    const int rounds = (int)__ldg(p.max_rounds + chunk);
+    if (rounds < 2 || rounds > 0x7fffffff - 8) {
+        flags |= kFlagCorrupt;
+        return;
+    }
+    const int first = start + lane;
+    const int n = first < end ? (end - 1 - first) / kLanes + 1 : 0;
+    const uint32_t *base = body + off + lane;
+    const int rm1 = rounds - 1;
+    // the chunk's stream into L2, one row per lane and step
+    for (int r = lane; r < rounds; r += kLanes) asm volatile("prefetch.global.L2 [%0];" ::"l"(body + off + (int64_t)r * kLanes));
+    // every lane runs the same number of groups (the warp's longest), so
+    // that the warp votes below always see all 32 lanes; a lane past its
+    // own symbols takes the guarded path and does nothing
+    int nmax = n;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
+    if (nmax == 0) return;
+    DecLane d;
+    d.x = (uint64_t)__ldg(base) | ((uint64_t)__ldg(base + kLanes) << 32);
+    d.word = 2;
+    d.cand = __ldg(base + (int64_t)min(2, rm1) * kLanes);
+    int ct = n > 0 ? first / p.HW : c0, rem = n > 0 ? first - ct * p.HW : 0;
+    int4 ch = chan[ct - c0];
+    const uint32_t *row = ent + (ct - c0) * Ls;
+    const uint2 *lrow = lut + (int64_t)(ct - c0) * (65536 >> shift);
+    const int64_t pos0 = (int64_t)b * p.N + first;
+    int32_t *orow = kMode == kModeLatent ? nullptr : p.out + pos0;
+    float *yrow = kMode == kModeLatent ? p.y_out + pos0 : nullptr;
+    bool bad = false;
+    auto finish_symbol = [&](int32_t s, int t) {
+        const bool esc = s == ch.z;
+        if (__any_sync(0xffffffffu, esc)) {  // some lane escapes: its value follows as bypass nibbles
+            if (esc) {
+                bad |= !dec_escape(d, base, rounds, ch.z, s);
+                d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+            }
+        }
+        const int32_t sym = (int32_t)((uint32_t)s + (uint32_t)ch.y);
+        if (kMode == kModeLatent) yrow[(int64_t)t * kLanes] = __int2float_rn(sym) + __int_as_float(ch.x);
+        else orow[(int64_t)t * kLanes] = sym;
+    };
+    auto finish_symbol_guarded = [&](int32_t s, int t, bool live) {
+        const bool esc = live && s == ch.z;
+        if (__any_sync(0xffffffffu, esc)) {
+            if (esc) {
+                bad |= !dec_escape(d, base, rounds, ch.z, s);
+                d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+            }
+        }
+        if (live) {
+            const int32_t sym = (int32_t)((uint32_t)s + (uint32_t)ch.y);
+            if (kMode == kModeLatent) yrow[(int64_t)t * kLanes] = __int2float_rn(sym) + __int_as_float(ch.x);
+            else orow[(int64_t)t * kLanes] = sym;
+        }
+    };
+    auto next_channel = [&]() {
+        do {
+            rem -= p.HW;
+            ++ct;
+        } while (rem >= p.HW);
+        ch = chan[ct - c0];
+        row = ent + (ct - c0) * Ls;
+        lrow = lut + (int64_t)(ct - c0) * (65536 >> shift);
+    };
+    for (int t = 0; t < nmax; t += kG) {
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(base + (int64_t)min(d.word + 6, rm1) * kLanes));
+        const bool one_channel = t + kG <= n && rem + (kG - 1) * kLanes < p.HW;
+        if (__all_sync(0xffffffffu, one_channel)) {
+#pragma unroll
+            for (int u = 0; u < kG; ++u) finish_symbol(dec_step<kPair>(d, lrow, row, shift, ch.z, base, rm1), t + u);
+            rem += kG * kLanes;
+            if (rem >= p.HW && t + kG < n) next_channel();
+        } else {
+            // lanes past their last symbol keep voting but do nothing
+#pragma unroll
+            for (int u = 0; u < kG; ++u) {
+                const bool live = t + u < n;
+                int32_t s = 0;
+                if (live) s = dec_step<kPair>(d, lrow, row, shift, ch.z, base, rm1);
+                finish_symbol_guarded(s, t + u, live);
+                if (live) {
+                    rem += kLanes;
+                    if (rem >= p.HW && t + u + 1 < n) next_channel();
+                }
+            }
+        }
+    }
+    if (n > 0 && (bad || d.word > rounds)) flags |= kFlagCorrupt;
+}
+
+template <int kMode, bool kPair>
+__global__ void __launch_bounds__(kThreads) decode_lanes_kernel(DecParams p) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_skip;
     uint32_t flags = 0;
-    // one read for the whole CTA: the loop below has barriers, so every
-    // thread must take the same number of iterations
     if (threadIdx.x == 0) s_skip = decode_skip(p) ? 1 : 0;
     __syncthreads();
     const bool skip = s_skip != 0;
@@ -1098,30 +1499,83 @@ __global__ void __launch_bounds__(kThreads) decode_group_kernel(DecParams p) {
     const int P = p.chunk_len / p.HW;
     const int nbb = (p.B + W - 1) / W;
     const int64_t groups = (int64_t)p.K * nbb;
-    const GroupSmem gs = group_smem(P, p.t.L, false);
-    GroupTables gt{reinterpret_cast<const uint32_t *>(smem + gs.tab), nullptr, reinterpret_cast<const int2 *>(smem + gs.ch),
-                   reinterpret_cast<const uint16_t *>(smem + gs.lut), reinterpret_cast<const float *>(smem + gs.med), 0,
-                   p.t.L - 1, group_lut_shift(P)};
-    Tables<false> tg{nullptr, nullptr, nullptr, p.t, p.medians};
-    if (!kSmem && blockIdx.x == 0) validate_tables_global(p.t, flags);
+    const LanesSmem ls = lanes_smem(P, p.t.L, false);
+    const uint32_t *ent = reinterpret_cast<const uint32_t *>(smem + ls.ent);
+    const int4 *chan = reinterpret_cast<const int4 *>(smem + ls.chan);
+    const uint2 *lut = reinterpret_cast<const uint2 *>(smem + ls.lut);
     for (int64_t g = blockIdx.x; g < groups && !skip; g += gridDim.x) {
         const int k = (int)(g % p.K), bb = (int)(g / p.K);
-        if (kSmem) {
-            const int c0 = min(k * P, p.t.C), nc = max(0, min(P, p.t.C - c0));
-            __syncthreads();
-            stage_group(p.t, c0, nc, reinterpret_cast<uint32_t *>(smem + gs.tab), nullptr,
-                        reinterpret_cast<int2 *>(smem + gs.ch), reinterpret_cast<uint16_t *>(smem + gs.lut),
-                        kMode == kModeLatent ? reinterpret_cast<float *>(smem + gs.med) : nullptr, p.medians, flags,
-                        group_lut_shift(P));
-            gt.c0 = c0;
-        }
+        const int c0 = min(k * P, p.t.C), nc = max(0, min(P, p.t.C - c0));
+        __syncthreads();
+        stage_lanes<kPair>(p.t, c0, nc, false, smem, ls, kMode == kModeLatent ? p.medians : nullptr, flags);
+        // an invalid row leaves buckets unfilled: decode nothing (the table
+        // error is reported)
+        if (__syncthreads_or((int)(flags & kFlagTable))) continue;
         const int b = bb * W + warp;
-        if (b < p.B) {
-            if (kSmem) decode_chunk<kMode>(p, gt, (int64_t)b * p.K + k, lane, flags);
-            else decode_chunk<kMode>(p, tg, (int64_t)b * p.K + k, lane, flags);
-        }
+        if (b < p.B)
+            decode_lanes<kMode, kPair>(p, ent, chan, lut, ls.lut_shift, c0, p.t.L - 1, (int64_t)b * p.K + k, lane,
+                                       flags);
     }
     finish_decode(p, flags);
+}
+
+// Pack with coalesced reads: a warp reads its chunk's staging rows in
+// emission order, 128 bytes a row, and each lane stores word j of its
+// stream at row used - 1 - j of the payload (its decode order); rows from
+// used to max_rounds hold zeros.  Stores scatter over the chunk's rows and
+// merge in L2.  Several warps share a chunk when chunks are few.
+__global__ void __launch_bounds__(kThreads) pack_rows_kernel(PackParams p, int split) {
+    const long long total_words = p.ctrl->status[kStTotalWords];
+    const int rows_cap = (int)p.ctrl->status[kStRowsCap];
+    if (p.header_bytes + 4 * (int64_t)total_words != p.packed_bytes) return;  // not the last encode's size
+    uint32_t *hdr = reinterpret_cast<uint32_t *>(p.packed);
+    if (blockIdx.x == 0 && threadIdx.x < 8) {
+        uint32_t h = 0;
+        switch (threadIdx.x) {
+            case 0: h = (uint32_t)p.N; break;
+            case 1: h = (uint32_t)p.chunk_len; break;
+            case 2: h = ((uint32_t)p.K & 0xFFFFu) | (((uint32_t)p.B & 0xFFFFu) << 16); break;
+            case 3: h = 2u | (32u << 16); break;
+            default: h = 0u;
+        }
+        hdr[threadIdx.x] = h;
+    }
+    const int64_t table_end = 32 + 4 * p.chunks;
+    if (blockIdx.x == 0 && threadIdx.x >= 8 && threadIdx.x < 8 + (p.header_bytes - table_end) / 4)
+        hdr[table_end / 4 + (threadIdx.x - 8)] = 0u;
+    const int lane = threadIdx.x & 31;
+    uint32_t *body = reinterpret_cast<uint32_t *>(p.packed + p.header_bytes);
+    const int64_t tasks = p.chunks * split;
+    const int64_t warp_stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tasks;
+         task += warp_stride) {
+        const int64_t chunk = task / split;
+        const int part = (int)(task - chunk * split);
+        const int rounds = __ldg(p.rounds + chunk);
+        int used = __ldg(p.used + chunk * kLanes + lane);
+        if (used > rows_cap) used = 0;  // overflowed staging: never packed by the host
+        if (lane == 0 && part == 0) hdr[8 + chunk] = (uint32_t)rounds;
+        const uint32_t *st = p.stage + chunk * (int64_t)rows_cap * kLanes + lane;
+        uint32_t *out = body + p.offsets[chunk] + lane;
+        const int per = (rounds + split - 1) / split;
+        const int j0 = part * per, j1 = min(rounds, j0 + per);
+        int j = j0;
+        for (; j + 8 <= j1; j += 8) {
+            uint32_t v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = j + i < rows_cap ? __ldcs(st + (int64_t)(j + i) * kLanes) : 0u;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int jj = j + i;
+                const bool word = jj < used;
+                out[(int64_t)(word ? used - 1 - jj : jj) * kLanes] = word ? v[i] : 0u;
+            }
+        }
+        for (; j < j1; ++j) {
+            const bool word = j < used;
+            out[(int64_t)(word ? used - 1 - j : j) * kLanes] = word ? st[(int64_t)j * kLanes] : 0u;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1348,13 +1802,13 @@ static int launch_encode_full(const EncParams &p, int64_t smem, cudaStream_t str
     return FCAI_OK;
 }
 
-template <int kMode, bool kSmem>
-static int launch_encode_group(const EncParams &p, int64_t smem, cudaStream_t stream) {
+template <int kMode>
+static int launch_encode_group(const EncParams &p, cudaStream_t stream) {
     int grid = 1, rc;
     const int warps = group_warps(p.B, p.K);
     const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
-    if ((rc = grid_for(encode_group_kernel<kMode, kSmem>, kSmem ? smem : 0, groups * warps, warps, grid))) return rc;
-    encode_group_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
+    if ((rc = grid_for(encode_group_kernel<kMode>, 0, groups * warps, warps, grid))) return rc;
+    encode_group_kernel<kMode><<<grid, warps * kLanes, 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
@@ -1369,13 +1823,35 @@ static int launch_decode_full(const DecParams &p, int64_t smem, cudaStream_t str
     return FCAI_OK;
 }
 
-template <int kMode, bool kSmem>
-static int launch_decode_group(const DecParams &p, int64_t smem, cudaStream_t stream) {
+template <int kMode>
+static int launch_encode_lanes(const EncParams &p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
     const int warps = group_warps(p.B, p.K);
     const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
-    if ((rc = grid_for(decode_group_kernel<kMode, kSmem>, kSmem ? smem : 0, groups * warps, warps, grid))) return rc;
-    decode_group_kernel<kMode, kSmem><<<grid, warps * kLanes, kSmem ? smem : 0, stream>>>(p);
+    if ((rc = grid_for(encode_lanes_kernel<kMode>, smem, groups * warps, warps, grid))) return rc;
+    encode_lanes_kernel<kMode><<<grid, warps * kLanes, smem, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+template <int kMode, bool kPair>
+static int launch_decode_lanes(const DecParams &p, int64_t smem, cudaStream_t stream) {
+    int grid = 1, rc;
+    const int warps = group_warps(p.B, p.K);
+    const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
+    if ((rc = grid_for(decode_lanes_kernel<kMode, kPair>, smem, groups * warps, warps, grid))) return rc;
+    decode_lanes_kernel<kMode, kPair><<<grid, warps * kLanes, smem, stream>>>(p);
+    FCAI_CUDA_TRY(cudaGetLastError());
+    return FCAI_OK;
+}
+
+template <int kMode>
+static int launch_decode_group(const DecParams &p, cudaStream_t stream) {
+    int grid = 1, rc;
+    const int warps = group_warps(p.B, p.K);
+    const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
+    if ((rc = grid_for(decode_group_kernel<kMode>, 0, groups * warps, warps, grid))) return rc;
+    decode_group_kernel<kMode><<<grid, warps * kLanes, 0, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
@@ -1516,14 +1992,15 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
         const int64_t smem = encode_smem_bytes(C, L);
         rc = smem <= kMaxSmemBytes ? launch_encode_full<true>(p, smem, stream) : launch_encode_full<false>(p, smem, stream);
     } else {
-        const int64_t smem = group_smem(d.P, L, true).bytes;
-        const bool sm = smem <= kMaxSmemBytes;
-        if (mode == kModeChannel)
-            rc = sm ? launch_encode_group<kModeChannel, true>(p, smem, stream)
-                    : launch_encode_group<kModeChannel, false>(p, smem, stream);
+        // the group's rows in shared memory (every P of the reference's
+        // sweep with 16-bit CDFs of <= 66 entries), else global tables
+        const int64_t smem = lanes_smem(d.P, L, true).bytes;
+        if (smem <= kMaxSmemBytes)
+            rc = mode == kModeChannel ? launch_encode_lanes<kModeChannel>(p, smem, stream)
+                                      : launch_encode_lanes<kModeLatent>(p, smem, stream);
         else
-            rc = sm ? launch_encode_group<kModeLatent, true>(p, smem, stream)
-                    : launch_encode_group<kModeLatent, false>(p, smem, stream);
+            rc = mode == kModeChannel ? launch_encode_group<kModeChannel>(p, stream)
+                                      : launch_encode_group<kModeLatent>(p, stream);
     }
     if (rc) return rc;
     if (submit) {
@@ -1616,14 +2093,22 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
             rc = sm ? launch_decode_full<kModeLatent, true>(p, smem, stream)
                     : launch_decode_full<kModeLatent, false>(p, smem, stream);
     } else {
-        const int64_t smem = group_smem(chunk_len / HW, L, false).bytes;
-        const bool sm = smem <= kMaxSmemBytes;
-        if (mode == kModeChannel)
-            rc = sm ? launch_decode_group<kModeChannel, true>(p, smem, stream)
-                    : launch_decode_group<kModeChannel, false>(p, smem, stream);
+        // buckets of at most 64 slots (P <= 8) resolve two-symbol buckets
+        // without a search; coarser ones keep the bucket's last symbol
+        const int Pg = chunk_len / HW;
+        const int64_t smem = lanes_smem(Pg, L, false).bytes;
+        const bool pair = lanes_lut_shift(Pg) <= 6;
+        if (smem <= kMaxSmemBytes) {
+            if (mode == kModeChannel)
+                rc = pair ? launch_decode_lanes<kModeChannel, true>(p, smem, stream)
+                          : launch_decode_lanes<kModeChannel, false>(p, smem, stream);
+            else
+                rc = pair ? launch_decode_lanes<kModeLatent, true>(p, smem, stream)
+                          : launch_decode_lanes<kModeLatent, false>(p, smem, stream);
+        }
         else
-            rc = sm ? launch_decode_group<kModeLatent, true>(p, smem, stream)
-                    : launch_decode_group<kModeLatent, false>(p, smem, stream);
+            rc = mode == kModeChannel ? launch_decode_group<kModeChannel>(p, stream)
+                                      : launch_decode_group<kModeLatent>(p, stream);
     }
     if (rc) return rc;
     if (!check) return FCAI_OK;
@@ -1735,10 +2220,13 @@ int fcai_warp_div_encode_pack(const void *workspace, int64_t workspace_bytes, in
     p.header_bytes = d.header_bytes;
     p.packed_bytes = packed_bytes;
     p.packed = packed;
-    int64_t want = (d.chunks + kWarps - 1) / kWarps;
-    int64_t cap = (int64_t)fcai::sm_count() * 8;
-    int grid = (int)(want < cap ? want : cap);
-    pack_kernel<<<grid, kThreads, 0, stream>>>(p);
+    // about 32 warps per SM: several warps share a chunk when chunks are few
+    const int64_t target = (int64_t)fcai::sm_count() * 32;
+    const int split = (int)std::min<int64_t>(16, std::max<int64_t>(1, target / std::max<int64_t>(d.chunks, 1)));
+    const int64_t want = (d.chunks * split + kWarps - 1) / kWarps;
+    const int64_t cap = (int64_t)fcai::sm_count() * 8;
+    const int grid = (int)(want < cap ? want : cap);
+    pack_rows_kernel<<<grid, kThreads, 0, stream>>>(p, split);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
