@@ -963,6 +963,19 @@ def run_ans_sweep(args):
             ts.append(a.elapsed_time(b))
         return statistics.median(ts)
 
+    # The reference's own extension (its warp_div CUDA sources compiled for
+    # sm_100a by oracle/build_ref.py; a test-only checker), timed the same
+    # way on the same symbols when it has been built: the coder bar of the
+    # reference on this GPU.
+    ref = None
+    try:
+        from oracle import build_ref
+
+        if build_ref.built_path().exists():
+            ref = build_ref.load()
+    except Exception as exc:  # noqa: BLE001 - report and carry on without it
+        print(f"reference extension unavailable: {exc}", file=sys.stderr)
+
     rows = []
     for P in (int(v) for v in args.sweep_p.split(",")):
         r = ext.encode(sym, None, cd, sz, of, P)
@@ -977,17 +990,31 @@ def run_ans_sweep(args):
         dcm = timed(lambda: ext.decode(r.packed, r.max_rounds, r.header_bytes, r.chunk_len, None, cd, sz, of,
                                        batch=B, symbols_per_batch=C * HW))
         dci = timed(lambda: ext.decode(r.packed, r.max_rounds, r.header_bytes, r.chunk_len, idx, cd, sz, of))
-        rows.append({"p_ch": P, "chunks": int(r.max_rounds.numel()), "payload_bytes": int(r.packed.numel()),
-                     "bits_per_symbol": r.packed.numel() * 8 / sym.numel(),
-                     "encode_ms": enc, "encode_indexes_ms": enc_i, "decode_ms": dcm, "decode_indexes_ms": dci,
-                     "encode_gbs": nbytes / enc / 1e6, "decode_gbs": nbytes / dcm / 1e6,
-                     "encode_frac": nbytes / enc / 1e6 / hbm, "decode_frac": nbytes / dcm / 1e6 / hbm})
+        row = {"p_ch": P, "chunks": int(r.max_rounds.numel()), "payload_bytes": int(r.packed.numel()),
+               "bits_per_symbol": r.packed.numel() * 8 / sym.numel(),
+               "encode_ms": enc, "encode_indexes_ms": enc_i, "decode_ms": dcm, "decode_indexes_ms": dci,
+               "encode_gbs": nbytes / enc / 1e6, "decode_gbs": nbytes / dcm / 1e6,
+               "encode_frac": nbytes / enc / 1e6 / hbm, "decode_frac": nbytes / dcm / 1e6 / hbm}
+        if ref is not None:
+            rp, rmr, rhb, rcl, rP = ref.encode_warp_div(sym, idx, cd, sz, of, P)
+            torch.cuda.synchronize()
+            if not torch.equal(rmr, r.max_rounds) or rp.numel() != r.packed.numel():
+                raise SystemExit(f"reference extension disagrees at P={P}")
+            row["reference_encode_ms"] = timed(lambda: ref.encode_warp_div(sym, idx, cd, sz, of, P))
+            row["reference_decode_ms"] = timed(lambda: ref.decode_warp_div(rp, rmr, rhb, rcl, rP, idx, cd, sz, of))
+            row["speedup_vs_reference"] = {"encode": row["reference_encode_ms"] / enc_i,
+                                           "decode": row["reference_decode_ms"] / dci}
+        rows.append(row)
     line = {
         "metric": "warp_div encode / decode GB/s (int32 symbols + payload bytes), BASELINE config 3",
         "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "dtype": "int32", "data": "synthetic: seeded discretised-Laplacian symbols and 16-bit CDFs (config 3)",
         "config": {"workload": "ANS sweep", "symbols": [B, C * HW], "l2": "flushed before each call (256 MB write)"},
         "hbm_peak_gbs": hbm, "sweep": rows,
+        "reference_extension": "built" if ref is not None else "not built (oracle/build_ref.py)",
+        "note": "host-call times (launches, the encode's size read-back and pack, the decode's check) with CUDA "
+                "events; reference_* time the reference's encode_warp_div / decode_warp_div, which take explicit "
+                "indexes, so speedup_vs_reference compares them with the *_indexes_ms calls",
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -18,11 +18,14 @@ from .coders import (
 )
 from .config import AccelerationConfig, CompileConfig, ConfigurationError
 from .errors import UnsupportedOperationError
+from .policies import PChSelection, choose_p_ch, legal_p_candidates
+from .profiling import CalibrationData, calibration_from_images, default_p_candidates, sweep_p_ch
 
 __all__ = [
     "AccelerationConfig",
     "AccelerationReport",
     "BitstreamError",
+    "CalibrationData",
     "CoderCapability",
     "CoderDependencyError",
     "CoderError",
@@ -33,14 +36,20 @@ __all__ = [
     "CompressAIANSBackend",
     "ConfigurationError",
     "FastModel",
+    "PChSelection",
     "UnsupportedOperationError",
     "WarpDivBackend",
     "WarpDivPayload",
     "accelerate",
+    "calibration_from_images",
+    "choose_p_ch",
     "coder_catalog",
     "compile",
     "create_coder",
+    "default_p_candidates",
+    "legal_p_candidates",
     "optimize",
+    "sweep_p_ch",
     "warp_div_capability",
 ]
 

@@ -138,10 +138,11 @@ def accelerate(
         raise ConfigurationError("do not combine precision_config_path with calibration_data")
     if transforms not in _TRANSFORMS:
         raise ConfigurationError(f"transforms must be one of {_TRANSFORMS}")
-    del dataset_name, precision_config_output_dir
+    del precision_config_output_dir
     codec = None
     runtime_model = model
     target = None
+    p_selection = p_sweep = None
     if cfg.coder == "warp_div":
         if not _is_factorized_prior(model):
             raise ConfigurationError("warp_div currently supports only CompressAI FactorizedPrior")
@@ -154,8 +155,19 @@ def accelerate(
         if target.type != "cuda":
             raise ConfigurationError("warp_div requires device='cuda'")
         if calibration_data is not None:
-            raise ConfigurationError("CAIEC precision selection is not part of this build; load a saved "
-                                     "precision config (precision_config_path) or use transforms='bf16'")
+            # This build selects P_ch from calibration data (the reference's
+            # sweep, api.py:255-263); the CAIEC precision search that the
+            # reference runs first is not part of it.
+            from .profiling import CalibrationData
+
+            if P is not None or cfg.p_ch is not None:
+                raise ConfigurationError("CAIEC precision selection is not part of this build; calibration_data "
+                                         "selects P_ch when P is None")
+            if not isinstance(calibration_data, CalibrationData):
+                raise ConfigurationError("calibration_data must be a CalibrationData object prepared outside "
+                                         "accelerate()")
+            if dataset_name is not None and dataset_name != calibration_data.dataset_name:
+                raise ConfigurationError("dataset_name does not match calibration_data")
         precision_config = None
         layer_precisions = None
         if cfg.precision_config_path is not None:
@@ -174,6 +186,12 @@ def accelerate(
         p_ch = cfg.p_ch if cfg.p_ch is not None else 1
         if precision_config is not None:
             p_ch = precision_config.p_ch
+        if calibration_data is not None:
+            from .profiling import sweep_p_ch
+
+            p_selection, p_sweep = sweep_p_ch(runtime_model, calibration_data, model_name=type(model).__qualname__,
+                                              warmup=1, repetitions=1)
+            p_ch = p_selection.selected_p_ch
         codec = FactorizedWarpDivCodec(runtime_model, p_ch)
     elif sample is not None:
         raise ConfigurationError("the legacy BF16 sample profiling of coder='rans' is not part of this build")
@@ -230,6 +248,10 @@ def accelerate(
     elif codec is not None and transforms == "fp8":
         apps = tuple(runtime_model.g_a.precision_notes) + tuple(runtime_model.g_s.precision_notes)
         wrapped.acceleration_report = replace(wrapped.acceleration_report, precision_applications=apps)
+    if codec is not None and p_selection is not None:
+        wrapped.acceleration_report = replace(
+            wrapped.acceleration_report, p_ch_selection_status=p_selection.status,
+            p_ch_selection_reason=p_selection.reason, p_ch_sweep=p_sweep)
     return wrapped
 
 
