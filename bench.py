@@ -56,6 +56,8 @@ def parse_args(argv=None):
     ap.add_argument("--transforms", choices=("bf16", "fp32"), default="bf16")
     ap.add_argument("--cpu-sample", type=int, default=1, help="images in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the BASELINE config 4 summary that the one-GPU line carries")
     ap.add_argument("--no-precision-map", action="store_true",
                     help="skip the extra measurement with the reference's example precision map (FP8 layers)")
     ap.add_argument("--chunk-images", type=int, default=4,
@@ -609,12 +611,15 @@ def run_b200(args):
             torch.cuda.synchronize()
             t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             t0.record(main)
-            nxt = fast.upload_host(hosts[0], chunk_images=stream_chunk)
+            # two uploads in flight: while the host waits for step i's payload
+            # size, step i + 1's batch is already queued behind step i's, so
+            # the host-to-device direction of the link never idles
+            ahead = [fast.upload_host(hosts[k % 2], chunk_images=stream_chunk) for k in range(min(2, nsteps))]
             readies = []
             for i in range(nsteps):
-                cur = nxt
-                if i + 1 < nsteps:
-                    nxt = fast.upload_host(hosts[(i + 1) % 2], chunk_images=stream_chunk)
+                cur = ahead.pop(0)
+                if i + 2 < nsteps:
+                    ahead.append(fast.upload_host(hosts[(i + 2) % 2], chunk_images=stream_chunk))
                 out = fast.compress(cur)
                 p = out["strings"][0]
                 if roundtrip:
@@ -877,10 +882,10 @@ def run_b200(args):
                     "ms_per_step": e2e_step_ms, "chunk_images": stream_chunk,
                     "link_ceiling": link, "frac_of_link_ceiling": e2e_value / link["value"],
                     "api": "FastModel.upload_host -> compress -> payload copied to pinned host memory on its own "
-                           "stream -> decompress_host(ordered=False) of the device payload, one host thread; step "
-                           "i+1's upload and step i's downloads (payload, reconstruction) run on copy streams "
-                           "during the neighbouring steps' GPU work; every step's images come up from pinned host "
-                           "memory and its payload and reconstruction go down to it",
+                           "stream -> decompress_host(ordered=False) of the device payload, one host thread; the "
+                           "uploads of steps i+1 and i+2 and step i's downloads (payload, reconstruction) run on "
+                           "copy streams during the neighbouring steps' GPU work; every step's images come up from "
+                           "pinned host memory and its payload and reconstruction go down to it",
                     "payload_roundtrip": e2e_roundtrip,
                     "serial": e2e_serial},
             "gpu_launches": launches,
@@ -919,6 +924,15 @@ def run_b200(args):
             with torch.inference_mode():
                 line["cpu_baseline"]["gpu_fp32_transforms_cpu_rans"] = time_gpu_transforms_cpu_rans(
                     build_model().to(dev), x, steps=3)
+        if world == 1 and not args.no_config4:
+            # BASELINE config 4 beside the headline (after its timed region):
+            # bf16 and fp8 transforms against FP32 on FactorizedPrior(192, 320)
+            rows4, _ = measure_config4(dev, steps=3, warmup=1)
+            line["config4"] = {
+                "workload": "FactorizedPrior(192,320), 4 x 3 x 2048 x 2048, P = 8, 3 timed steps each",
+                **{name: {k: row[k] for k in ("value", "ms_per_step", "psnr_drop_db_vs_fp32", "payload_ratio_vs_fp32",
+                                               "symbol_mismatch_rate_vs_fp32")} for name, row in rows4.items()},
+                "unit": UNIT}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -1020,39 +1034,34 @@ def run_ans_sweep(args):
     return 0
 
 
-def run_config4(args):
-    """FactorizedPrior(192, 320), random-init weights with update(force=True), 4 x 3 x
-    2048 x 2048 seeded smoothed-noise images, P = 8.  Compress + decompress throughput (fp32 input-image
-    bytes per second, input resident on the device, each step bracketed by CUDA events) with the FP32
-    transforms (the model's own torch modules, cuDNN with PyTorch's default conv settings, as the
-    reference runs them without a precision config), the B200 bf16 transforms and the B200 fp8
-    transforms; per variant the PSNR of the reconstruction, its drop against FP32, the payload size
-    against FP32's and the per-layer kernel times.  Each step's working set (> 3 GB of activations)
-    exceeds the 126 MB L2."""
+def measure_config4(dev, steps, warmup):
+    """FactorizedPrior(192, 320), random init from seed 0 with its latent spread over its
+    CDF tables (as build_model does for config 2, calibrated on one 512 x 512 image), 4 x 3 x 2048 x 2048
+    seeded smoothed-noise images, P = 8.  Compress + decompress throughput (fp32 input-image bytes per
+    second, input resident on the device, each step bracketed by CUDA events) with the FP32 transforms (the
+    model's own torch modules, cuDNN with TF32 off), the B200 bf16 transforms and the B200 fp8 transforms;
+    per variant the PSNR of the reconstruction, its drop against FP32, the payload size against FP32's, the
+    share of latent symbols that differ from FP32's and the per-layer kernel times.  Each step's working
+    set (> 3 GB of activations) exceeds the 126 MB L2.  Returns (variants, clocks of the bf16 run)."""
     import torch
 
     import fast_compressai
     from fast_compressai import _native, transforms
-    from fast_compressai.balle import FactorizedPrior
+    from tests.model_inputs import spread_latent_prior
 
-    if int(os.environ.get("RANK", "0")) != 0:
-        return 0
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    torch.manual_seed(0)
-    model = FactorizedPrior(192, 320).eval()
-    model.update(force=True)
+    model = spread_latent_prior(192, 320, smooth_noise_images(1, 512, 512, seed=17), target_std=12.0, seed=0)
     B, H, W, P = 4, 2048, 2048, 8
     x = smooth_noise_images(B, H, W, seed=4321).to(dev)
     in_bytes = x.numel() * 4
-    peaks = read_peaks()
     rows = {}
-    ref_psnr = ref_bytes = None
+    ref_psnr = ref_bytes = sym_ref = None
     clock_info = None
+    tf32 = torch.backends.cudnn.allow_tf32
     for name in ("fp32", "bf16", "fp8"):
+        torch.backends.cudnn.allow_tf32 = False if name == "fp32" else tf32
         fast = fast_compressai.accelerate(model, P=P, device=str(dev), transforms=name)
         with torch.inference_mode():
-            for _ in range(max(args.warmup, 1)):
+            for _ in range(max(warmup, 1)):
                 out = fast.compress(x)
                 x_hat = fast.decompress(out["strings"], out["shape"])["x_hat"]
             torch.cuda.synchronize()
@@ -1060,7 +1069,7 @@ def run_config4(args):
             launches0 = _native.LAUNCHES["kernels"]
             transforms.LAYER_TIMING = layer_events = []
             events = []
-            for _ in range(args.steps):
+            for _ in range(steps):
                 e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 e0.record()
                 out = fast.compress(x)
@@ -1074,12 +1083,15 @@ def run_config4(args):
             info = clocks.stop()
             if name == "bf16":
                 clock_info = info
-        ms = sum(a.elapsed_time(c) for a, _, c in events) / args.steps
-        comp = sum(a.elapsed_time(b) for a, b, _ in events) / args.steps
+            med = fast.model.entropy_bottleneck._get_medians().detach().reshape(1, -1, 1, 1)
+            sym = torch.round(fast.model.g_a(x).float() - med)
+        torch.backends.cudnn.allow_tf32 = tf32
+        ms = sum(a.elapsed_time(c) for a, _, c in events) / steps
+        comp = sum(a.elapsed_time(b) for a, b, _ in events) / steps
         q = psnr(x_hat, x)
         nbytes = out["strings"][0].packed.numel()
         if name == "fp32":
-            ref_psnr, ref_bytes = q, nbytes
+            ref_psnr, ref_bytes, sym_ref = q, nbytes, sym
         per_layer = {}
         for lname, flops, a, b in layer_events:
             d = per_layer.setdefault(lname, {"ms": 0.0, "n": 0, "flops": flops})
@@ -1090,23 +1102,38 @@ def run_config4(args):
         row = {"value": in_bytes / (ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": ms, "compress_ms": comp,
                "decompress_ms": ms - comp, "psnr_db": q, "psnr_drop_db_vs_fp32": ref_psnr - q,
                "payload_bytes": nbytes, "payload_ratio_vs_fp32": nbytes / ref_bytes,
-               "bpp_per_value": nbytes * 8 / x.numel(), "gpu_launches_per_step": launches / args.steps}
+               "symbol_mismatch_rate_vs_fp32": float((sym != sym_ref).float().mean()),
+               "bpp_per_value": nbytes * 8 / x.numel(), "gpu_launches_per_step": launches / steps}
         if layers:
             row["layers"] = layers
         rep = fast.acceleration_report
         if rep.precision_applications:
             row["fp8_modules"] = [m for m, _, got, _ in rep.precision_applications if got == "fp8"]
         rows[name] = row
-        del fast, out, x_hat
+        del fast, out, x_hat, sym
         torch.cuda.empty_cache()
+    return rows, clock_info
+
+
+def run_config4(args):
+    """BASELINE config 4 as its own JSON line (measure_config4)."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    rows, clock_info = measure_config4(dev, args.steps, args.warmup)
+    peaks = read_peaks()
     line = {
         "metric": "compress+decompress GB/s (fp32 input image bytes), FactorizedPrior(192,320) P=8, BASELINE config 4",
         "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "dtype": "bf16 / e4m3 operands, fp32 accumulate (fp32: the torch modules)",
-        "data": "synthetic: seeded smoothed-noise images (config 4), random-init weights",
-        "config": {"workload": "config 4", "model": "FactorizedPrior(192,320)", "batch": B, "image": [H, W],
-                   "p_ch": P, "l2": "working set > L2 (activations > 3 GB per step)",
-                   "cudnn_allow_tf32": bool(torch.backends.cudnn.allow_tf32)},
+        "data": "synthetic: seeded smoothed-noise images (config 4), random-init weights with the latent spread "
+                "over the CDF tables",
+        "config": {"workload": "config 4", "model": "FactorizedPrior(192,320)", "batch": 4, "image": [2048, 2048],
+                   "p_ch": 8, "l2": "working set > L2 (activations > 3 GB per step)",
+                   "fp32_variant": "cuDNN with TF32 off"},
         "variants": rows, "clocks": clock_info, "peaks": {k: peaks.get(k) for k in ("bf16_tflops", "bf16_tflops_sustained")},
     }
     print(json.dumps(line), flush=True)
