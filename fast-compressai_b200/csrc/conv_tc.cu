@@ -616,7 +616,192 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
         }
     } else if (warp < Lay::kEpiWarps) {
         // ------------------------------------------------------------ epilogue
-        if constexpr (Lay::kDual) {
+        if constexpr (Lay::kDual && kEpi == kEpiIgdn) {
+            // Two epilogue variants of dual tiles, chosen by measurement (the
+            // same build, batch 24, alternating runs): the IGDN layers (short
+            // phase mainloops of 4-9 taps) run faster when the two groups do
+            // not take turns with one operand tile (g_s.4 0.477 -> 0.461 ms,
+            // g_s.2 0.130 -> 0.125 ms); the GDN layers (25-tap mainloops that
+            // already hide the epilogue) run faster with one shared tile and
+            // a single GDN GEMM per half (g_a.2 0.388 against 0.396 ms).
+            //
+            // Dual tiles: rows 0-127 of the tile (TMEM columns [0, 128) of the
+            // buffer) belong to group 0 (warps 0-3), rows 128-255 (columns
+            // [128, 256)) to group 1 (warps 4-7).  Each thread keeps its
+            // pixel's 128 conv outputs in registers, so the GDN GEMM writes
+            // the norm over them in TMEM.  Each group owns one 16 KB half of
+            // the x^2 / staging area: the GDN GEMM runs in two K halves (x^2
+            // of channels 0-63, then of 64-127, through the group's half), and
+            // the output leaves in two 64-channel boxes staged there in turn,
+            // so the two groups never wait for each other inside a tile.
+            // Named barriers: 1 + h (group h), 3 (all 256 threads, tile
+            // start).  Every barrier of a tile is taken by every thread of its
+            // group, whatever the outcome of the waits (the work between them
+            // is what the outcome skips).
+            const int h = warp >> 2;
+            const int m = threadIdx.x & 127;
+            const bool hleader = m == 0;
+            const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+            const uint32_t x2 = smem_u32(smem + Lay::offX2) + (uint32_t)h * (kBM * 128);  // this group's half
+            volatile int *t_ok = epi_ok;
+            volatile int *h_ok = epi_ok + 1 + h;
+            uint32_t am2 = 0;  // max |output| of this thread's valid pixels (amax_out)
+            bool consts = false;
+            int j = 0;
+            for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
+                int b, ph, gy0, gx0;
+                tile_coords(p, tile, b, ph, gy0, gx0);
+                const int buf = j & 1;
+                const uint32_t use = j >> 1;
+                if (threadIdx.x == 0) {
+                    bool ok = !*abort;
+                    if (ok && !consts) ok = mbar_wait(cbar, 0, abort, kWaitNs);
+                    if (ok) ok = mbar_wait(&accf[buf], use & 1, abort, kWaitNs);
+                    if (!ok) fail(p, abort, kErrEpilogue);
+                    *t_ok = ok ? 1 : 0;
+                }
+                // the group has passed its last read of h_ok for the previous
+                // tile (its last barrier), so the leader may reset it here
+                if (hleader) *h_ok = 1;
+                // each group's leader saw its previous tile's stores read its
+                // half before it got here
+                named_barrier_sync(3, 2 * kBM);
+                if (!*t_ok) break;
+                consts = true;
+                tc_fence_after();
+                const uint32_t dcol = tmem_base + buf * p.buf_stride + h * kBM;  // this half's columns
+                uint32_t xv[kNpad / 16][16];
+#pragma unroll
+                for (int k = 0; k < kNpad / 16; ++k) tmem_ld16(dcol + lane_addr + k * 16, xv[k]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < kNpad / 16; ++k) tmem_regs_ready(xv[k]);
+                if (kFp8) {
+                    // x = (s_x s_w) * accumulator + bias
+                    const float sc = *p.act_scale * p.w_scale;
+#pragma unroll
+                    for (int k = 0; k < kNpad / 16; ++k)
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            xv[k][e] = __float_as_uint(fmaf(__uint_as_float(xv[k][e]), sc, s_bias[k * 16 + e]));
+                }
+                // norm = beta (ones x beta) + x^2 gamma^T in two K halves of
+                // 64 channels through this group's 16 KB operand tile
+#pragma unroll
+                for (int q = 0; q < kNpad / kBK; ++q) {
+                    if (*h_ok) {
+#pragma unroll
+                        for (int k = q * (kBK / 16); k < (q + 1) * (kBK / 16); ++k) {
+#pragma unroll
+                            for (int hh = 0; hh < 2; ++hh) {
+                                uint32_t w[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    const float a = __uint_as_float(xv[k][hh * 8 + 2 * e]);
+                                    const float c = __uint_as_float(xv[k][hh * 8 + 2 * e + 1]);
+                                    w[e] = pack_bf16x2(a * a, c * c);
+                                }
+                                const int chunk = ((k * 16 + hh * 8) % kBK) / 8;
+                                st_shared_v4(x2 + m * 128 + ((chunk ^ (m & 7)) << 4), w[0], w[1], w[2], w[3]);
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    tc_fence_before();  // the TMEM loads above precede the GEMM that overwrites those columns
+                    named_barrier_sync(1 + h, kBM);
+                    if (hleader && *h_ok) {
+                        tc_fence_after();
+                        const uint32_t g0 = smem_u32(smem + Lay::offG) + q * (kNpad * 128);
+                        const uint32_t idesc = idesc_bf16(kBM, kNpad);
+                        if (q == 0)
+                            mma_bf16(dcol, smem_desc(smem_u32(smem + Lay::offOnes), 128, 256, 0),
+                                     smem_desc(smem_u32(smem + Lay::offBetaB), 128, 256, 0), idesc, 0);
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 16; ++kk)
+                            mma_bf16(dcol, smem_desc(x2 + kk * 32, 16, 1024, 2), smem_desc(g0 + kk * 32, 16, 1024, 2),
+                                     idesc, 1);
+                        mma_commit(&g2bar[h]);
+                        // two GEMM halves a tile: the q-th completion of the tile has parity q
+                        const bool ok = mbar_wait(&g2bar[h], (uint32_t)q & 1u, abort, kWaitNs);
+                        if (!ok) fail(p, abort, kErrEpilogue);
+                        *h_ok = ok ? 1 : 0;
+                    }
+                    named_barrier_sync(1 + h, kBM);
+                }
+                const bool hok = *h_ok != 0;
+                tc_fence_after();
+                // y = x * rsqrt(norm) (IGDN: x * sqrt(norm)), one 64-channel box at
+                // a time: staged in this group's half and stored by TMA, or
+                // stored straight to global memory
+                const int row = h * kBM + m;
+                const int ty = row / p.TX, tx = row - ty * p.TX;
+                const int gy = gy0 + ty, gx = gx0 + tx;
+                const bool valid = gy < p.GH && gx < p.GW;
+                const int oy = gy * p.out_step + (p.phases == 4 ? (ph >> 1) : 0);
+                const int ox = gx * p.out_step + (p.phases == 4 ? (ph & 1) : 0);
+                __nv_bfloat16 *orow = reinterpret_cast<__nv_bfloat16 *>(p.out) +
+                                      (((int64_t)b * p.Hout + oy) * p.Wout + ox) * kNpad;
+                const int hy = gy0 + h * (p.TY / 2);  // this half: TY / 2 rows of the tile
+#pragma unroll
+                for (int kb = 0; kb < kNpad / kBK; ++kb) {
+                    if (hok) {
+                        uint32_t nv[2][16];
+                        constexpr int kPer = kBK / 16;
+                        tmem_ld16(dcol + lane_addr + kb * kBK, nv[0]);
+#pragma unroll
+                        for (int i = 0; i < kPer; ++i) {
+                            const int k = kb * kPer + i;
+                            tmem_wait_ld();
+                            tmem_regs_ready(nv[i & 1]);
+                            if (i + 1 < kPer) tmem_ld16(dcol + lane_addr + (k + 1) * 16, nv[(i + 1) & 1]);
+                            uint32_t o[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float n0 = __uint_as_float(nv[i & 1][2 * e]);
+                                const float n1 = __uint_as_float(nv[i & 1][2 * e + 1]);
+                                const float r0 = kEpi == kEpiIgdn ? sqrt_approx(n0) : rsqrt_approx(n0);
+                                const float r1 = kEpi == kEpiIgdn ? sqrt_approx(n1) : rsqrt_approx(n1);
+                                o[e] = pack_bf16x2(__uint_as_float(xv[k][2 * e]) * r0,
+                                                   __uint_as_float(xv[k][2 * e + 1]) * r1);
+                                if (valid) am2 = amax_bf16x2(am2, o[e]);
+                            }
+                            if (p.tma_store) {
+#pragma unroll
+                                for (int hh = 0; hh < 2; ++hh) {
+                                    const int chunk = ((k * 16 + hh * 8) % kBK) / 8;
+                                    st_shared_v4(x2 + m * 128 + ((chunk ^ (m & 7)) << 4), o[hh * 4], o[hh * 4 + 1],
+                                                 o[hh * 4 + 2], o[hh * 4 + 3]);
+                                }
+                            } else if (valid) {
+                                uint4 *dst = reinterpret_cast<uint4 *>(orow + k * 16);
+                                dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                                dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                            }
+                        }
+                    }
+                    if (kb == kNpad / kBK - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&acce[buf]);  // this thread is done with the accumulator
+                    }
+                    fence_proxy_async_smem();
+                    named_barrier_sync(1 + h, kBM);
+                    if (hleader && p.tma_store) {
+                        if (hok) {
+                            const uint8_t *stg = smem + Lay::offX2 + h * (kBM * 128);
+                            if (p.tma_store == 2)
+                                tma_store_5d(&tmO, stg, kb * kBK, ph & 1, gx0, ph >> 1, b * p.GH + hy);
+                            else
+                                tma_store_4d(&tmO, stg, kb * kBK, gx0, hy, b);
+                            bulk_commit_group();
+                        }
+                        bulk_wait_read_all();  // the half may be rewritten (next box or next tile's x^2)
+                    }
+                    if (kb + 1 < kNpad / kBK) named_barrier_sync(1 + h, kBM);
+                }
+            }
+            if (hleader && p.tma_store) bulk_wait_all();  // stores complete before the CTA exits
+            if (p.amax_out) amax_flush(p.amax_out, am2);
+        } else if constexpr (Lay::kDual) {
             // Dual tiles: rows 0-127 of the tile (TMEM columns [0, 128) of the
             // buffer) belong to group 0 (warps 0-3), rows 128-255 (columns
             // [128, 256)) to group 1 (warps 4-7).  Each thread keeps its
