@@ -1126,11 +1126,18 @@ __device__ __forceinline__ uint32_t escape_raw(int32_t value, int32_t maxv) {
 // of the warp escapes and every lane has room for 8 more words the steps
 // have no per-symbol checks.  Other batches, the ragged end and escapes go
 // through the checked per-symbol path.
+//
+// With explicit indexes (kModeIdx) each batch also checks, by warp vote,
+// that its indexes are the channel layout the group staged; a batch with
+// any other index takes the checked path, where a symbol whose row lies
+// outside the group reads its entry from global memory (and the call
+// reports that the indexes are not the channel layout).
 template <int kMode>
 __device__ __forceinline__ void encode_lanes(const EncParams &p, const uint4 *__restrict__ ent,
-                                             const int4 *__restrict__ chan, int c0, int Ls, int64_t chunk, int lane,
-                                             uint32_t &flags, unsigned int &my_max_used) {
+                                             const int4 *__restrict__ chan, int c0, int nc, int Ls, int64_t chunk,
+                                             int lane, uint32_t &flags, unsigned int &my_max_used) {
     constexpr int kB = 8, kH = 4;
+    constexpr bool kIdx = kMode == kModeIdx;
     const int b = (int)(chunk / p.K);
     const int k = (int)(chunk - (int64_t)b * p.K);
     const int start = k * p.chunk_len;
@@ -1153,21 +1160,36 @@ __device__ __forceinline__ void encode_lanes(const EncParams &p, const uint4 *__
         const uint4 *row = ent + (ct - c0) * Ls;
         const int64_t pos_last = (int64_t)b * p.N + last;
         const int32_t *src = kMode == kModeLatent ? reinterpret_cast<const int32_t *>(p.y) + pos_last : p.sym + pos_last;
+        const int32_t *isrc = kIdx ? p.idx + pos_last : nullptr;
         uint64_t x = kRansL;
         int32_t cur[kB], nxt[kB];
+        int32_t icur[kIdx ? kB : 1], inxt[kIdx ? kB : 1];
 #pragma unroll
-        for (int u = 0; u < kB; ++u) cur[u] = u < n ? __ldg(src - u * kLanes) : 0;
+        for (int u = 0; u < kB; ++u) {
+            cur[u] = u < n ? __ldg(src - u * kLanes) : 0;
+            if (kIdx) icur[u] = u < n ? __ldg(isrc - u * kLanes) : 0;
+        }
         for (int t0 = 0; t0 < nmax; t0 += kB) {
             if (t0 + 2 * kB <= n) {
 #pragma unroll
-                for (int u = 0; u < kB; ++u) nxt[u] = __ldg(src - (t0 + kB + u) * kLanes);
+                for (int u = 0; u < kB; ++u) {
+                    nxt[u] = __ldg(src - (t0 + kB + u) * kLanes);
+                    if (kIdx) inxt[u] = __ldg(isrc - (t0 + kB + u) * kLanes);
+                }
             } else {
 #pragma unroll
-                for (int u = 0; u < kB; ++u) nxt[u] = t0 + kB + u < n ? __ldg(src - (t0 + kB + u) * kLanes) : 0;
+                for (int u = 0; u < kB; ++u) {
+                    nxt[u] = t0 + kB + u < n ? __ldg(src - (t0 + kB + u) * kLanes) : 0;
+                    if (kIdx) inxt[u] = t0 + kB + u < n ? __ldg(isrc - (t0 + kB + u) * kLanes) : 0;
+                }
             }
             // this lane's symbols t0 .. t0 + 7 all lie in channel ct when the
             // position of the 8th is still at or above the channel's start
-            const bool one_channel = t0 + kB <= n && rem >= (kB - 1) * kLanes;
+            bool one_channel = t0 + kB <= n && rem >= (kB - 1) * kLanes;
+            if (kIdx) {
+#pragma unroll
+                for (int u = 0; u < kB; ++u) one_channel = one_channel && icur[u] == ct;
+            }
             if (__all_sync(0xffffffffu, one_channel)) {
                 const int32_t off = ch.y, maxv = ch.z;
                 // two halves of four: a half's entries are read before its
@@ -1218,14 +1240,48 @@ __device__ __forceinline__ void encode_lanes(const EncParams &p, const uint4 *__
                     int32_t s;
                     if (kMode == kModeLatent) s = __float2int_rn(__int_as_float(cur[u]) - __int_as_float(ch.x));
                     else s = cur[u];
-                    const int32_t value = (int32_t)((uint32_t)s - (uint32_t)ch.y);
-                    const bool oor = (uint32_t)value >= (uint32_t)ch.z;
+                    int4 cs = ch;              // the symbol's row: the layout's ...
+                    const uint4 *rs = row;
+                    bool global = false;       // ... or one outside the group
+                    if (kIdx && icur[u] != ct) {
+                        flags |= kFlagNonChannel;
+                        int c = icur[u];
+                        if ((unsigned)c >= (unsigned)p.t.C) {
+                            flags |= kFlagIndexRange;
+                            c = 0;
+                        }
+                        if (c >= c0 && c < c0 + nc) {
+                            cs = chan[c - c0];
+                            rs = ent + (c - c0) * Ls;
+                        } else {
+                            global = true;
+                            int32_t size = __ldg(p.t.sizes + c);
+                            if (size < 2 || size > p.t.L) {
+                                flags |= kFlagTable;
+                                size = size < 2 ? 2 : p.t.L;
+                            }
+                            cs = make_int4(0, __ldg(p.t.offs + c), size - 2, c);
+                        }
+                    }
+                    const int32_t value = (int32_t)((uint32_t)s - (uint32_t)cs.y);
+                    const bool oor = (uint32_t)value >= (uint32_t)cs.z;
                     if (oor) {
-                        const EscOut r = put_escape_call(x, escape_raw(value, ch.z), wrow, cap, j);
+                        const EscOut r = put_escape_call(x, escape_raw(value, cs.z), wrow, cap, j);
                         x = r.x;
                         j = r.j;
                     }
-                    enc_step<true>(x, j, wrow, cap, row[oor ? ch.z : value]);
+                    const int v = oor ? cs.z : value;
+                    uint4 e;
+                    if (kIdx && global) {
+                        const int32_t *crow = p.t.cdfs + (int64_t)cs.w * p.t.L;
+                        const uint32_t pe = pack_entry(__ldg(crow + v), __ldg(crow + v + 1), flags);
+                        const uint32_t freq = (pe >> 16) + 1u;
+                        const uint64_t m = g_magic[freq];
+                        e = make_uint4((uint32_t)m, (uint32_t)(m >> 32), freq, pe & 0xFFFFu);
+                    } else {
+                        e = rs[v];
+                    }
+                    enc_step<true>(x, j, wrow, cap, e);
                     if (t0 + u + 1 < n) {  // step to the next symbol's channel only when one follows
                         rem -= kLanes;
                         if (rem < 0) {
@@ -1240,7 +1296,10 @@ __device__ __forceinline__ void encode_lanes(const EncParams &p, const uint4 *__
                 }
             }
 #pragma unroll
-            for (int u = 0; u < kB; ++u) cur[u] = nxt[u];
+            for (int u = 0; u < kB; ++u) {
+                cur[u] = nxt[u];
+                if (kIdx) icur[u] = inxt[u];
+            }
         }
         // flush: the decoder reads the low word first
         if (n > 0) {
@@ -1280,7 +1339,8 @@ __global__ void __launch_bounds__(kThreads, 3) encode_lanes_kernel(EncParams p) 
         __syncthreads();  // the previous group's rows are no longer read
         stage_lanes<false>(p.t, c0, nc, true, smem, ls, kMode == kModeLatent ? p.medians : nullptr, flags);
         const int b = bb * W + warp;
-        if (b < p.B) encode_lanes<kMode>(p, ent, chan, c0, p.t.L - 1, (int64_t)b * p.K + k, lane, flags, my_max_used);
+        if (b < p.B)
+            encode_lanes<kMode>(p, ent, chan, c0, nc, p.t.L - 1, (int64_t)b * p.K + k, lane, flags, my_max_used);
     }
     finish_encode(p, flags, my_max_used);
 }
@@ -1334,6 +1394,28 @@ __device__ __forceinline__ int32_t dec_step(DecLane &d, const uint2 *__restrict_
     return s;
 }
 
+// dec_step for a row outside the staged group (explicit indexes): a binary
+// search of the row's CDF in global memory, the full-table decode's lookup.
+__device__ __forceinline__ int32_t dec_step_global(DecLane &d, const TableArgs &t, int c, int maxv,
+                                                   const uint32_t *__restrict__ base, int rm1, uint32_t &flags) {
+    const uint32_t slot = (uint32_t)d.x & 0xFFFFu;
+    const int32_t *row = t.cdfs + (int64_t)c * t.L;
+    int lo = 0, hi = maxv;
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((uint32_t)__ldg(row + mid + 1) > slot) hi = mid;
+        else lo = mid + 1;
+    }
+    const uint32_t e = pack_entry(__ldg(row + lo), __ldg(row + lo + 1), flags);
+    const uint32_t st = e & 0xFFFFu, freq = (e >> 16) + 1u;
+    d.x = (uint64_t)freq * (d.x >> 16) + (uint64_t)(int64_t)(int32_t)(slot - st);
+    const bool need = d.x < kRansL;
+    d.x = need ? (d.x << 32) | (uint64_t)d.cand : d.x;
+    d.word += need ? 1 : 0;
+    d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+    return lo;
+}
+
 // Escape decode inlined into the decode loop (warp_ans_kernel.cu:308-325):
 // the count nibbles, then the value nibbles low to high.  Words are read
 // straight from the lane's stream, bounded by its rounds; returns false on
@@ -1374,11 +1456,17 @@ __device__ __forceinline__ bool dec_escape(DecLane &d, const uint32_t *__restric
 // group when HW is a multiple of 128) has no channel bookkeeping; the ragged
 // end and groups that cross a channel step per symbol.  A lane that
 // consumes more words than its chunk holds marks the payload corrupt.
+//
+// With explicit indexes (kModeIdx) a group also needs its indexes to be the
+// channel layout (warp vote); otherwise it steps per symbol, and a symbol
+// whose row lies outside the staged group searches that row in global
+// memory.
 template <int kMode, bool kPair>
 __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t *__restrict__ ent,
                                              const int4 *__restrict__ chan, const uint2 *__restrict__ lut, int shift,
-                                             int c0, int Ls, int64_t chunk, int lane, uint32_t &flags) {
+                                             int c0, int nc, int Ls, int64_t chunk, int lane, uint32_t &flags) {
     constexpr int kG = 4;
+    constexpr bool kIdx = kMode == kModeIdx;
     const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
     const int b = (int)(chunk / p.K);
     const int k = (int)(chunk - (int64_t)b * p.K);
@@ -1425,6 +1513,12 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
     const int64_t pos0 = (int64_t)b * p.N + first;
     int32_t *orow = kMode == kModeLatent ? nullptr : p.out + pos0;
     float *yrow = kMode == kModeLatent ? p.y_out + pos0 : nullptr;
+    const int32_t *irow = kIdx ? p.idx + pos0 : nullptr;
+    int32_t icur[kIdx ? kG : 1], inxt[kIdx ? kG : 1];
+    if (kIdx) {
+#pragma unroll
+        for (int u = 0; u < kG; ++u) icur[u] = u < n ? __ldg(irow + (int64_t)u * kLanes) : 0;
+    }
     bool bad = false;
     auto finish_symbol = [&](int32_t s, int t) {
         const bool esc = s == ch.z;
@@ -1438,17 +1532,19 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
         if (kMode == kModeLatent) yrow[(int64_t)t * kLanes] = __int2float_rn(sym) + __int_as_float(ch.x);
         else orow[(int64_t)t * kLanes] = sym;
     };
-    auto finish_symbol_guarded = [&](int32_t s, int t, bool live) {
-        const bool esc = live && s == ch.z;
+    // cs: the symbol's row ({median, offset, maxv}); ch unless an explicit
+    // index names another row
+    auto finish_symbol_guarded = [&](int32_t s, int t, bool live, const int4 &cs) {
+        const bool esc = live && s == cs.z;
         if (__any_sync(0xffffffffu, esc)) {
             if (esc) {
-                bad |= !dec_escape(d, base, rounds, ch.z, s);
+                bad |= !dec_escape(d, base, rounds, cs.z, s);
                 d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
             }
         }
         if (live) {
-            const int32_t sym = (int32_t)((uint32_t)s + (uint32_t)ch.y);
-            if (kMode == kModeLatent) yrow[(int64_t)t * kLanes] = __int2float_rn(sym) + __int_as_float(ch.x);
+            const int32_t sym = (int32_t)((uint32_t)s + (uint32_t)cs.y);
+            if (kMode == kModeLatent) yrow[(int64_t)t * kLanes] = __int2float_rn(sym) + __int_as_float(cs.x);
             else orow[(int64_t)t * kLanes] = sym;
         }
     };
@@ -1463,7 +1559,14 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
     };
     for (int t = 0; t < nmax; t += kG) {
         asm volatile("prefetch.global.L1 [%0];" ::"l"(base + (int64_t)min(d.word + 6, rm1) * kLanes));
-        const bool one_channel = t + kG <= n && rem + (kG - 1) * kLanes < p.HW;
+        bool one_channel = t + kG <= n && rem + (kG - 1) * kLanes < p.HW;
+        if (kIdx) {
+#pragma unroll
+            for (int u = 0; u < kG; ++u) {
+                one_channel = one_channel && icur[u] == ct;
+                inxt[u] = t + kG + u < n ? __ldg(irow + (int64_t)(t + kG + u) * kLanes) : 0;
+            }
+        }
         if (__all_sync(0xffffffffu, one_channel)) {
 #pragma unroll
             for (int u = 0; u < kG; ++u) finish_symbol(dec_step<kPair>(d, lrow, row, shift, ch.z, base, rm1), t + u);
@@ -1475,13 +1578,40 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
             for (int u = 0; u < kG; ++u) {
                 const bool live = t + u < n;
                 int32_t s = 0;
-                if (live) s = dec_step<kPair>(d, lrow, row, shift, ch.z, base, rm1);
-                finish_symbol_guarded(s, t + u, live);
+                int4 cs = ch;
+                if (kIdx && live && icur[u] != ct) {
+                    flags |= kFlagNonChannel;
+                    int c = icur[u];
+                    if ((unsigned)c >= (unsigned)p.t.C) {
+                        flags |= kFlagIndexRange;
+                        c = 0;
+                    }
+                    if (c >= c0 && c < c0 + nc) {
+                        cs = chan[c - c0];
+                        s = dec_step<kPair>(d, lut + (int64_t)(c - c0) * (65536 >> shift), ent + (c - c0) * Ls, shift,
+                                            cs.z, base, rm1);
+                    } else {
+                        int32_t size = __ldg(p.t.sizes + c);
+                        if (size < 2 || size > p.t.L) {
+                            flags |= kFlagTable;
+                            size = size < 2 ? 2 : p.t.L;
+                        }
+                        cs = make_int4(0, __ldg(p.t.offs + c), size - 2, 0);
+                        s = dec_step_global(d, p.t, c, cs.z, base, rm1, flags);
+                    }
+                } else if (live) {
+                    s = dec_step<kPair>(d, lrow, row, shift, ch.z, base, rm1);
+                }
+                finish_symbol_guarded(s, t + u, live, cs);
                 if (live) {
                     rem += kLanes;
                     if (rem >= p.HW && t + u + 1 < n) next_channel();
                 }
             }
+        }
+        if (kIdx) {
+#pragma unroll
+            for (int u = 0; u < kG; ++u) icur[u] = inxt[u];
         }
     }
     if (n > 0 && (bad || d.word > rounds)) flags |= kFlagCorrupt;
@@ -1513,8 +1643,8 @@ __global__ void __launch_bounds__(kThreads) decode_lanes_kernel(DecParams p) {
         if (__syncthreads_or((int)(flags & kFlagTable))) continue;
         const int b = bb * W + warp;
         if (b < p.B)
-            decode_lanes<kMode, kPair>(p, ent, chan, lut, ls.lut_shift, c0, p.t.L - 1, (int64_t)b * p.K + k, lane,
-                                       flags);
+            decode_lanes<kMode, kPair>(p, ent, chan, lut, ls.lut_shift, c0, nc, p.t.L - 1, (int64_t)b * p.K + k,
+                                       lane, flags);
     }
     finish_decode(p, flags);
 }
@@ -1988,19 +2118,20 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     p.stage = reinterpret_cast<uint32_t *>(ws + el.stage);
     p.max_rounds_out = max_rounds;
 
-    if (mode == kModeIdx) {
-        const int64_t smem = encode_smem_bytes(C, L);
-        rc = smem <= kMaxSmemBytes ? launch_encode_full<true>(p, smem, stream) : launch_encode_full<false>(p, smem, stream);
+    // the group's rows in shared memory (every P of the reference's sweep
+    // with 16-bit CDFs of <= 66 entries), else global tables; explicit
+    // indexes outside the group's rows read theirs from global memory
+    const int64_t smem = lanes_smem(d.P, L, true).bytes;
+    if (smem <= kMaxSmemBytes) {
+        rc = mode == kModeIdx       ? launch_encode_lanes<kModeIdx>(p, smem, stream)
+             : mode == kModeChannel ? launch_encode_lanes<kModeChannel>(p, smem, stream)
+                                    : launch_encode_lanes<kModeLatent>(p, smem, stream);
+    } else if (mode == kModeIdx) {
+        const int64_t full = encode_smem_bytes(C, L);
+        rc = full <= kMaxSmemBytes ? launch_encode_full<true>(p, full, stream) : launch_encode_full<false>(p, full, stream);
     } else {
-        // the group's rows in shared memory (every P of the reference's
-        // sweep with 16-bit CDFs of <= 66 entries), else global tables
-        const int64_t smem = lanes_smem(d.P, L, true).bytes;
-        if (smem <= kMaxSmemBytes)
-            rc = mode == kModeChannel ? launch_encode_lanes<kModeChannel>(p, smem, stream)
-                                      : launch_encode_lanes<kModeLatent>(p, smem, stream);
-        else
-            rc = mode == kModeChannel ? launch_encode_group<kModeChannel>(p, stream)
-                                      : launch_encode_group<kModeLatent>(p, stream);
+        rc = mode == kModeChannel ? launch_encode_group<kModeChannel>(p, stream)
+                                  : launch_encode_group<kModeLatent>(p, stream);
     }
     if (rc) return rc;
     if (submit) {
@@ -2081,12 +2212,16 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     p.offsets = prep ? offs : nullptr;
     p.out = symbols_out;
     const int HW = N / C;
-    if (mode == kModeIdx || chunk_len % HW != 0) {
+    const int Pg = chunk_len / HW;
+    const bool lanes = chunk_len % HW == 0 && lanes_smem(Pg, L, false).bytes <= kMaxSmemBytes;
+    if (mode == kModeIdx && !lanes) {
+        const int64_t smem = decode_smem_bytes(C, L);
+        rc = smem <= kMaxSmemBytes ? launch_decode_full<kModeIdx, true>(p, smem, stream)
+                                   : launch_decode_full<kModeIdx, false>(p, smem, stream);
+    } else if (chunk_len % HW != 0) {
         const int64_t smem = decode_smem_bytes(C, L);
         const bool sm = smem <= kMaxSmemBytes;
-        if (mode == kModeIdx)
-            rc = sm ? launch_decode_full<kModeIdx, true>(p, smem, stream) : launch_decode_full<kModeIdx, false>(p, smem, stream);
-        else if (mode == kModeChannel)
+        if (mode == kModeChannel)
             rc = sm ? launch_decode_full<kModeChannel, true>(p, smem, stream)
                     : launch_decode_full<kModeChannel, false>(p, smem, stream);
         else
@@ -2095,11 +2230,13 @@ static int decode_impl(int mode, const uint8_t *packed, int64_t packed_bytes, co
     } else {
         // buckets of at most 64 slots (P <= 8) resolve two-symbol buckets
         // without a search; coarser ones keep the bucket's last symbol
-        const int Pg = chunk_len / HW;
         const int64_t smem = lanes_smem(Pg, L, false).bytes;
         const bool pair = lanes_lut_shift(Pg) <= 6;
-        if (smem <= kMaxSmemBytes) {
-            if (mode == kModeChannel)
+        if (lanes) {
+            if (mode == kModeIdx)
+                rc = pair ? launch_decode_lanes<kModeIdx, true>(p, smem, stream)
+                          : launch_decode_lanes<kModeIdx, false>(p, smem, stream);
+            else if (mode == kModeChannel)
                 rc = pair ? launch_decode_lanes<kModeChannel, true>(p, smem, stream)
                           : launch_decode_lanes<kModeChannel, false>(p, smem, stream);
             else

@@ -79,6 +79,24 @@ def test_arbitrary_indexes_and_short_rows(cuda_device):
     assert not r.index_layout_is_channel
 
 
+@pytest.mark.parametrize("B,C,HW,P,esc", [(3, 40, 97, 8, 0.02), (2, 24, 256, 3, 0.0), (2, 96, 64, 48, 0.01),
+                                          (4, 10, 33, 1, 0.05)])
+def test_mixed_indexes_fast_and_checked_paths(cuda_device, B, C, HW, P, esc):
+    # mostly the channel layout (vote-checked fast batches) with scattered
+    # positions naming another row, inside the chunk's group or outside it
+    # (rows read from global memory), escapes included
+    cdfs, sizes, offs, scales = laplacian_tables(C, seed=C * P)
+    sym = laplacian_symbols(B, C, HW, scales, seed=HW, escape_rate=esc)
+    idx = channel_indexes(B, C, HW).copy()
+    rng = np.random.default_rng(B * C + HW)
+    pos = rng.random(idx.shape) < 0.01
+    idx[pos] = rng.integers(0, C, size=int(pos.sum()))
+    near = rng.random(idx.shape) < 0.01
+    idx[near] = np.minimum(C - 1, idx[near] + 1)
+    r = _compare(sym, idx, cdfs, sizes, offs, P, cuda_device)
+    assert not r.index_layout_is_channel
+
+
 def test_extreme_symbol_values(cuda_device):
     cdfs, sizes, offs = small_tables()
     big = np.array([[2**31 - 1, -(2**31), 2**30 - 7, -(2**30) + 3] * 8], dtype=np.int32)
