@@ -65,7 +65,7 @@ constexpr int kGatherThreads = 128;
 // scatter layers: 8 x 16 input pixels per tile, of which the 6 x 14 core
 // produces a 12 x 28 output block; cout = 3 (25 taps x 3 = 75 -> npad 80)
 constexpr int kScatterTY = 8, kScatterTX = 16, kScatterCoreH = 6, kScatterCoreW = 14, kScatterCout = 3;
-constexpr int kScatterMaxCinBlocks = 4;  // scatter layers keep their weights resident: cin <= 256
+constexpr int kScatterMaxCinBlocks = 3;  // scatter layers keep their weights resident: cin <= 192
 constexpr int kGatherK = 80;         // 3 x 5 x 5 = 75, padded to 5 MMAs of K = 16
 // First layer, patch path: the tile's fp32 input window (3 channels x
 // (2 TY + 3) rows x (2 TX + 8) columns, TX <= 64) arrives by one TMA load
@@ -154,10 +154,11 @@ struct Layout {
     static constexpr int kPatchBufs = kWide ? 1 : 2;  // first layer: input window buffers
     static constexpr int kX2One = kNorm ? kBM * kNpad * 2 : 0;
     static constexpr int kX2 = kPingPong ? 2 * kX2One : kX2One;
-    // scatter buffer: fp32 words per pixel, a multiple of 4 whose quarter is
-    // odd (84 for 80 columns), so that a warp's 16-byte row stores hit every
+    // scatter buffer: per input pixel its 25 taps as 16-byte quads {3
+    // outputs, 0}: 100 words, whose quarter (25) is odd, so that 8
+    // consecutive pixels' quads (a warp's 16-byte stores and loads) hit every
     // bank group once
-    static constexpr int kSRow = ((kNpad / 4) | 1) * 4;
+    static constexpr int kSRow = 25 * 4;
     static constexpr int kSOne = kEpi == kEpiScatter ? kBM * kSRow * 4 : 0;
     static constexpr int kS = kPingPong ? 2 * kSOne : kSOne;
     // operand ring: as many stages as the shared memory left over holds
@@ -258,6 +259,13 @@ __device__ __forceinline__ void amax_flush(uint32_t *dst, uint32_t am2) {
     uint32_t am = max(am2 & 0xFFFFu, am2 >> 16) << 16;
     am = __reduce_max_sync(0xffffffffu, am);
     if (dst && (threadIdx.x & 31) == 0) atomicMax(dst, am);
+}
+
+__device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -1019,8 +1027,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                 // pixel of the 8 x 16 tile incl. a 1-pixel halo) holds its
                 // contribution to all 25 taps x 3 outputs.  Each output pixel
                 // of the 12 x 28 core block sums the 4-9 contributions that
-                // land on it; one work item = one output pixel.
-                float *S = reinterpret_cast<float *>(smem + Lay::offS + grp * Lay::kSOne);
+                // land on it.
+                const uint32_t S = smem_u32(smem + Lay::offS + grp * Lay::kSOne);
                 {
                     constexpr int kChunks = kNpad / 16;
                     uint32_t v[kChunks][16];
@@ -1028,54 +1036,70 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                     for (int c = 0; c < kChunks; ++c) tmem_ld16(d1 + c * 16, v[c]);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < kChunks; ++c) {
-                        tmem_regs_ready(v[c]);
-                        float4 *row = reinterpret_cast<float4 *>(S + m * Lay::kSRow + c * 16);
+                    for (int c = 0; c < kChunks; ++c) tmem_regs_ready(v[c]);
+                    // column 3 k + o = tap k, output o
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            row[q] = make_float4(__uint_as_float(v[c][4 * q]), __uint_as_float(v[c][4 * q + 1]),
-                                                 __uint_as_float(v[c][4 * q + 2]), __uint_as_float(v[c][4 * q + 3]));
+                    for (int k = 0; k < 25; ++k) {
+                        constexpr int kO = kScatterCout;
+                        st_shared_v4(S + (m * Lay::kSRow + k * 4) * 4, v[(kO * k) / 16][(kO * k) % 16],
+                                     v[(kO * k + 1) / 16][(kO * k + 1) % 16], v[(kO * k + 2) / 16][(kO * k + 2) % 16],
+                                     0u);
                     }
                 }
                 named_barrier_sync(gbar, Lay::kGroupThreads);
-                float *out = reinterpret_cast<float *>(p.out);
-                const int64_t plane = (int64_t)p.Hout * p.Wout;
-                const float b0 = s_bias[0], b1 = s_bias[1], b2 = s_bias[2];
-                for (int item = threadIdx.x & (Lay::kGroupThreads - 1); item < kScatterCoreH * kScatterCoreW * 4;
-                     item += Lay::kGroupThreads) {
-                    const int core = item >> 2, py = (item >> 1) & 1, px = item & 1;
-                    const int ci = core / kScatterCoreW, cj = core - ci * kScatterCoreW;
-                    const int oyv = 2 * (gy0 + ci) + py, oxv = 2 * (gx0 + cj) + px;
-                    if (oyv >= p.Hout || oxv >= p.Wout) continue;
-                    float a0 = b0, a1 = b1, a2 = b2;
+                // One thread per core pixel (ci, cj): its 2 x 2 output pixels
+                // (phase py, px) sum the taps ky = py, py + 2, .. and kx = px,
+                // px + 2, .. of input pixel (ci + 1 + dr, cj + 1 + dc) with
+                // dr = 1 - (ky - py) / 2, dc = 1 - (kx - px) / 2: every offset
+                // is a constant, each tap one 16-byte load.  Taps are added
+                // in ky-major order, as the 4-9 terms of each output pixel.
+                const int t = threadIdx.x & (Lay::kGroupThreads - 1);
+                if (t < kScatterCoreH * kScatterCoreW) {
+                    const int ci = t / kScatterCoreW, cj = t - ci * kScatterCoreW;
+                    const uint32_t sb = S + (((ci + 1) * kScatterTX + cj + 1) * Lay::kSRow) * 4;
+                    float acc[2][2][kScatterCout];
 #pragma unroll
-                    for (int ty = 0; ty < 3; ++ty) {
-                        const int ky = py + 2 * ty;
-                        if (ky < 5) {
-                            const int r = ci + 1 + ((py + 2 - ky) >> 1);
+                    for (int q = 0; q < 4; ++q)
 #pragma unroll
-                            for (int tx = 0; tx < 3; ++tx) {
-                                const int kx = px + 2 * tx;
-                                if (kx < 5) {
-                                    const int col = cj + 1 + ((px + 2 - kx) >> 1);
-                                    const float *src =
-                                        S + (r * kScatterTX + col) * Lay::kSRow + (ky * 5 + kx) * kScatterCout;
-                                    a0 += src[0];
-                                    a1 += src[1];
-                                    a2 += src[2];
-                                }
+                        for (int o = 0; o < kScatterCout; ++o) acc[q >> 1][q & 1][o] = s_bias[o];
+#pragma unroll
+                    for (int ky = 0; ky < 5; ++ky) {
+#pragma unroll
+                        for (int kx = 0; kx < 5; ++kx) {
+                            const int dr = (2 - ky + (ky & 1)) >> 1, dc = (2 - kx + (kx & 1)) >> 1;
+                            const float4 q =
+                                ld_shared_v4f(sb + ((dr * kScatterTX + dc) * Lay::kSRow + (ky * 5 + kx) * 4) * 4);
+                            float *a = acc[ky & 1][kx & 1];
+                            a[0] += q.x;
+                            a[1] += q.y;
+                            a[2] += q.z;
+                        }
+                    }
+                    float *out = reinterpret_cast<float *>(p.out);
+                    const int64_t plane = (int64_t)p.Hout * p.Wout;
+                    const int oy0 = 2 * (gy0 + ci), ox0 = 2 * (gx0 + cj);
+                    // 8-byte pairs when every row starts 8-byte aligned
+                    const bool pair = ox0 + 1 < p.Wout && (p.Wout & 1) == 0;
+#pragma unroll
+                    for (int py = 0; py < 2; ++py) {
+                        const int oyv = oy0 + py;
+                        if (oyv >= p.Hout || ox0 >= p.Wout) continue;
+#pragma unroll
+                        for (int o = 0; o < kScatterCout; ++o) {
+                            float y0 = acc[py][0][o], y1 = acc[py][1][o];
+                            if (p.clamp) {
+                                y0 = fminf(fmaxf(y0, 0.f), 1.f);
+                                y1 = fminf(fmaxf(y1, 0.f), 1.f);
+                            }
+                            float *dst = out + ((int64_t)b * kScatterCout + o) * plane + (int64_t)oyv * p.Wout + ox0;
+                            if (pair) {
+                                *reinterpret_cast<float2 *>(dst) = make_float2(y0, y1);
+                            } else {
+                                dst[0] = y0;
+                                if (ox0 + 1 < p.Wout) dst[1] = y1;
                             }
                         }
                     }
-                    if (p.clamp) {
-                        a0 = fminf(fmaxf(a0, 0.f), 1.f);
-                        a1 = fminf(fmaxf(a1, 0.f), 1.f);
-                        a2 = fminf(fmaxf(a2, 0.f), 1.f);
-                    }
-                    float *o = out + (int64_t)b * kScatterCout * plane + (int64_t)oyv * p.Wout + oxv;
-                    o[0] = a0;
-                    o[plane] = a1;
-                    o[2 * plane] = a2;
                 }
                 named_barrier_sync(gbar, Lay::kGroupThreads);  // S is rewritten by the next tile
             } else if (kNorm) {
