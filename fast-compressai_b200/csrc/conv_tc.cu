@@ -1646,24 +1646,49 @@ __global__ void amax_bf16_kernel(const uint4 *__restrict__ x, int64_t n8, uint32
     if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));
 }
 
-__global__ void quantize_e4m3_kernel(const uint4 *__restrict__ x, uint2 *__restrict__ out, int64_t n8,
-                                     const uint32_t *__restrict__ amax_bits, float *__restrict__ scale_out) {
+// e4m3 code of one bf16 value x under the reference's rule (the scale as
+// below): e4m3(clamp(x / scale, +-448)), x / scale a true division.  A NaN
+// input divides to the GPU's canonical (positive) NaN, which torch.clamp
+// passes through: code 0x7F whatever the input's sign.
+__device__ __forceinline__ uint32_t e4m3_code(float x, float scale) {
+    if (x != x) return 0x7Fu;
+    float2 f;
+    f.x = fminf(fmaxf(__fdiv_rn(x, scale), -448.f), 448.f);
+    f.y = 0.f;
+    return (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3) & 0xFFu;
+}
+
+// The output depends on the input's 16 bits alone, and the rule is odd in x
+// (a negative x, -0 included, gives the code of |x| with the sign bit) but
+// for NaN (0x7F, a code no number produces).  So
+// each CTA first quantises the 32768 non-negative bf16 patterns into a
+// shared-memory table with the same expression, then maps every element
+// through it: one table read per element instead of a division, and the
+// same bytes as quantising each element directly.
+constexpr int kQuantThreads = 1024;
+__global__ void __launch_bounds__(kQuantThreads) quantize_e4m3_kernel(const uint4 *__restrict__ x, uint2 *__restrict__ out,
+                                                                      int64_t n8, const uint32_t *__restrict__ amax_bits,
+                                                                      float *__restrict__ scale_out) {
+    __shared__ uint8_t lut[32768];
     // the reference divides by the Python float 448, which PyTorch's CUDA
     // division by a host scalar computes as amax * fl(1 / 448); the elements
     // are then divided by the scale tensor (a true division)
     const float scale = fmaxf(__fmul_rn(__uint_as_float(*amax_bits), 1.0f / 448.0f), 1.17549435e-38f);
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+    for (int i = threadIdx.x; i < 32768; i += blockDim.x) lut[i] = (uint8_t)e4m3_code(__uint_as_float((uint32_t)i << 16), scale);
+    __syncthreads();
+    auto code = [&](uint32_t h) -> uint32_t {
+        const uint32_t c = lut[h & 0x7FFFu];
+        return c == 0x7Fu ? c : c | ((h >> 8) & 0x80u);
+    };
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
         const uint4 v = x[i];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint32_t q[2] = {0u, 0u};
+        uint32_t q[2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float2 f;
-            f.x = fminf(fmaxf(__fdiv_rn(__uint_as_float(w[j] << 16), scale), -448.f), 448.f);
-            f.y = fminf(fmaxf(__fdiv_rn(__uint_as_float(w[j] & 0xFFFF0000u), scale), -448.f), 448.f);
-            const uint32_t pair = (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
-            q[j >> 1] |= pair << (16 * (j & 1));
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t a = w[2 * j], b = w[2 * j + 1];
+            q[j] = code(a & 0xFFFFu) | (code(a >> 16) << 8) | (code(b & 0xFFFFu) << 16) | (code(b >> 16) << 24);
         }
         out[i] = make_uint2(q[0], q[1]);
     }
@@ -1952,7 +1977,11 @@ int fcai_quantize_e4m3(const void *input_bf16, void *output_e4m3, float *scale_o
                                                                         amax_work);
         FCAI_CUDA_TRY(cudaGetLastError());
     }
-    ct::quantize_e4m3_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+    // one CTA of 1024 threads per SM (each builds its 32 KB table once),
+    // fewer for small inputs
+    const int64_t qblocks =
+        std::min<int64_t>((n8 + ct::kQuantThreads - 1) / ct::kQuantThreads, (int64_t)fcai::sm_count());
+    ct::quantize_e4m3_kernel<<<(unsigned)qblocks, ct::kQuantThreads, 0, stream>>>(
         static_cast<const uint4 *>(input_bf16), static_cast<uint2 *>(output_e4m3), n8, amax_work, scale_out);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;

@@ -61,6 +61,27 @@ def test_quantiser_matches_the_reference_rule(cuda_device, shape, spread):
     assert sz.item() == FP8_SCALE_MIN and int(qz.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("amax", [1.0, 300.0, 1e-30, 3.0e38, 0.0])
+def test_quantiser_every_bf16_pattern(cuda_device, amax):
+    # all 65536 bf16 bit patterns (zeros, subnormals, infinities and NaNs
+    # included) through the quantiser with a given amax, against the
+    # reference's rule evaluated by torch with the scale the call wrote
+    x = torch.arange(65536, dtype=torch.int32, device=cuda_device).to(torch.int16).view(torch.bfloat16)
+    q = torch.empty(65536, dtype=torch.uint8, device=cuda_device)
+    scal = torch.tensor([0.0, amax], dtype=torch.float32, device=cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    _native.check(_native.lib().fcai_quantize_e4m3(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(q.data_ptr()),
+                                                   ctypes.c_void_p(scal.data_ptr()),
+                                                   ctypes.c_void_p(scal.data_ptr() + 4), 1, 65536,
+                                                   ctypes.c_void_p(stream)))
+    torch.cuda.synchronize()
+    scale = scal[0:1]
+    assert scale.item() == max(float(torch.tensor(amax, dtype=torch.float32) * torch.tensor(1.0 / 448.0)),
+                               FP8_SCALE_MIN)
+    ref = torch.clamp(x.float() / scale, -FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert torch.equal(q, ref), f"{int((q != ref).sum())} patterns differ"
+
+
 def _ref_fp8_layer(x_nchw, conv, gdn, out_bf16=True):
     """The scaled GEMM on dequantised e4m3 operands, then bias and (I)GDN."""
     xq, xs = _ref_quant(_bf(x_nchw))
