@@ -111,7 +111,8 @@ int fcai_layer_forward(const fcai_layer *layer, int32_t batch, int32_t h_in, int
  * _symmetric_scale / _quantize_fp8 (backends/pytorch/fp8_operators.py:44-51):
  * scale = max(amax(|x|) * fl(1 / 448), FLT_MIN) (the reference's amax / 448.0,
  * which PyTorch's CUDA division by a host scalar evaluates this way),
- * out = e4m3(clamp(x / scale, +-448)) rounded to nearest even.  Writes the
+ * out = e4m3(clamp(x / scale, +-448)) rounded to nearest even (NaN inputs give
+ * 0x7F of either sign, as torch computes it on the GPU).  Writes the
  * scale to *scale_out (device).  With amax_ready = 0 the call computes the
  * amax into *amax_work (device, 4 bytes, cleared first); with amax_ready != 0,
  * *amax_work already holds it (the producing layer's amax_out) and the call
