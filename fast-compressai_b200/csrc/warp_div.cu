@@ -1348,13 +1348,31 @@ __global__ void __launch_bounds__(kThreads, 3) encode_lanes_kernel(EncParams p) 
 // One decode step (warp_ans_kernel.cu:219-329 semantics): the bucket of the
 // slot names the symbol unless the slot lies past the bucket's first
 // symbol, then a binary search over the rest of the bucket finds it.  The
-// refill word is `cand`, loaded during the previous step; reads are clamped
-// to the chunk's last round.
+// refill word is `cand` (word `word` of the lane's stream) and the one after
+// it `cand2`: a refill moves `cand2` up and loads the next word, so each
+// load has a whole renormalisation interval to arrive and steps without a
+// refill load nothing.  Reads are clamped to the chunk's last round.
 struct DecLane {
     uint64_t x;
     int word;
-    uint32_t cand;
+    uint32_t cand, cand2;
 };
+
+// cand / cand2 from the lane's stream at d.word (after an escape's reads)
+__device__ __forceinline__ void dec_reload(DecLane &d, const uint32_t *__restrict__ base, int rm1) {
+    d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+    d.cand2 = __ldg(base + (int64_t)min(d.word + 1, rm1) * kLanes);
+}
+
+__device__ __forceinline__ void dec_refill(DecLane &d, const uint32_t *__restrict__ base, int rm1) {
+    const bool need = d.x < kRansL;
+    d.x = need ? (d.x << 32) | (uint64_t)d.cand : d.x;
+    if (need) {
+        ++d.word;
+        d.cand = d.cand2;
+        d.cand2 = __ldg(base + (int64_t)min(d.word + 1, rm1) * kLanes);
+    }
+}
 
 template <bool kPair>
 __device__ __forceinline__ int32_t dec_step(DecLane &d, const uint2 *__restrict__ lrow, const uint32_t *__restrict__ row,
@@ -1387,10 +1405,7 @@ __device__ __forceinline__ int32_t dec_step(DecLane &d, const uint2 *__restrict_
     }
     const uint32_t freq = endm1 - st + 1u;
     d.x = (uint64_t)freq * (d.x >> 16) + (uint64_t)(int64_t)(int32_t)(slot - st);
-    const bool need = d.x < kRansL;
-    d.x = need ? (d.x << 32) | (uint64_t)d.cand : d.x;
-    d.word += need ? 1 : 0;
-    d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+    dec_refill(d, base, rm1);
     return s;
 }
 
@@ -1409,10 +1424,7 @@ __device__ __forceinline__ int32_t dec_step_global(DecLane &d, const TableArgs &
     const uint32_t e = pack_entry(__ldg(row + lo), __ldg(row + lo + 1), flags);
     const uint32_t st = e & 0xFFFFu, freq = (e >> 16) + 1u;
     d.x = (uint64_t)freq * (d.x >> 16) + (uint64_t)(int64_t)(int32_t)(slot - st);
-    const bool need = d.x < kRansL;
-    d.x = need ? (d.x << 32) | (uint64_t)d.cand : d.x;
-    d.word += need ? 1 : 0;
-    d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+    dec_refill(d, base, rm1);
     return lo;
 }
 
@@ -1505,7 +1517,7 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
     DecLane d;
     d.x = (uint64_t)__ldg(base) | ((uint64_t)__ldg(base + kLanes) << 32);
     d.word = 2;
-    d.cand = __ldg(base + (int64_t)min(2, rm1) * kLanes);
+    dec_reload(d, base, rm1);
     int ct = n > 0 ? first / p.HW : c0, rem = n > 0 ? first - ct * p.HW : 0;
     int4 ch = chan[ct - c0];
     const uint32_t *row = ent + (ct - c0) * Ls;
@@ -1525,7 +1537,7 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
         if (__any_sync(0xffffffffu, esc)) {  // some lane escapes: its value follows as bypass nibbles
             if (esc) {
                 bad |= !dec_escape(d, base, rounds, ch.z, s);
-                d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+                dec_reload(d, base, rm1);
             }
         }
         const int32_t sym = (int32_t)((uint32_t)s + (uint32_t)ch.y);
@@ -1539,7 +1551,7 @@ __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t 
         if (__any_sync(0xffffffffu, esc)) {
             if (esc) {
                 bad |= !dec_escape(d, base, rounds, cs.z, s);
-                d.cand = __ldg(base + (int64_t)min(d.word, rm1) * kLanes);
+                dec_reload(d, base, rm1);
             }
         }
         if (live) {
