@@ -779,8 +779,9 @@ def run_b200(args):
         # (examples/precision_configs/FactorizedPrior of the reference, kept as
         # a test fixture): convolutions it maps to fp8 run the e4m3 kernels
         # where one exists, everything else bf16.  The fixture's model
-        # fingerprint is rewritten for this random-init model.  Same step,
-        # timing and L2 flush as the headline.
+        # fingerprint is rewritten for this random-init model.  Same step and
+        # timing as the headline: batches overlapped (compress_async), the two
+        # resident inputs alternating, no L2 flush.
         pmap = None
         fixture = ROOT / "tests" / "golden" / "precision_map_factorized.json"
         if not args.no_precision_map and fixture.exists():
@@ -795,27 +796,35 @@ def run_b200(args):
                 mp = Path(td) / "map.json"
                 mp.write_text(json.dumps(data))
                 fast_pm = fast_compressai.accelerate(model, P=args.p_ch, device=str(dev), precision_config_path=str(mp))
-            for _ in range(max(args.warmup, 1)):
-                out_pm = fast_pm.compress(x)
-                x_hat_pm = fast_pm.decompress(out_pm["strings"], out_pm["shape"])["x_hat"]
-            pm_ev = []
-            for _ in range(args.steps):
-                flush.fill_(1.0)
+            def run_overlap_pm(nsteps):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record()
-                out_pm = fast_pm.compress(x)
-                x_hat_pm = fast_pm.decompress(out_pm["strings"], out_pm["shape"])["x_hat"]
+                pending = fast_pm.compress_async(inputs[0])
+                o = None
+                for k in range(nsteps):
+                    o = pending.result()
+                    if k + 1 < nsteps:
+                        pending = fast_pm.compress_async(inputs[(k + 1) % 2])
+                    fast_pm.decompress(o["strings"], o["shape"])
                 b.record()
-                pm_ev.append((a, b))
-            torch.cuda.synchronize()
-            pm_ms = sum(a.elapsed_time(b) for a, b in pm_ev) / len(pm_ev)
+                b.synchronize()
+                return a.elapsed_time(b), o
+
+            run_overlap_pm(max(args.warmup, 3))
+            pm_total, _ = run_overlap_pm(args.steps)
+            pm_ms = pm_total / args.steps
+            # quality and payload size on x itself, after the timed region
+            out_pm = fast_pm.compress(x)
+            x_hat_pm = fast_pm.decompress(out_pm["strings"], out_pm["shape"])["x_hat"]
             rep_pm = fast_pm.acceleration_report
             pmap = {
                 "value": in_bytes / (pm_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": pm_ms,
+                "ratio_vs_headline_value": ms_per_step / pm_ms,
                 "psnr_drop_db_vs_fp32": psnr(x_ref, xs) - psnr(x_hat_pm[:nq], xs),
                 "payload_bytes_ratio_vs_headline": out_pm["strings"][0].packed.numel() / packed_bytes,
                 "fp8_modules": [m for m, _, got, _ in rep_pm.precision_applications if got == "fp8"],
-                "note": "per rank, not gathered; the reference's example map with its fingerprint rewritten",
+                "note": "per rank, not gathered; the reference's example map with its fingerprint rewritten; timed "
+                        "like the headline value (batches overlapped, no L2 flush)",
             }
             del fast_pm
 
