@@ -89,6 +89,7 @@ struct ConvParams {
     int step_x, step_y;                               // tile origin step (TX/TY, or the scatter core)
     int clamp;                                        // scatter epilogue: clamp to [0, 1]
     int stride;                                       // input step per GEMM pixel (2 conv, 1 deconv)
+    int phase_major;                                  // tile order: phase slowest (see tile_coords)
     int cin, cout, cin_blocks;
     int out_c0, cout_total;                           // fp32 NCHW output: first channel written, channels per image
     int Hout, Wout, out_step;                         // output tensor size, output step per GEMM pixel
@@ -232,13 +233,25 @@ struct Layout {
     static_assert(kNpad % 16 == 0 && kNpad >= 16 && kNpad <= 256, "MMA N");
 };
 
+// Tile order: x fastest, then y, then phase, then image (an image's phases
+// close together in time, so its input stays in L2); or, with phase_major
+// (transposed IGDN layers only; other instances compile without the
+// branch), image before phase: the CTAs' round-robin shares then hold about
+// one tile of each phase (9, 6, 6 and 4 taps) instead of runs of one phase,
+// which balances layers of few tiles per CTA.
+template <bool kPhaseMajor>
 __device__ __forceinline__ void tile_coords(const ConvParams &p, int tile, int &b, int &ph, int &gy0, int &gx0) {
     const int tx = tile % p.tiles_x;
     int rest = tile / p.tiles_x;
     const int ty = rest % p.tiles_y;
     rest /= p.tiles_y;
-    ph = rest % p.phases;
-    b = rest / p.phases;
+    if (kPhaseMajor && p.phase_major) {
+        b = rest % p.B;
+        ph = rest / p.B;
+    } else {
+        ph = rest % p.phases;
+        b = rest / p.phases;
+    }
     gy0 = ty * p.step_y;
     gx0 = tx * p.step_x;
 }
@@ -459,7 +472,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             bool stop = false;
             for (int tile = unit0; tile < p.tiles_total && !stop; tile += unit_step) {
                 int b, ph, gy0, gx0;
-                tile_coords(p, tile, b, ph, gy0, gx0);
+                tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
                 gx0 += sub_x;
                 const Taps &tp = p.taps[ph];
                 for (int t = 0; t < tp.n && !stop; ++t) {
@@ -506,7 +519,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             int last_round[2] = {-1, -1};
             for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
                 int b, ph, gy0, gx0;
-                tile_coords(p, tile, b, ph, gy0, gx0);
+                tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
                 const int pb = (int)(it % Lay::kPatchBufs);
                 const uint32_t r = it / Lay::kPatchBufs;
                 if (!mbar_wait(&pempty[pb], (r & 1) ^ 1, abort, kWaitNs)) {
@@ -549,7 +562,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                     consts = true;
                 }
                 int b, ph, gy0, gx0;
-                tile_coords(p, tile, b, ph, gy0, gx0);
+                tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
                 const int buf = j % Lay::kAccBufs;
                 const uint32_t use = j / Lay::kAccBufs;
                 if (!wait_for<W>(&acce[buf], (use & 1) ^ 1, abort, kPair)) {
@@ -658,7 +671,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             int j = 0;
             for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
                 int b, ph, gy0, gx0;
-                tile_coords(p, tile, b, ph, gy0, gx0);
+                tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
                 const int buf = j & 1;
                 const uint32_t use = j >> 1;
                 if (threadIdx.x == 0) {
@@ -831,7 +844,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
             int j = 0;
             for (int tile = unit0; tile < p.tiles_total; tile += unit_step, ++j) {
                 int b, ph, gy0, gx0;
-                tile_coords(p, tile, b, ph, gy0, gx0);
+                tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
                 const int buf = j & 1;
                 const uint32_t use = j >> 1;
                 if (threadIdx.x == 0) {
@@ -999,7 +1012,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
         for (int tile = unit0 + grp * unit_step; tile < p.tiles_total;
              tile += Lay::kGroups * unit_step, j += Lay::kGroups, ++gj) {
             int b, ph, gy0, gx0;
-            tile_coords(p, tile, b, ph, gy0, gx0);
+            tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
             gx0 += sub_x;
             const int buf = j % Lay::kAccBufs;
             const uint32_t use = j / Lay::kAccBufs;
@@ -1365,7 +1378,7 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
         uint32_t it = 0;
         for (int tile = blockIdx.x; tile < p.tiles_total && !*abort; tile += gridDim.x, ++it) {
             int b, ph, gy0, gx0;
-            tile_coords(p, tile, b, ph, gy0, gx0);
+            tile_coords<kEpi == kEpiIgdn>(p, tile, b, ph, gy0, gx0);
             const int s = it % kStages;
             const uint32_t r = it / kStages;
             if (!mbar_wait(&empty[s], (r & 1) ^ 1, abort, kWaitNs)) {
@@ -1791,6 +1804,10 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     ConvParams p{};
     p.B = batch;
     p.phases = deconv && !scatter ? 4 : 1;
+    // phase-major tile order where the whole input is a small part of the
+    // 126 MB L2 (every phase re-reads it; measured: it paid at 14 MB, g_s.0
+    // at batch 24, and cost 1.6% at 38 MB, g_s.2)
+    p.phase_major = p.phases == 4 && (int64_t)batch * h_in * w_in * L->cin * 2 <= (24ll << 20) ? 1 : 0;
     p.GH = deconv ? h_in : ho;
     p.GW = deconv ? w_in : wo;
     if (scatter) {
