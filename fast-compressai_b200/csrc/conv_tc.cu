@@ -84,12 +84,27 @@ struct Taps {
     uint8_t w[25];
 };
 
+// Division by a per-launch constant d >= 1 as a multiply and shift, exact for
+// 0 <= n < 2^31 (Granlund and Montgomery, "Division by invariant integers
+// using multiplication", 1994, with N = 31): l = ceil(log2 d),
+// m = floor(2^(31 + l) / d) + 1 < 2^32, n / d = (n * m) >> (31 + l).
+struct FastDiv {
+    uint32_t m, s;
+};
+static inline FastDiv make_fastdiv(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    return FastDiv{(uint32_t)((1ull << (31 + l)) / d + 1), 31 + l};
+}
+__device__ __forceinline__ int fdiv(int n, FastDiv f) { return (int)(((uint64_t)(uint32_t)n * f.m) >> f.s); }
+
 struct ConvParams {
     int B, phases, tiles_x, tiles_y, TY, TX, GH, GW;  // per-phase GEMM pixel grid
     int step_x, step_y;                               // tile origin step (TX/TY, or the scatter core)
     int clamp;                                        // scatter epilogue: clamp to [0, 1]
     int stride;                                       // input step per GEMM pixel (2 conv, 1 deconv)
     int phase_major;                                  // tile order: phase slowest (see tile_coords)
+    FastDiv div_tx, div_ty, div_ph, div_b;            // tiles_x, tiles_y, phases, B
     int cin, cout, cin_blocks;
     int out_c0, cout_total;                           // fp32 NCHW output: first channel written, channels per image
     int Hout, Wout, out_step;                         // output tensor size, output step per GEMM pixel
@@ -241,16 +256,17 @@ struct Layout {
 // which balances layers of few tiles per CTA.
 template <bool kPhaseMajor>
 __device__ __forceinline__ void tile_coords(const ConvParams &p, int tile, int &b, int &ph, int &gy0, int &gx0) {
-    const int tx = tile % p.tiles_x;
-    int rest = tile / p.tiles_x;
-    const int ty = rest % p.tiles_y;
-    rest /= p.tiles_y;
+    int rest = fdiv(tile, p.div_tx);
+    const int tx = tile - rest * p.tiles_x;
+    int r2 = fdiv(rest, p.div_ty);
+    const int ty = rest - r2 * p.tiles_y;
+    rest = r2;
     if (kPhaseMajor && p.phase_major) {
-        b = rest % p.B;
-        ph = rest / p.B;
+        ph = fdiv(rest, p.div_b);
+        b = rest - ph * p.B;
     } else {
-        ph = rest % p.phases;
-        b = rest / p.phases;
+        b = fdiv(rest, p.div_ph);
+        ph = rest - b * p.phases;
     }
     gy0 = ty * p.step_y;
     gx0 = tx * p.step_x;
@@ -1843,6 +1859,10 @@ int fcai_layer_forward(const fcai_layer *L, int32_t batch, int32_t h_in, int32_t
     p.clamp = L->clamp01 ? 1 : 0;
     p.tiles_x = (p.GW + p.step_x - 1) / p.step_x;
     p.tiles_y = (p.GH + p.step_y - 1) / p.step_y;
+    p.div_tx = make_fastdiv((uint32_t)p.tiles_x);
+    p.div_ty = make_fastdiv((uint32_t)p.tiles_y);
+    p.div_ph = make_fastdiv((uint32_t)p.phases);
+    p.div_b = make_fastdiv((uint32_t)batch);
     p.stride = deconv ? 1 : 2;
     p.cin = L->cin;
     p.cout = L->cout;
