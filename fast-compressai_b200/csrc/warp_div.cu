@@ -417,6 +417,7 @@ struct EncParams {
     unsigned long long *offsets;
     uint32_t *stage;
     uint32_t *max_rounds_out;
+    long long *status_out;  // optional: a mapped host slot that also receives the 8 status words
 };
 
 constexpr int kPrefetch = 16;  // symbols each lane loads ahead of the coding chain
@@ -586,6 +587,9 @@ __device__ __forceinline__ void finish_encode(const EncParams &p, uint32_t flags
         ctl->flags = 0;
         ctl->max_used = 0;
         ctl->done = 0;
+        // the host's copy, visible to it once the kernel has completed
+        if (p.status_out)
+            for (int i = 0; i < 8; ++i) p.status_out[i] = ctl->status[i];
     }
 }
 
@@ -2069,7 +2073,7 @@ static int encode_info_from_status(const Dims &d, const EncLayout &el, const lon
 
 // How an encode returns its status words to the host.
 enum class StatusPath {
-    kMapped,  // one-warp kernel into the stream's mapped pinned slot, then a stream wait
+    kMapped,  // the encode's last CTA writes the stream's mapped pinned slot, then a stream wait
     kSubmit,  // as kMapped into the second slot, collected by fcai_warp_div_encode_finish
     kCopy,    // cudaMemcpyAsync into the caller's stack, then a stream wait: creates
               // nothing (no pinned slot, no event) on any call
@@ -2129,6 +2133,9 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     p.offsets = reinterpret_cast<unsigned long long *>(ws + el.offsets);
     p.stage = reinterpret_cast<uint32_t *>(ws + el.stage);
     p.max_rounds_out = max_rounds;
+    // the last CTA writes the status words to the stream's mapped slot itself
+    // (no copy kernel); the no-allocation path copies them with the stream
+    p.status_out = path == StatusPath::kCopy ? nullptr : (submit ? ms.dev + 8 : ms.dev);
 
     // the group's rows in shared memory (every P of the reference's sweep
     // with 16-bit CDFs of <= 66 entries), else global tables; explicit
@@ -2147,8 +2154,6 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     }
     if (rc) return rc;
     if (submit) {
-        status_to_host_kernel<<<1, 32, 0, stream>>>(p.ctrl->status, ms.dev + 8, 8);
-        FCAI_CUDA_TRY(cudaGetLastError());
         FCAI_CUDA_TRY(cudaEventRecord(ms.done, stream));
         *ms.pending = 1;
         return FCAI_OK;
@@ -2157,8 +2162,9 @@ static int encode_impl(int mode, const int32_t *symbols, const int32_t *indexes,
     if (path == StatusPath::kCopy) {
         FCAI_CUDA_TRY(cudaMemcpyAsync(status, p.ctrl->status, sizeof(status), cudaMemcpyDeviceToHost, stream));
         FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
-    } else if ((rc = read_status(p.ctrl->status, 8, stream, status))) {
-        return rc;
+    } else {
+        FCAI_CUDA_TRY(cudaStreamSynchronize(stream));
+        for (int i = 0; i < 8; ++i) status[i] = ms.host[i];
     }
     return encode_info_from_status(d, el, status, workspace_bytes, info);
 }

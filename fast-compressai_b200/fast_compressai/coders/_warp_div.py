@@ -122,7 +122,7 @@ def _run_encode(B: int, N: int, C: int, P: int, dev: torch.device, call) -> Enco
         for attempt in range(2):
             ws = workspace("encode", dev, stream, nbytes)
             rc = call(lib, ws, max_rounds, info, stream)
-            _native.count_launches(2)  # the encode and the copy of its status words
+            _native.count_launches(1)  # the encode (its last CTA also writes the status words to the host)
             if rc == _native.FCAI_ERR_WORKSPACE and attempt == 0 and info.required_workspace_bytes > ws.numel():
                 nbytes = info.required_workspace_bytes
                 continue
@@ -168,7 +168,7 @@ def encode_latent_submit(y: torch.Tensor, medians: torch.Tensor, cdfs: torch.Ten
             ws.numel(), _ptr(max_rounds), stream)
         if rc:
             _native.check(rc)
-        _native.count_launches(2)
+        _native.count_launches(1)
     return PendingEncode(B, N, C, int(P), dev, stream, ws, max_rounds, (y, medians, cdfs, cdf_sizes, offsets))
 
 

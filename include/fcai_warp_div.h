@@ -138,7 +138,8 @@ int fcai_warp_div_encode_latent(const float *y, const float *medians, int32_t B,
 
 /* The encode of fcai_warp_div_encode_latent in two halves, so that the
  * host's wait for the payload size overlaps device work.  _submit enqueues
- * the encode and the copy of its status words and returns at once (same
+ * the encode (its last CTA writes the status words to the stream's mapped
+ * pinned slot) and returns at once (same
  * arguments, no info); the caller may then enqueue other work on the stream
  * (the next batch's analysis transform, an earlier batch's decode).
  * _finish waits for the submitted encode alone, not for that later work,
