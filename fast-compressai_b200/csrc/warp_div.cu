@@ -1069,27 +1069,34 @@ __device__ void stage_lanes(const TableArgs &t, int c0, int nc, bool encode, uns
     if (encode) return;
     const uint32_t *ent = reinterpret_cast<const uint32_t *>(smem + ls.ent);
     uint2 *lut = reinterpret_cast<uint2 *>(smem + ls.lut);
+    // A warp fills a row's buckets (or a slice of them, when the CTA has
+    // more warps than rows): lane l takes buckets l, l + 32, ..., so that a
+    // warp's stores hit consecutive words, and walks its symbol forward from
+    // one of its buckets to the next (a binary search finds the first).
     const int shift = ls.lut_shift, buckets = 65536 >> shift;
-    const int64_t all = (int64_t)nc * buckets;
-    const int64_t per = (all + blockDim.x - 1) / blockDim.x;
-    const int64_t i0 = (int64_t)threadIdx.x * per, i1 = min(all, i0 + per);
-    int c = -1, maxv = 0, s = 0;
-    const uint32_t *row = ent;
-    for (int64_t i = i0; i < i1; ++i) {
-        const int ci = (int)(i >> (16 - shift)), u = (int)(i & (buckets - 1));
-        const uint32_t first = (uint32_t)u << shift, last = first + (1u << shift) - 1u;
-        if (ci != c) {  // a new row: search the first bucket's symbol
-            c = ci;
-            maxv = chan[c].z;
-            row = ent + c * Ls;
-            s = lanes_find(row, 0, maxv, first);
+    const int warps = (int)(blockDim.x >> 5), wid = (int)(threadIdx.x >> 5), ln = (int)(threadIdx.x & 31);
+    int parts = 1;
+    while (nc > 0 && 2 * parts * nc <= warps && buckets / (2 * parts) >= 32) parts *= 2;
+    const int span = buckets / parts;
+    for (int item = wid; item < nc * parts; item += warps) {
+        const int c = item / parts, u0 = (item - c * parts) * span;
+        const uint32_t *row = ent + c * Ls;
+        const int maxv = chan[c].z;
+        uint2 *lrow = lut + (int64_t)c * buckets;
+        int s = lanes_find(row, 0, maxv, (uint32_t)(u0 + ln) << shift), s1 = s;
+        for (int u = u0 + ln; u < u0 + span; u += 32) {
+            const uint32_t first = (uint32_t)u << shift, last = first + (1u << shift) - 1u;
+            while (s < maxv && (row[s] >> 16) < first) ++s;
+            uint32_t hi;
+            if (kPair) {
+                hi = (s < maxv ? row[s + 1] >> 16 : 0xFFFFu) | ((uint32_t)s << 16);
+            } else {
+                s1 = max(s1, s);
+                while (s1 < maxv && (row[s1] >> 16) < last) ++s1;
+                hi = (uint32_t)s | ((uint32_t)s1 << 16);
+            }
+            lrow[u] = make_uint2(row[s], hi);
         }
-        while (s < maxv && (row[s] >> 16) < first) ++s;
-        const int s0 = s;
-        while (s < maxv && (row[s] >> 16) < last) ++s;
-        const uint32_t hi = kPair ? ((s0 < maxv ? row[s0 + 1] >> 16 : 0xFFFFu) | ((uint32_t)s0 << 16))
-                                  : ((uint32_t)s0 | ((uint32_t)s << 16));
-        lut[i] = make_uint2(row[s0], hi);
     }
     __syncthreads();
 }
