@@ -9,8 +9,9 @@ The metric is the reference's: fp32 input-image bytes per second
 (examples/balle_example.py:197-216 of the reference), whole job over all
 GPUs.  The headline times the whole job with consecutive batches overlapped
 (execution_mode="overlap": FastModel.compress_async enqueues the next batch's
-g_a and encode before this batch's decode, so the host's wait for each
-payload size overlaps device work); ``serial`` reports the same steps one
+g_a, and its encode on an encode stream, before this batch's decode, so the
+host's wait for each payload size overlaps device work and the encode runs
+beside the decode); ``serial`` reports the same steps one
 batch at a time, each bracketed by events.  N > 1 GPUs: one process per GPU (torchrun), each with its own 24
 images (weak scaling); the only collective is a final gather of payload
 sizes.
@@ -509,7 +510,8 @@ def run_b200(args):
         # execution_mode="overlap": batch k+1's g_a and encode are enqueued
         # (FastModel.compress_async) before batch k's decode and g_s, so the
         # host's wait for each payload size overlaps device work instead of
-        # leaving the GPU idle.  Every step still compresses and decompresses
+        # leaving the GPU idle, and the encode (on its own stream, after g_a)
+        # runs beside batch k's decode.  Every step still compresses and decompresses
         # a whole batch.  Two resident input batches alternate, and each
         # step's activations (> 600 MB) exceed the 126 MB L2, so no step finds
         # its input there; the L2 is not flushed inside the timed region.
@@ -878,7 +880,8 @@ def run_b200(args):
                 "p_ch": args.p_ch,
                 "transforms": f"{args.transforms} (tcgen05 implicit GEMM)" if args.transforms == "bf16" else "fp32 torch",
                 "execution_mode": "overlap (FastModel.compress_async: batch k+1's g_a and encode enqueued "
-                                  "before batch k's decode and g_s)",
+                                  "before batch k's decode and g_s; the encode on its own stream, beside "
+                                  "batch k's decode)",
                 "l2": "not flushed: two resident input batches alternate and each step's activations "
                       "(> 600 MB) exceed the 126 MB L2; the serial measurement flushes before each step",
                 "parallelism": f"dp{world}",

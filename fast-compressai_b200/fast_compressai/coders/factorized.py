@@ -42,20 +42,30 @@ def _copy_stream(device: torch.device, compute: torch.cuda.Stream, direction: st
 class PendingCompress:
     """A compress whose device work is enqueued (``compress_async``)."""
 
-    __slots__ = ("_codec", "_pending", "_shape", "_result")
+    __slots__ = ("_codec", "_pending", "_shape", "_result", "_compute", "_encode")
 
-    def __init__(self, codec, pending, shape) -> None:
+    def __init__(self, codec, pending, shape, compute: torch.cuda.Stream, encode: torch.cuda.Stream) -> None:
         self._codec = codec
         self._pending = pending
         self._shape = shape
         self._result = None
+        self._compute = compute
+        self._encode = encode
 
     def result(self) -> dict:
         """Wait for the encode, pack the payload and return
         ``{"strings": [payload], "shape": (h, w)}`` (once; later calls
-        return the same dict)."""
+        return the same dict).  The pack runs on the encode stream; the
+        stream that was current at ``compress_async`` then waits for it, so
+        work enqueued there afterwards sees the payload."""
         if self._result is None:
-            payload = self._codec.backend._encode_latent_finish(self._pending)
+            with torch.cuda.stream(self._encode):
+                payload = self._codec.backend._encode_latent_finish(self._pending)
+            packed = torch.cuda.Event()
+            packed.record(self._encode)
+            self._compute.wait_event(packed)
+            payload.packed.record_stream(self._compute)
+            payload.max_rounds.record_stream(self._compute)
             self._result = {"strings": [payload], "shape": self._shape}
             self._pending = None
         return self._result
@@ -146,13 +156,16 @@ class FactorizedWarpDivCodec:
     def compress_async(self, x: torch.Tensor | HostUpload) -> "PendingCompress":
         """``compress`` in two halves, for overlapped batches (the
         reference's ``execution_mode="overlap"``, accepted there but not
-        implemented).  This enqueues g_a and the encode on the current stream
-        and returns at once; ``result()`` waits for the encode alone (not for
-        work enqueued after it), packs the payload and returns what
-        ``compress`` returns.  In between, the caller can enqueue the next
-        batch's or an earlier batch's work, so that the device stays busy
-        while the host learns the payload size.  One pending compress per
-        stream at a time."""
+        implemented).  This enqueues g_a on the current stream and the encode
+        on an encode stream of its own that waits for g_a alone, and returns
+        at once; ``result()`` waits for the encode alone (not for work
+        enqueued after it), packs the payload and returns what ``compress``
+        returns.  In between, the caller can enqueue the next batch's or an
+        earlier batch's work: the device stays busy while the host learns the
+        payload size, and an earlier batch's decode, enqueued on the current
+        stream after this call, runs beside this encode (both are chains of
+        dependent coder steps that leave most of each SM's issue slots
+        free).  One pending compress per stream at a time."""
         if isinstance(x, HostUpload):
             compute = torch.cuda.current_stream(x.tensor.device)
             compute.wait_event(x.ready)
@@ -168,8 +181,15 @@ class FactorizedWarpDivCodec:
             cdfs, lengths, offsets = self._tables(entropy)
             y = y.float().contiguous()
             medians = self._medians(entropy)
-            pending = self.backend._encode_latent_submit(y, medians, cdfs, lengths, offsets, self.p_ch)
-        return PendingCompress(self, pending, tuple(y.shape[-2:]))
+            compute = torch.cuda.current_stream(y.device)
+            encode = _copy_stream(y.device, compute, "encode")
+            latent = torch.cuda.Event()
+            latent.record(compute)
+            with torch.cuda.stream(encode):
+                encode.wait_event(latent)
+                y.record_stream(encode)
+                pending = self.backend._encode_latent_submit(y, medians, cdfs, lengths, offsets, self.p_ch)
+        return PendingCompress(self, pending, tuple(y.shape[-2:]), compute, encode)
 
     def _device(self) -> torch.device:
         return self.model.entropy_bottleneck._quantized_cdf.device

@@ -2,9 +2,11 @@
 batches (the reference's execution_mode="overlap").  The payload equals the
 synchronous compress's byte for byte; an overlapped loop (batch k+1's g_a
 and encode enqueued before batch k's decode and g_s) reconstructs every batch
-as the serial loop does; a second submit on a stream before the finish is
-refused; a staging overflow at the finish falls back to the synchronous
-encode with the workspace it needs."""
+as the serial loop does; the encode runs on an encode stream of the
+compute stream, and work enqueued on the compute stream after result()
+sees the payload however late the pack runs; a second submit on a stream
+before the finish is refused; a staging overflow at the finish falls back to
+the synchronous encode with the workspace it needs."""
 
 from __future__ import annotations
 
@@ -15,6 +17,7 @@ from fast_compressai import accelerate
 from fast_compressai.balle import FactorizedPrior
 from fast_compressai.coders import _warp_div as ext
 from fast_compressai.coders.errors import CoderError
+from fast_compressai.coders.factorized import _copy_stream
 from tests.test_transforms_gpu import _smooth_images
 
 pytestmark = pytest.mark.gpu
@@ -61,16 +64,19 @@ def test_overlapped_loop_matches_serial(fast, cuda_device):
 
 
 def test_one_pending_encode_per_stream(fast, cuda_device):
+    # the pending encode lives on the compute stream's encode stream: a
+    # synchronous compress on the compute stream runs beside it, a second
+    # compress_async waits for the first one's result()
     x = _smooth_images(1, 64, 64, cuda_device, seed=3)
     with torch.inference_mode():
         pending = fast.compress_async(x)
-        with pytest.raises(CoderError, match="awaits fcai_warp_div_encode_finish"):
-            fast.compress(x)
+        sync = fast.compress(x)["strings"][0]
         with pytest.raises(CoderError, match="awaits fcai_warp_div_encode_finish"):
             fast.compress_async(x)
-        pending.result()
-        fast.compress(x)  # the stream is free again
+        got = pending.result()["strings"][0]
+        again = fast.compress_async(x).result()["strings"][0]  # the encode stream is free again
     torch.cuda.synchronize()
+    assert torch.equal(sync.packed, got.packed) and torch.equal(got.packed, again.packed)
 
 
 def test_staging_overflow_falls_back_to_the_synchronous_encode(cuda_device):
@@ -113,3 +119,19 @@ def test_finish_waits_for_the_encode_only(fast, cuda_device):
         assert not torch.cuda.current_stream().query()  # the sleep is still running
     torch.cuda.synchronize()
     assert out["strings"][0].packed.numel() > 0
+
+
+def test_compute_stream_waits_for_a_late_pack(fast, cuda_device):
+    # the pack queued behind a long sleep on the encode stream: a read of the
+    # payload on the compute stream right after result() still sees it whole
+    x = _smooth_images(2, 64, 64, cuda_device, seed=5)
+    with torch.inference_mode():
+        sync = fast.compress(x)["strings"][0]
+        compute = torch.cuda.current_stream()
+        encode = _copy_stream(compute.device, compute, "encode")
+        pending = fast.compress_async(x)
+        with torch.cuda.stream(encode):
+            torch.cuda._sleep(500_000_000)  # enqueued after the encode, before the pack
+        got = pending.result()["strings"][0]
+        same = torch.equal(got.packed, sync.packed) and torch.equal(got.max_rounds, sync.max_rounds)
+    assert same
