@@ -625,19 +625,29 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                         // resident weights: K block ks (the scatter layer has one tap)
                         const uint32_t b0 = Lay::kWRes ? smem_u32(smem + Lay::offWRes) + ks * (kNpad * kBK * 2)
                                                        : a0 + Lay::kA;
+                        if constexpr (Lay::kWRes) {
+                            // the scatter layer's short N = 80 MMAs: the K
+                            // block's four in one issue block (one elect, the
+                            // descriptors advanced inside it), which issues
+                            // them faster than four calls; the dual-tile
+                            // layers ran slower that way and keep the loop
+                            mma_kblock<W, kFp8, false>(d, d, smem_desc(a0, 16, 1024, 2), 0ull,
+                                                       smem_desc(b0, 16, 1024, 2), idesc_main, !fresh);
+                        } else {
 #pragma unroll
-                        // 4 MMAs per 128-byte K block: K = 16 bf16 or 32 e4m3 each
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const uint64_t bd = smem_desc(b0 + kk * 32, 16, 1024, 2);
-                            const uint64_t ad = smem_desc(a0 + kk * 32, 16, 1024, 2);
-                            const uint32_t acc = !(fresh && kk == 0);
-                            if (kFp8) mma_issue_f8<W>(d, ad, bd, idesc_main, acc);
-                            else mma_issue<W>(d, ad, bd, idesc, acc);
-                            // dual tiles: rows 128-255 of A into the second half's columns
-                            if (Lay::kDual) {
-                                const uint64_t ad1 = smem_desc(a0 + kBM * 128 + kk * 32, 16, 1024, 2);
-                                if (kFp8) mma_issue_f8<W>(d + kBM, ad1, bd, idesc_main, acc);
-                                else mma_issue<W>(d + kBM, ad1, bd, idesc, acc);
+                            // 4 MMAs per 128-byte K block: K = 16 bf16 or 32 e4m3 each
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint64_t bd = smem_desc(b0 + kk * 32, 16, 1024, 2);
+                                const uint64_t ad = smem_desc(a0 + kk * 32, 16, 1024, 2);
+                                const uint32_t acc = !(fresh && kk == 0);
+                                if (kFp8) mma_issue_f8<W>(d, ad, bd, idesc_main, acc);
+                                else mma_issue<W>(d, ad, bd, idesc, acc);
+                                // dual tiles: rows 128-255 of A into the second half's columns
+                                if (Lay::kDual) {
+                                    const uint64_t ad1 = smem_desc(a0 + kBM * 128 + kk * 32, 16, 1024, 2);
+                                    if (kFp8) mma_issue_f8<W>(d + kBM, ad1, bd, idesc_main, acc);
+                                    else mma_issue<W>(d + kBM, ad1, bd, idesc, acc);
+                                }
                             }
                         }
                     }
