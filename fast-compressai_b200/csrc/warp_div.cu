@@ -706,6 +706,7 @@ struct DecParams {
     Control *ctrl;
     const unsigned long long *offsets;
     int32_t *__restrict__ out;
+    int group_warps;  // lanes decode: warps that decode (one image each); the CTA's others only stage
 };
 
 // The lane's words in decode order, read four at a time: r0..r3 hold words
@@ -1648,7 +1649,10 @@ __global__ void __launch_bounds__(kThreads) decode_lanes_kernel(DecParams p) {
     if (threadIdx.x == 0) s_skip = decode_skip(p) ? 1 : 0;
     __syncthreads();
     const bool skip = s_skip != 0;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    // W warps decode a group's W images; a CTA of fewer images than kWarps
+    // launches kWarps warps anyway, and the rest help stage the group's rows
+    // and bucket tables
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = p.group_warps;
     const int P = p.chunk_len / p.HW;
     const int nbb = (p.B + W - 1) / W;
     const int64_t groups = (int64_t)p.K * nbb;
@@ -1665,7 +1669,7 @@ __global__ void __launch_bounds__(kThreads) decode_lanes_kernel(DecParams p) {
         // error is reported)
         if (__syncthreads_or((int)(flags & kFlagTable))) continue;
         const int b = bb * W + warp;
-        if (b < p.B)
+        if (warp < W && b < p.B)
             decode_lanes<kMode, kPair>(p, ent, chan, lut, ls.lut_shift, c0, nc, p.t.L - 1, (int64_t)b * p.K + k,
                                        lane, flags);
     }
@@ -1988,12 +1992,14 @@ static int launch_encode_lanes(const EncParams &p, int64_t smem, cudaStream_t st
 }
 
 template <int kMode, bool kPair>
-static int launch_decode_lanes(const DecParams &p, int64_t smem, cudaStream_t stream) {
+static int launch_decode_lanes(DecParams p, int64_t smem, cudaStream_t stream) {
     int grid = 1, rc;
     const int warps = group_warps(p.B, p.K);
+    p.group_warps = warps;
     const int64_t groups = (int64_t)p.K * ((p.B + warps - 1) / warps);
-    if ((rc = grid_for(decode_lanes_kernel<kMode, kPair>, smem, groups * warps, warps, grid))) return rc;
-    decode_lanes_kernel<kMode, kPair><<<grid, warps * kLanes, smem, stream>>>(p);
+    // grid sized as for one warp per image; every CTA has kWarps warps
+    if ((rc = grid_for(decode_lanes_kernel<kMode, kPair>, smem, groups * kWarps, kWarps, grid))) return rc;
+    decode_lanes_kernel<kMode, kPair><<<grid, kThreads, smem, stream>>>(p);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
