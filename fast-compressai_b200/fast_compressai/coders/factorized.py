@@ -23,10 +23,10 @@ import torch
 from .errors import CoderInputError
 from .warp_div import WarpDivBackend, WarpDivPayload
 
-# Copy streams of the host-batch entry points, one per (compute stream,
-# direction): uploads and downloads never queue behind each other (PCIe is
-# full duplex), and callers on different compute streams do not serialise
-# their copies on one queue.
+# Side streams, one per (device, compute stream, role): "up" and "down" for
+# the host-batch entry points' copies, which never queue behind each other
+# (PCIe is full duplex), and "encode" for compress_async's encode and pack.
+# Callers on different compute streams never share one.
 _COPY_STREAMS: dict[tuple[int, int, str], torch.cuda.Stream] = {}
 
 
