@@ -942,7 +942,7 @@ def run_b200(args):
                     "decode_gbs": ans_bytes / (dec_kernel_ms / 1e3) / 1e9,
                     "encode_frac": ans_bytes / ((enc_kernel_ms + pack_kernel_ms) / 1e3) / 1e9 / hbm,
                     "decode_frac": ans_bytes / (dec_kernel_ms / 1e3) / 1e9 / hbm,
-                    "note": "CUDA events around the kernels alone: encode (+ its status-word copy) and pack "
+                    "note": "CUDA events around the kernels alone: encode (its last CTA writes the status words to the host) and pack "
                             "count together for encode; L2 flushed before each",
                 },
                 "host_call": {
