@@ -631,8 +631,8 @@ __global__ void __launch_bounds__(Layout<kNpad, kEpi, kGather, kPair, kFp8>::kTh
                             // descriptors advanced inside it), which issues
                             // them faster than four calls; the dual-tile
                             // layers ran slower that way and keep the loop
-                            mma_kblock<W, kFp8, false>(d, d, smem_desc(a0, 16, 1024, 2), 0ull,
-                                                       smem_desc(b0, 16, 1024, 2), idesc_main, !fresh);
+                            mma_kblock<W, kFp8>(d, smem_desc(a0, 16, 1024, 2), smem_desc(b0, 16, 1024, 2), idesc_main,
+                                                !fresh);
                         } else {
 #pragma unroll
                             // 4 MMAs per 128-byte K block: K = 16 bf16 or 32 e4m3 each

@@ -315,56 +315,42 @@ __device__ __forceinline__ void mma_bf16_w(uint32_t d_tmem, uint64_t adesc, uint
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-// The four MMAs of one 128-byte K block (K = 16 bf16 or 32 e4m3 each), and
-// with kDual the same four into a second accumulator d1 from a second A
-// tile a1 sharing B: one elect.sync (kElect; otherwise the calling lane
-// issues), the descriptors advanced by 32 bytes (2 in their 16-byte address
-// field) from one MMA to the next.  The address field holds at most
-// 228 KB / 16 < 2^14 - 6, so the additions never carry out of it, and the
-// descriptors equal smem_desc(base + 32 k, ...).  The first MMA (pair)
-// accumulates when `accumulate` is non-zero, the others always.
-#define FCAI_MMA_KBLOCK_ONE(kind, D, A, B) "@e tcgen05.mma.cta_group::1.kind::" kind " [" D "], " A ", " B ", %5, "
-#define FCAI_MMA_KBLOCK(kind)                                                                           \
-    "{\n\t.reg .pred p, t, e;\n\t.reg .b64 a, c, b;\n\t"                                                \
-    FCAI_ELECT                                                                                          \
-    "setp.ne.b32 p, %6, 0;\n\tsetp.eq.b32 t, %6, %6;\n\t"                                              \
-    FCAI_MMA_KBLOCK_ONE(kind, "%0", "%2", "%4") "p;\n\t"                                               \
-    FCAI_DUAL(FCAI_MMA_KBLOCK_ONE(kind, "%1", "%3", "%4") "p;\n\t")                                    \
-    "add.s64 a, %2, 2;\n\tadd.s64 b, %4, 2;\n\t" FCAI_DUAL("add.s64 c, %3, 2;\n\t")                    \
-    FCAI_MMA_KBLOCK_ONE(kind, "%0", "a", "b") "t;\n\t" FCAI_DUAL(FCAI_MMA_KBLOCK_ONE(kind, "%1", "c", "b") "t;\n\t") \
-    "add.s64 a, a, 2;\n\tadd.s64 b, b, 2;\n\t" FCAI_DUAL("add.s64 c, c, 2;\n\t")                        \
-    FCAI_MMA_KBLOCK_ONE(kind, "%0", "a", "b") "t;\n\t" FCAI_DUAL(FCAI_MMA_KBLOCK_ONE(kind, "%1", "c", "b") "t;\n\t") \
-    "add.s64 a, a, 2;\n\tadd.s64 b, b, 2;\n\t" FCAI_DUAL("add.s64 c, c, 2;\n\t")                        \
-    FCAI_MMA_KBLOCK_ONE(kind, "%0", "a", "b") "t;\n\t" FCAI_DUAL(FCAI_MMA_KBLOCK_ONE(kind, "%1", "c", "b") "t;\n\t") \
-    "}"
-#define FCAI_MMA_KBLOCK_ARGS                                                                            \
-    ::"r"(d0), "r"(d1), "l"(a0), "l"(a1), "l"(b), "r"(idesc), "r"(accumulate)
-
-template <bool kElect, bool kF8, bool kDual>
-__device__ __forceinline__ void mma_kblock(uint32_t d0, uint32_t d1, uint64_t a0, uint64_t a1, uint64_t b,
-                                           uint32_t idesc, uint32_t accumulate) {
-#define FCAI_DUAL(x) x
-#define FCAI_ELECT "elect.sync _|e, 0xffffffff;\n\t"
-    if constexpr (kElect && kDual && !kF8) asm volatile(FCAI_MMA_KBLOCK("f16") FCAI_MMA_KBLOCK_ARGS);
-    if constexpr (kElect && kDual && kF8) asm volatile(FCAI_MMA_KBLOCK("f8f6f4") FCAI_MMA_KBLOCK_ARGS);
-#undef FCAI_ELECT
-#define FCAI_ELECT "setp.eq.b32 e, %6, %6;\n\t"
-    if constexpr (!kElect && kDual && !kF8) asm volatile(FCAI_MMA_KBLOCK("f16") FCAI_MMA_KBLOCK_ARGS);
-    if constexpr (!kElect && kDual && kF8) asm volatile(FCAI_MMA_KBLOCK("f8f6f4") FCAI_MMA_KBLOCK_ARGS);
-#undef FCAI_DUAL
-#define FCAI_DUAL(x)
-    if constexpr (!kElect && !kDual && !kF8) asm volatile(FCAI_MMA_KBLOCK("f16") FCAI_MMA_KBLOCK_ARGS);
-    if constexpr (!kElect && !kDual && kF8) asm volatile(FCAI_MMA_KBLOCK("f8f6f4") FCAI_MMA_KBLOCK_ARGS);
-#undef FCAI_ELECT
-#define FCAI_ELECT "elect.sync _|e, 0xffffffff;\n\t"
-    if constexpr (kElect && !kDual && !kF8) asm volatile(FCAI_MMA_KBLOCK("f16") FCAI_MMA_KBLOCK_ARGS);
-    if constexpr (kElect && !kDual && kF8) asm volatile(FCAI_MMA_KBLOCK("f8f6f4") FCAI_MMA_KBLOCK_ARGS);
-#undef FCAI_ELECT
-#undef FCAI_DUAL
+// The four MMAs of one 128-byte K block (K = 16 bf16 or 32 e4m3 each) into
+// d: one elect.sync (kElect; otherwise the calling lane issues), the
+// descriptors advanced by 32 bytes (2 in their 16-byte address field) from
+// one MMA to the next.  The address field holds at most 228 KB / 16 < 2^14 - 6,
+// so the additions never carry out of it, and the descriptors equal
+// smem_desc(base + 32 k, ...).  The first MMA accumulates when `accumulate`
+// is non-zero, the other three always.
+#define FCAI_MMA_KBLOCK(kind, pick)                                                                  \
+    "{\n\t.reg .pred p, t, e;\n\t.reg .b64 a, b;\n\t" pick                                            \
+    "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"                                            \
+    "@e tcgen05.mma.cta_group::1.kind::" kind " [%0], %1, %2, %3, p;\n\t"                             \
+    "add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\t"                                                     \
+    "@e tcgen05.mma.cta_group::1.kind::" kind " [%0], a, b, %3, t;\n\t"                               \
+    "add.s64 a, a, 2;\n\tadd.s64 b, b, 2;\n\t"                                                       \
+    "@e tcgen05.mma.cta_group::1.kind::" kind " [%0], a, b, %3, t;\n\t"                               \
+    "add.s64 a, a, 2;\n\tadd.s64 b, b, 2;\n\t"                                                       \
+    "@e tcgen05.mma.cta_group::1.kind::" kind " [%0], a, b, %3, t;\n\t}"
+#define FCAI_ELECTED "elect.sync _|e, 0xffffffff;\n\t"
+#define FCAI_CALLER "setp.eq.b32 e, %4, %4;\n\t"
+template <bool kElect, bool kF8>
+__device__ __forceinline__ void mma_kblock(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    if constexpr (kElect && !kF8)
+        asm volatile(FCAI_MMA_KBLOCK("f16", FCAI_ELECTED) ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    if constexpr (kElect && kF8)
+        asm volatile(FCAI_MMA_KBLOCK("f8f6f4", FCAI_ELECTED) ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc),
+                     "r"(accumulate));
+    if constexpr (!kElect && !kF8)
+        asm volatile(FCAI_MMA_KBLOCK("f16", FCAI_CALLER) ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    if constexpr (!kElect && kF8)
+        asm volatile(FCAI_MMA_KBLOCK("f8f6f4", FCAI_CALLER) ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc),
+                     "r"(accumulate));
 }
-#undef FCAI_MMA_KBLOCK_ARGS
+#undef FCAI_CALLER
+#undef FCAI_ELECTED
 #undef FCAI_MMA_KBLOCK
-#undef FCAI_MMA_KBLOCK_ONE
 
 __device__ __forceinline__ void mma_bf16_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                 uint32_t accumulate) {
