@@ -55,7 +55,9 @@ def test_reference_known_answer_cases(cuda_device, P):
     "B,C,HW,P,esc",
     [(1, 12, 16, 4, 0.0), (2, 12, 16, 5, 0.02), (2, 12, 16, 12, 0.0), (3, 7, 33, 3, 0.05), (1, 4, 1, 1, 0.3),
      (4, 16, 100, 16, 0.0), (2, 192, 48, 4, 0.001), (2, 192, 48, 192, 0.0), (1, 5, 7, 2, 0.5),
-     (2, 320, 64, 8, 0.0), (1, 3, 1000, 1, 0.01)],
+     (2, 320, 64, 8, 0.0), (1, 3, 1000, 1, 0.01),
+     # >= 148 chunk groups: decode CTAs of 5 and 7 decoding warps plus staging-only warps
+     (5, 192, 32, 1, 0.01), (7, 160, 16, 1, 0.0)],
 )
 def test_payload_bit_exact_vs_oracle(cuda_device, B, C, HW, P, esc):
     cdfs, sizes, offs, scales = laplacian_tables(C, seed=C + P)
