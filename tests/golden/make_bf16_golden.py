@@ -11,7 +11,7 @@ fixture pins the tcgen05 layers to the reference's definition of its BF16
 path (tests/test_bf16_golden_gpu.py).  The checkout is ``$FCAI_REFERENCE``,
 else the ``reference_path`` that BASELINE.json records.
 
-    python tests/golden/make_bf16_golden.py --out tests/golden/bf16_layers.npz
+    python tests/golden/make_bf16_golden.py --out tests/golden/transforms/bf16_layers.npz
 """
 
 from __future__ import annotations
@@ -62,7 +62,7 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default=str(ROOT / "tests" / "golden" / "bf16_layers.npz"))
+    ap.add_argument("--out", default=str(ROOT / "tests" / "golden" / "transforms" / "bf16_layers.npz"))
     args = ap.parse_args()
     ops = _load_reference_operators()
     model = golden_model()

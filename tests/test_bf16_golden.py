@@ -1,4 +1,4 @@
-"""CPU checks of the BF16 per-layer golden fixture (tests/golden/bf16_layers.npz,
+"""CPU checks of the BF16 per-layer golden fixture (tests/golden/transforms/bf16_layers.npz,
 made by tests/golden/make_bf16_golden.py from the reference's BF16 operators):
 the seeded model still has the weights the fixture was made with, and every
 stored layer output has the shape the layer produces."""
@@ -12,7 +12,7 @@ import torch
 
 from tests.bf16_golden_model import IMAGE_SHAPE, LATENT_SHAPE, golden_model, layers, weight_checksum
 
-FIXTURE = Path(__file__).resolve().parent / "golden" / "bf16_layers.npz"
+FIXTURE = Path(__file__).resolve().parent / "golden" / "transforms" / "bf16_layers.npz"
 
 
 def test_fixture_matches_the_seeded_model():

@@ -1,6 +1,6 @@
 """The tcgen05 transform layers against the reference's own BF16 operators.
 
-tests/golden/bf16_layers.npz holds, per layer of a seeded FactorizedPrior(128,
+tests/golden/transforms/bf16_layers.npz holds, per layer of a seeded FactorizedPrior(128,
 192), the output of the reference's ``BF16Conv2d`` / ``BF16ConvTranspose2d`` /
 ``BF16GDN`` (backends/pytorch/bf16_operators.py:13-60 of the reference) for the
 previous reference layer's output as input.  Each kernel here takes that same
@@ -26,7 +26,7 @@ from tests.bf16_golden_model import golden_model, layers
 
 pytestmark = pytest.mark.gpu
 
-FIXTURE = Path(__file__).resolve().parent / "golden" / "bf16_layers.npz"
+FIXTURE = Path(__file__).resolve().parent / "golden" / "transforms" / "bf16_layers.npz"
 
 
 def _bf16(bits: np.ndarray) -> torch.Tensor:
