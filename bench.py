@@ -63,9 +63,10 @@ def parse_args(argv=None):
                     help="skip the extra measurement with the reference's example precision map (FP8 layers)")
     ap.add_argument("--chunk-images", type=int, default=4,
                     help="images per upload / download chunk of the one-batch-at-a-time end-to-end measurement")
-    ap.add_argument("--stream-chunk-images", type=int, default=0,
-                    help="images per upload / download chunk of the streamed end-to-end measurement "
-                         "(0: the whole batch; its copies overlap the neighbouring batches anyway)")
+    ap.add_argument("--stream-chunk-images", type=int, default=8,
+                    help="images per upload / download chunk of the streamed end-to-end measurement (0: the "
+                         "whole batch); g_s runs per chunk, so the last batch's download starts after its "
+                         "first chunk rather than its whole synthesis")
     ap.add_argument("--ans-sweep", action="store_true",
                     help="BASELINE config 3 instead: the coder alone on 64 x 192 x 32 x 48 Laplacian symbols, "
                          "P in {1, 2, 4, 8, 16, 48, 192}")
