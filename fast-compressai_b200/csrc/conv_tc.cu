@@ -1750,6 +1750,27 @@ __global__ void nchw_to_nhwc_kernel(const float *__restrict__ in, __nv_bfloat16 
     *reinterpret_cast<uint4 *>(out + pix * C + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// The same with 16 channels a thread where the channel count allows: the
+// thread's two 16-byte stores fill one 32-byte sector of the pixel's NHWC
+// row (rows of 16 k channels are 32-byte multiples), so no sector is written
+// in halves by two threads far apart in time.
+__global__ void nchw_to_nhwc16_kernel(const float *__restrict__ in, __nv_bfloat16 *__restrict__ out, int C, int HW,
+                                      int64_t total_pix) {
+    const int groups = C / 16;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= total_pix * groups) return;
+    const int g = (int)(idx / total_pix);
+    const int64_t pix = idx - (int64_t)g * total_pix;
+    const int64_t b = pix / HW, hw = pix - b * HW;
+    const float *src = in + (b * C + g * 16) * HW + hw;
+    uint32_t w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w[e] = pack_bf16x2(__ldg(src + (2 * e) * (int64_t)HW), __ldg(src + (2 * e + 1) * (int64_t)HW));
+    uint4 *dst = reinterpret_cast<uint4 *>(out + pix * C + g * 16);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 }  // namespace ct
 
 using namespace ct;
@@ -2040,11 +2061,16 @@ int fcai_nchw_f32_to_nhwc_bf16(const float *input, void *output, int32_t batch, 
     if (!input || !output || batch <= 0 || channels <= 0 || channels % 8 || h <= 0 || w <= 0)
         return fcai::fail(FCAI_ERR_INVALID, "invalid layout conversion arguments");
     const int64_t pix = (int64_t)batch * h * w;
-    const int64_t total = pix * (channels / 8);
+    const bool wide = channels % 16 == 0;
+    const int64_t total = pix * (channels / (wide ? 16 : 8));
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;
-    nchw_to_nhwc_kernel<<<(unsigned)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
-        input, static_cast<__nv_bfloat16 *>(output), channels, h * w, pix);
+    if (wide)
+        nchw_to_nhwc16_kernel<<<(unsigned)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+            input, static_cast<__nv_bfloat16 *>(output), channels, h * w, pix);
+    else
+        nchw_to_nhwc_kernel<<<(unsigned)blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream_)>>>(
+            input, static_cast<__nv_bfloat16 *>(output), channels, h * w, pix);
     FCAI_CUDA_TRY(cudaGetLastError());
     return FCAI_OK;
 }
