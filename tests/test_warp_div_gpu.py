@@ -81,6 +81,17 @@ def test_arbitrary_indexes_and_short_rows(cuda_device):
     assert not r.index_layout_is_channel
 
 
+@pytest.mark.parametrize("B,C,HW,P", [(32767, 4, 1, 4), (1, 46340, 1, 1)])
+def test_largest_batch_and_channel_counts(cuda_device, B, C, HW, P):
+    # the largest batch the reference's decode accepts (its header compares
+    # batch << 16 as int32) and a channel count at the N * C < 2^31 limit:
+    # tens of thousands of one-chunk groups through the persistent grids
+    cdfs, sizes, offs, scales = laplacian_tables(C, seed=3)
+    sym = laplacian_symbols(B, C, HW, scales, seed=4, escape_rate=0.01)
+    r = _compare(sym, channel_indexes(B, C, HW), cdfs, sizes, offs, P, cuda_device, explicit=False)
+    assert r.max_rounds.shape == (B, (C + P - 1) // P)
+
+
 @pytest.mark.parametrize("B,C,HW,P,esc", [(3, 40, 97, 8, 0.02), (2, 24, 256, 3, 0.0), (2, 96, 64, 48, 0.01),
                                           (4, 10, 33, 1, 0.05)])
 def test_mixed_indexes_fast_and_checked_paths(cuda_device, B, C, HW, P, esc):
