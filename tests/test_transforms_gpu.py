@@ -194,6 +194,34 @@ def test_accelerate_bf16_end_to_end(cuda_device):
     assert abs(out["strings"][0].packed.numel() / ref_bytes - 1.0) <= 0.01
 
 
+@pytest.mark.parametrize("B,H,W", [(1, 16, 16), (2, 40, 56), (1, 17, 33)])
+def test_bf16_codec_at_tiny_and_ragged_sizes(cuda_device, B, H, W):
+    # a 1 x 1 latent, and sizes that are not multiples of 16 (the latent is
+    # ceil-halved four times; the reconstruction is 16 x the latent): the
+    # decoded symbols are the quantised B200 latent bit for bit, and
+    # decompress is the B200 synthesis of exactly them
+    torch.manual_seed(0)
+    model = FactorizedPrior(128, 192).to(cuda_device).eval()
+    model.update(force=True)
+    fast = accelerate(model, P=4, device="cuda:0", transforms="bf16")
+    x = _smooth_images(B, H, W, cuda_device, seed=H + W)
+    with torch.inference_mode():
+        out = fast.compress(x)
+        x_hat = fast.decompress(out["strings"], out["shape"])["x_hat"]
+        fe = fast.model.entropy_bottleneck
+        med = fe._get_medians().detach().reshape(1, -1, 1, 1)
+        y = fast.model.g_a(x)
+        sym = torch.round(y - med).int()
+        assert out["shape"] == tuple(y.shape[-2:])
+        idx = fe._build_indexes(sym.shape, device="cuda:0").reshape(B, -1).contiguous()
+        dec = fast._coder.backend.decode(out["strings"][0], idx, fe._quantized_cdf.contiguous(),
+                                         fe._cdf_length.contiguous(), fe._offset.contiguous())
+        expect = fast.model.g_s(sym.float() + med, clamp=True)
+    assert torch.equal(dec.reshape_as(sym), sym)
+    assert x_hat.shape == (B, 3, 16 * y.shape[-2], 16 * y.shape[-1])
+    assert torch.equal(x_hat, expect)
+
+
 @pytest.mark.parametrize("transforms", ["bf16", "fp32"])
 def test_host_batch_entry_points_match_device_ones(cuda_device, transforms):
     # compress_host / decompress_host overlap the PCIe copies with the
