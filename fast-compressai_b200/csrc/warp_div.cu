@@ -1476,9 +1476,11 @@ __device__ __forceinline__ bool dec_escape(DecLane &d, const uint32_t *__restric
 }
 
 // Decodes one chunk: each lane reads its state, then its symbols first to
-// last, four at a time.  A group of four symbols in one channel (every
-// group when HW is a multiple of 128) has no channel bookkeeping; the ragged
-// end and groups that cross a channel step per symbol.  A lane that
+// last, eight at a time (one vote and one bookkeeping step per eight
+// symbols: about 2% faster than four).  A group of eight symbols in one
+// channel (every group when HW is a multiple of 256) has no channel
+// bookkeeping; the ragged end and groups that cross a channel step per
+// symbol.  A lane that
 // consumes more words than its chunk holds marks the payload corrupt.
 //
 // With explicit indexes (kModeIdx) a group also needs its indexes to be the
@@ -1489,7 +1491,7 @@ template <int kMode, bool kPair>
 __device__ __forceinline__ void decode_lanes(const DecParams &p, const uint32_t *__restrict__ ent,
                                              const int4 *__restrict__ chan, const uint2 *__restrict__ lut, int shift,
                                              int c0, int nc, int Ls, int64_t chunk, int lane, uint32_t &flags) {
-    constexpr int kG = 4;
+    constexpr int kG = 8;
     constexpr bool kIdx = kMode == kModeIdx;
     const uint32_t *body = reinterpret_cast<const uint32_t *>(p.packed + p.header_bytes);
     const int b = (int)(chunk / p.K);
